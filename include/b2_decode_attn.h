@@ -1,0 +1,160 @@
+/*
+ * b2_decode_attn.h - C ABI of the B200 LFM2.5 decode-attention library
+ * (libb2attn.so).
+ *
+ * The library implements one hot path of the LFM2.5-230M decoder: for each
+ * sequence of a batch and one attention layer,
+ *   1. per-head RMSNorm of the raw q/k projections, rotate-half RoPE, and the
+ *      append of the new (k, v) into a paged BF16 KV cache      (b2_append_rope)
+ *   2. grouped-query attention of the one new query over every cached token,
+ *      split along the token axis into partial softmax states (b2_decode_attn)
+ *   3. the log-sum-exp merge of those partial states              (b2_combine)
+ *
+ * Shapes are fixed by the model: 16 query heads, 8 KV heads, head_dim 64,
+ * query head h reads KV head h / 2, KV blocks of 64 tokens.
+ *
+ * Memory layout (all buffers are owned by the caller; nothing is allocated here):
+ *   qkv          bf16 [batch][row_stride]; a row starts with
+ *                q[16][64] | k[8][64] | v[8][64]  (the reference's qkv vector,
+ *                experiments/kernels/lfm25_attention_append_cache.cc:20-21)
+ *   k_pool/v_pool bf16 [num_blocks][8 kv heads][64 tokens][64 dims]: one
+ *                (block, head) tile is 8 KiB contiguous
+ *   block_tables int32 [batch][max_blocks_per_seq]: logical block -> pool block
+ *   past_lens    int32 [batch]: tokens cached before this step (the slot the
+ *                new token is written to, and its RoPE position)
+ *   seq_lens     int32 [batch]: tokens attended (cached + the new one)
+ *   part_ml      fp32 [batch][num_splits][16][2]: partial (max, sum) per head,
+ *                max in log2 units (scores are pre-multiplied by scale*log2 e)
+ *   part_o       fp32 [batch][num_splits][16][64]: unnormalised partial output
+ *
+ * bf16 values are passed as their raw 16-bit patterns (uint16_t).  `stream`
+ * is a cudaStream_t.  Every call is stream-ordered and asynchronous.  Return
+ * value: B2_OK, or a negative B2_ERR_* code; b2_last_error() gives the
+ * message (thread-local).  Faults the host cannot see (a block id outside the
+ * pool, a length beyond the block table, a bounded wait that ran out) are
+ * OR-ed into the caller's device word `dev_err` as B2_DEV_* bits; the kernel
+ * skips the bad access instead of performing it.
+ */
+#ifndef B2_DECODE_ATTN_H
+#define B2_DECODE_ATTN_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  B2_OK = 0,
+  B2_ERR_ARG = -1,    /* bad pointer, shape, alignment or mode */
+  B2_ERR_CUDA = -2,   /* the CUDA runtime refused a launch */
+  B2_ERR_NOSYM = -3   /* the driver lacks cuTensorMapEncodeTiled */
+};
+
+enum {
+  B2_DEV_BAD_BLOCK = 1,     /* block table entry outside [0, num_blocks) */
+  B2_DEV_BAD_LENGTH = 2,    /* length/position outside the block table */
+  B2_DEV_BAD_POSITION = 4,  /* RoPE position outside the cos/sin table */
+  B2_DEV_TIMEOUT = 8        /* an mbarrier wait gave up (no hang) */
+};
+
+/* b2_append_rope mode bits */
+enum {
+  B2_NORM_QK = 1,   /* per-head RMSNorm of q and k, times gamma */
+  B2_ROPE_QK = 2,   /* rotate-half RoPE of q and k at position past_lens[b] */
+  B2_STORE_KV = 4   /* write k and v into slot past_lens[b] of the pool */
+};
+
+/* Library ABI version (major * 100 + minor). */
+int b2_version(void);
+
+/* Copy the calling thread's last error message into buf (NUL-terminated,
+ * truncated to len).  Returns the message length. */
+int b2_last_error(char *buf, int len);
+
+/*
+ * Fused q/k RMSNorm + RoPE + KV append for one decode token per sequence.
+ *
+ * Replaces, for the whole batch in one launch:
+ *   append_attention_cache(qkv, prior_cache, next_cache)
+ *     experiments/lfm25_attention_append_cache_kernel.py:20-73 with its core
+ *     kernel lfm25_attention_append_cache{,_dynamic}
+ *     (experiments/kernels/lfm25_attention_append_cache.cc:5-39), and
+ *   lfm25_attention_norm_rope(qkv, aux)
+ *     (experiments/kernels/lfm25_attention_norm_rope.cc:17-54; the x8
+ *     engine's norm_rope, experiments/kernels/x8/x8_math.h:150-177).
+ * Unlike the reference, the old cache is not copied: only the new token's
+ * 128-byte k and v rows are written, in place, into the paged pool.
+ *
+ * qkv          bf16 rows of row_stride elements (row_stride >= 2048, multiple
+ *              of 8), 16-byte aligned.
+ * gamma_q/k    bf16 [64] RMSNorm weights (required when B2_NORM_QK).
+ * eps          RMSNorm epsilon (LFM2: 1e-5).
+ * rope_cos/sin bf16 [rope_rows][64] tables (required when B2_ROPE_QK).
+ * q_out        bf16 [batch][16][64] normalised + rotated query, or NULL.
+ * k/v_pool     required when B2_STORE_KV.
+ */
+int b2_append_rope(const uint16_t *qkv, int64_t row_stride,
+                   const uint16_t *gamma_q, const uint16_t *gamma_k, float eps,
+                   const uint16_t *rope_cos, const uint16_t *rope_sin,
+                   int32_t rope_rows,
+                   const int32_t *past_lens,
+                   const int32_t *block_tables, int32_t max_blocks_per_seq,
+                   uint16_t *k_pool, uint16_t *v_pool, int32_t num_blocks,
+                   uint16_t *q_out, int32_t batch, int32_t mode,
+                   int32_t *dev_err, void *stream);
+
+/*
+ * Split-KV flash-decode over the paged pool: one CTA per
+ * (split, kv head, sequence); split s covers logical blocks
+ * [s * blocks_per_split, (s + 1) * blocks_per_split) of its sequence.  K/V
+ * tiles stream HBM -> shared memory through TMA (128-byte swizzle) in a
+ * 4-stage mbarrier pipeline; both query heads of the GQA pair share each tile.
+ *
+ * Replaces the context computation of
+ *   attention_context(qkv, past_cache, context)
+ *     experiments/lfm25_attention_context_kernel.py:20-72,
+ *     experiments/kernels/lfm25_attention_context_head.cc:19-82
+ *   attention_context_cache / _fixed64 / _chunked
+ *     experiments/lfm25_attention_context_cache_kernel.py:16-106,
+ *     experiments/lfm25_attention_fixed64_cache_kernel.py:30-136,
+ *     experiments/lfm25_attention_chunked_cache_kernel.py:21-89 and the
+ *     online softmax of experiments/kernels/lfm25_attention_chunked_head.cc:49-88
+ *   the x8 engine's attn_prep/attn_block/attn_final + attn_positions
+ *     experiments/kernels/x8/x8_core.cc:89-121, x8/x8_math.h:185-254
+ *
+ * q            bf16 [batch][16][64] (output of b2_append_rope).
+ * num_splits   >= ceil(max_blocks_per_seq / blocks_per_split).
+ * scale        softmax scale (head_dim^-0.5 = 0.125).
+ * Pool pointers must be 16-byte aligned; num_blocks * 512 < 2^31.
+ */
+int b2_decode_attn(const uint16_t *q,
+                   const uint16_t *k_pool, const uint16_t *v_pool,
+                   int32_t num_blocks,
+                   const int32_t *block_tables, int32_t max_blocks_per_seq,
+                   const int32_t *seq_lens, int32_t batch,
+                   int32_t blocks_per_split, int32_t num_splits, float scale,
+                   float *part_ml, float *part_o,
+                   int32_t *dev_err, void *stream);
+
+/*
+ * Log-sum-exp merge of partial states [batch][num_parts][16] into either the
+ * bf16 context out[batch][16][64] (head-major, the reference's context layout,
+ * experiments/kernels/lfm25_attention_context_head.cc:75) and/or one merged
+ * fp32 state (state_ml [batch][16][2], state_o [batch][16][64]) for a further
+ * merge across GPUs.  With seq_lens != NULL only the parts that cover tokens
+ * of each sequence are read (ceil(ceil(len/64)/blocks_per_split)); with NULL
+ * all num_parts are read.  Replaces the final acc/l step of
+ * experiments/kernels/lfm25_attention_chunked_head.cc:84-88 and attn_final
+ * (experiments/kernels/x8/x8_core.cc:113-121).
+ */
+int b2_combine(const float *part_ml, const float *part_o, int32_t num_parts,
+               const int32_t *seq_lens, int32_t blocks_per_split,
+               int32_t batch, uint16_t *out, float *state_ml, float *state_o,
+               void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B2_DECODE_ATTN_H */

@@ -1,0 +1,111 @@
+"""ctypes binding of libb2attn.so (the C ABI in include/b2_decode_attn.h).
+
+This module loads the in-tree shared library and nothing else: there is no
+fallback.  If the library is missing or fails to load, every entry point
+raises, so a GPU run can never silently take another path.
+"""
+from __future__ import annotations
+
+import ctypes
+import pathlib
+
+LIB_PATH = pathlib.Path(__file__).resolve().parent / "libb2attn.so"
+
+B2_OK = 0
+B2_ERR_ARG = -1
+B2_ERR_CUDA = -2
+B2_ERR_NOSYM = -3
+
+B2_DEV_BAD_BLOCK = 1
+B2_DEV_BAD_LENGTH = 2
+B2_DEV_BAD_POSITION = 4
+B2_DEV_TIMEOUT = 8
+
+B2_NORM_QK = 1
+B2_ROPE_QK = 2
+B2_STORE_KV = 4
+
+DEV_ERR_NAMES = {
+    B2_DEV_BAD_BLOCK: "block table entry outside the pool",
+    B2_DEV_BAD_LENGTH: "length or position outside the block table",
+    B2_DEV_BAD_POSITION: "RoPE position outside the cos/sin table",
+    B2_DEV_TIMEOUT: "a bounded device wait ran out",
+}
+
+_p = ctypes.c_void_p
+_i32 = ctypes.c_int32
+_i64 = ctypes.c_int64
+_f32 = ctypes.c_float
+
+# name -> (restype, argtypes); the order mirrors the header.
+SIGNATURES = {
+    "b2_version": (ctypes.c_int, []),
+    "b2_last_error": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_int]),
+    "b2_append_rope": (ctypes.c_int, [
+        _p, _i64,            # qkv, row_stride
+        _p, _p, _f32,        # gamma_q, gamma_k, eps
+        _p, _p, _i32,        # rope_cos, rope_sin, rope_rows
+        _p,                  # past_lens
+        _p, _i32,            # block_tables, max_blocks_per_seq
+        _p, _p, _i32,        # k_pool, v_pool, num_blocks
+        _p, _i32, _i32,      # q_out, batch, mode
+        _p, _p,              # dev_err, stream
+    ]),
+    "b2_decode_attn": (ctypes.c_int, [
+        _p, _p, _p, _i32,    # q, k_pool, v_pool, num_blocks
+        _p, _i32,            # block_tables, max_blocks_per_seq
+        _p, _i32,            # seq_lens, batch
+        _i32, _i32, _f32,    # blocks_per_split, num_splits, scale
+        _p, _p,              # part_ml, part_o
+        _p, _p,              # dev_err, stream
+    ]),
+    "b2_combine": (ctypes.c_int, [
+        _p, _p, _i32,        # part_ml, part_o, num_parts
+        _p, _i32, _i32,      # seq_lens, blocks_per_split, batch
+        _p, _p, _p,          # out, state_ml, state_o
+        _p,                  # stream
+    ]),
+}
+
+_LIB = None
+
+
+class B2Error(RuntimeError):
+    """A C-ABI call returned a negative status."""
+
+    def __init__(self, code: int, message: str):
+        super().__init__(f"{message} (status {code})")
+        self.code = code
+
+
+def load() -> ctypes.CDLL:
+    """Load libb2attn.so once and bind every exported entry point."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    if not LIB_PATH.exists():
+        raise RuntimeError(
+            f"{LIB_PATH.name} is not built; run __graft_entry__.build() "
+            f"(or python {LIB_PATH.parent.name}/build.py)")
+    lib = ctypes.CDLL(str(LIB_PATH))
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _LIB = lib
+    return lib
+
+
+def last_error() -> str:
+    buf = ctypes.create_string_buffer(512)
+    load().b2_last_error(buf, len(buf))
+    return buf.value.decode(errors="replace")
+
+
+def check(status: int, call: str) -> None:
+    if status != B2_OK:
+        raise B2Error(status, f"{call}: {last_error()}")
+
+
+def decode_dev_err(word: int) -> list[str]:
+    return [text for bit, text in DEV_ERR_NAMES.items() if word & bit]

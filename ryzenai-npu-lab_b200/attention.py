@@ -1,0 +1,224 @@
+"""Torch-facing wrappers over the C ABI, and the decode-attention runner.
+
+PyTorch provides device memory and streams here; every byte of attention
+math runs in libb2attn.so (see _lib.py).  Each wrapper checks dtypes, shapes,
+devices and contiguity on the host (raising ValueError like the reference's
+operators, e.g. experiments/lfm25_attention_context_cache_kernel.py:25-26) and
+raises B2Error when the library refuses a call.  Device-side faults (a bad
+block id, a length beyond the block table) are collected in a device word
+that `PagedDecodeAttention.check()` reads and turns into RuntimeError, like
+the reference's failed-run check (experiments/npu_direct.py:110-114).
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from . import _lib
+from .paged_cache import BLOCK, PagedKVCache
+from .rope import rope_table
+
+HQ, HKV, D = 16, 8, 64
+QKV_WIDTH = (HQ + 2 * HKV) * D
+SCALE = D ** -0.5
+EPS = 1.0e-5
+B200_SMS = 148
+
+
+def _ptr(t: torch.Tensor | None):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(device: torch.device, stream: torch.cuda.Stream | None):
+    s = stream if stream is not None else torch.cuda.current_stream(device)
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+def _need(t: torch.Tensor, name: str, dtype: torch.dtype, device: torch.device, shape=None):
+    if not isinstance(t, torch.Tensor):
+        raise ValueError(f"{name} must be a tensor")
+    if t.dtype != dtype:
+        raise ValueError(f"{name} must be {dtype}, got {t.dtype}")
+    if t.device != device:
+        raise ValueError(f"{name} must be on {device}, got {t.device}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    if shape is not None and tuple(t.shape) != tuple(shape):
+        raise ValueError(f"{name} must have shape {tuple(shape)}, got {tuple(t.shape)}")
+
+
+def append_rope(qkv: torch.Tensor, past_lens: torch.Tensor, *, q_out: torch.Tensor | None,
+                dev_err: torch.Tensor, mode: int = _lib.B2_NORM_QK | _lib.B2_ROPE_QK | _lib.B2_STORE_KV,
+                gamma_q: torch.Tensor | None = None, gamma_k: torch.Tensor | None = None,
+                cos: torch.Tensor | None = None, sin: torch.Tensor | None = None,
+                k_pool: torch.Tensor | None = None, v_pool: torch.Tensor | None = None,
+                block_tables: torch.Tensor | None = None, eps: float = EPS,
+                stream: torch.cuda.Stream | None = None) -> None:
+    """q/k RMSNorm + RoPE at position past_lens[b] + write of k, v into slot
+    past_lens[b] of the pool (b2_append_rope).  qkv: bf16 [B, W >= 2048]."""
+    dev = qkv.device
+    if qkv.dim() != 2 or qkv.shape[1] < QKV_WIDTH:
+        raise ValueError(f"qkv must be [batch, >= {QKV_WIDTH}], got {tuple(qkv.shape)}")
+    _need(qkv, "qkv", torch.bfloat16, dev)
+    b = qkv.shape[0]
+    _need(past_lens, "past_lens", torch.int32, dev, (b,))
+    _need(dev_err, "dev_err", torch.int32, dev)
+    if q_out is not None:
+        _need(q_out, "q_out", torch.bfloat16, dev, (b, HQ, D))
+    rope_rows = 0
+    if mode & _lib.B2_NORM_QK:
+        _need(gamma_q, "gamma_q", torch.bfloat16, dev, (D,))
+        _need(gamma_k, "gamma_k", torch.bfloat16, dev, (D,))
+    if mode & _lib.B2_ROPE_QK:
+        _need(cos, "cos", torch.bfloat16, dev)
+        _need(sin, "sin", torch.bfloat16, dev, tuple(cos.shape))
+        if cos.dim() != 2 or cos.shape[1] != D:
+            raise ValueError("cos/sin must be [positions, 64]")
+        rope_rows = cos.shape[0]
+    max_blocks = num_blocks = 0
+    if mode & _lib.B2_STORE_KV:
+        _need(k_pool, "k_pool", torch.bfloat16, dev)
+        _need(v_pool, "v_pool", torch.bfloat16, dev, tuple(k_pool.shape))
+        if k_pool.dim() != 4 or tuple(k_pool.shape[1:]) != (HKV, BLOCK, D):
+            raise ValueError("pools must be [num_blocks, 8, 64, 64]")
+        _need(block_tables, "block_tables", torch.int32, dev)
+        if block_tables.dim() != 2 or block_tables.shape[0] != b:
+            raise ValueError("block_tables must be [batch, max_blocks_per_seq]")
+        max_blocks, num_blocks = block_tables.shape[1], k_pool.shape[0]
+    rc = _lib.load().b2_append_rope(
+        _ptr(qkv), qkv.stride(0), _ptr(gamma_q), _ptr(gamma_k), ctypes.c_float(eps),
+        _ptr(cos), _ptr(sin), rope_rows, _ptr(past_lens), _ptr(block_tables), max_blocks,
+        _ptr(k_pool), _ptr(v_pool), num_blocks, _ptr(q_out), b, mode, _ptr(dev_err),
+        _stream(dev, stream))
+    _lib.check(rc, "b2_append_rope")
+
+
+def num_splits_for(max_blocks: int, blocks_per_split: int) -> int:
+    return max(1, (max_blocks + blocks_per_split - 1) // blocks_per_split)
+
+
+def choose_blocks_per_split(batch: int, work_blocks: int, sms: int = B200_SMS) -> int:
+    """Blocks per CTA so that the (split, kv head, sequence) grid gives about
+    8 CTAs per SM of real work (3 are resident at a time; the rest balance the
+    tail).  work_blocks: total 64-token blocks over the batch (one head)."""
+    target = 8 * sms
+    return int(min(64, max(2, math.ceil(work_blocks * HKV / target))))
+
+
+def decode_attn(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
+                block_tables: torch.Tensor, seq_lens: torch.Tensor, *, blocks_per_split: int,
+                part_ml: torch.Tensor, part_o: torch.Tensor, dev_err: torch.Tensor,
+                scale: float = SCALE, stream: torch.cuda.Stream | None = None) -> int:
+    """Split-KV decode (b2_decode_attn) into partial states; returns num_splits."""
+    dev = q.device
+    b = q.shape[0]
+    _need(q, "q", torch.bfloat16, dev, (b, HQ, D))
+    _need(k_pool, "k_pool", torch.bfloat16, dev)
+    _need(v_pool, "v_pool", torch.bfloat16, dev, tuple(k_pool.shape))
+    if k_pool.dim() != 4 or tuple(k_pool.shape[1:]) != (HKV, BLOCK, D):
+        raise ValueError("pools must be [num_blocks, 8, 64, 64]")
+    _need(block_tables, "block_tables", torch.int32, dev)
+    if block_tables.dim() != 2 or block_tables.shape[0] != b:
+        raise ValueError("block_tables must be [batch, max_blocks_per_seq]")
+    _need(seq_lens, "seq_lens", torch.int32, dev, (b,))
+    max_blocks = block_tables.shape[1]
+    splits = num_splits_for(max_blocks, blocks_per_split)
+    _need(part_ml, "part_ml", torch.float32, dev)
+    _need(part_o, "part_o", torch.float32, dev)
+    if part_ml.numel() < b * splits * HQ * 2 or part_o.numel() < b * splits * HQ * D:
+        raise ValueError(f"partial-state buffers too small for {b} x {splits} splits")
+    rc = _lib.load().b2_decode_attn(
+        _ptr(q), _ptr(k_pool), _ptr(v_pool), k_pool.shape[0], _ptr(block_tables), max_blocks,
+        _ptr(seq_lens), b, blocks_per_split, splits, ctypes.c_float(scale), _ptr(part_ml),
+        _ptr(part_o), _ptr(dev_err), _stream(dev, stream))
+    _lib.check(rc, "b2_decode_attn")
+    return splits
+
+
+def combine(part_ml: torch.Tensor, part_o: torch.Tensor, num_parts: int, batch: int, *,
+            seq_lens: torch.Tensor | None = None, blocks_per_split: int = 1,
+            out: torch.Tensor | None = None, state_ml: torch.Tensor | None = None,
+            state_o: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None) -> None:
+    """Log-sum-exp merge (b2_combine) into bf16 out [B, 16, 64] and/or a merged
+    fp32 state (state_ml [B, 16, 2], state_o [B, 16, 64])."""
+    dev = part_ml.device
+    _need(part_ml, "part_ml", torch.float32, dev)
+    _need(part_o, "part_o", torch.float32, dev)
+    if part_ml.numel() < batch * num_parts * HQ * 2 or part_o.numel() < batch * num_parts * HQ * D:
+        raise ValueError("partial-state buffers smaller than batch x num_parts")
+    if seq_lens is not None:
+        _need(seq_lens, "seq_lens", torch.int32, dev, (batch,))
+    if out is not None:
+        _need(out, "out", torch.bfloat16, dev)
+        if out.numel() != batch * HQ * D:
+            raise ValueError("out must hold batch x 16 x 64 elements")
+    if state_o is not None:
+        _need(state_ml, "state_ml", torch.float32, dev, (batch, HQ, 2))
+        _need(state_o, "state_o", torch.float32, dev, (batch, HQ, D))
+    rc = _lib.load().b2_combine(
+        _ptr(part_ml), _ptr(part_o), num_parts, _ptr(seq_lens), blocks_per_split, batch,
+        _ptr(out), _ptr(state_ml), _ptr(state_o), _stream(dev, stream))
+    _lib.check(rc, "b2_combine")
+
+
+class PagedDecodeAttention:
+    """Decode attention of one new token per sequence over a PagedKVCache.
+
+    step(layer, qkv, past_lens, seq_lens) runs, on the current stream:
+      b2_append_rope  (q/k norm + RoPE, k/v into slot past_lens[b])
+      b2_decode_attn  (split-KV flash-decode over seq_lens[b] tokens)
+      b2_combine      (partial states -> bf16 context [B, 16, 64])
+    seq_lens must equal past_lens + 1 (the new token is attended).  All
+    buffers are allocated here once; step() allocates nothing, so it can be
+    captured in a CUDA graph.
+    """
+
+    def __init__(self, cache: PagedKVCache, gamma_q: torch.Tensor, gamma_k: torch.Tensor,
+                 max_batch: int, rope_positions: int, *, eps: float = EPS,
+                 blocks_per_split: int | None = None, work_blocks: int | None = None):
+        self.cache = cache
+        dev = cache.device
+        self.device = dev
+        self.eps = eps
+        self.gamma_q = gamma_q.to(dev, torch.bfloat16).contiguous()
+        self.gamma_k = gamma_k.to(dev, torch.bfloat16).contiguous()
+        self.cos, self.sin = rope_table(rope_positions, device=dev)
+        if blocks_per_split is None:
+            wb = work_blocks if work_blocks is not None else max_batch * cache.max_blocks
+            blocks_per_split = choose_blocks_per_split(max_batch, wb)
+        self.blocks_per_split = blocks_per_split
+        self.num_splits = num_splits_for(cache.max_blocks, blocks_per_split)
+        self.max_batch = max_batch
+        self.q = torch.empty(max_batch, HQ, D, dtype=torch.bfloat16, device=dev)
+        self.part_ml = torch.empty(max_batch, self.num_splits, HQ, 2, dtype=torch.float32, device=dev)
+        self.part_o = torch.empty(max_batch, self.num_splits, HQ, D, dtype=torch.float32, device=dev)
+        self.out = torch.empty(max_batch, HQ, D, dtype=torch.bfloat16, device=dev)
+        self.dev_err = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def step(self, layer: int, qkv: torch.Tensor, past_lens: torch.Tensor, seq_lens: torch.Tensor,
+             block_tables: torch.Tensor, out: torch.Tensor | None = None,
+             stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        b = qkv.shape[0]
+        if b > self.max_batch:
+            raise ValueError(f"batch {b} > max_batch {self.max_batch}")
+        kp, vp = self.cache.pool(layer)
+        q = self.q[:b]
+        append_rope(qkv, past_lens, q_out=q, dev_err=self.dev_err, gamma_q=self.gamma_q,
+                    gamma_k=self.gamma_k, cos=self.cos, sin=self.sin, k_pool=kp, v_pool=vp,
+                    block_tables=block_tables, eps=self.eps, stream=stream)
+        splits = decode_attn(q, kp, vp, block_tables, seq_lens, blocks_per_split=self.blocks_per_split,
+                             part_ml=self.part_ml, part_o=self.part_o, dev_err=self.dev_err,
+                             stream=stream)
+        o = self.out[:b] if out is None else out
+        combine(self.part_ml, self.part_o, splits, b, seq_lens=seq_lens,
+                blocks_per_split=self.blocks_per_split, out=o, stream=stream)
+        return o
+
+    def check(self) -> None:
+        """Synchronise on the device error word; raise if any kernel flagged one."""
+        word = int(self.dev_err.item())
+        if word:
+            self.dev_err.zero_()
+            raise RuntimeError("decode attention device error: " + "; ".join(_lib.decode_dev_err(word)))

@@ -1,0 +1,688 @@
+// B200 (sm_100a) kernels and C ABI for LFM2.5 decode attention.
+//
+//   append_rope_kernel   q/k RMSNorm + rotate-half RoPE + paged KV append
+//   paged_decode_kernel  split-KV flash-decode, TMA + mbarrier pipeline
+//   combine_kernel       log-sum-exp merge of partial softmax states
+//
+// Model constants: 16 query heads, 8 KV heads, head_dim 64, 64-token blocks.
+// The numerics follow the reference's PyTorch BF16 path (Hugging Face
+// transformers Lfm2Attention, modeling_lfm2.py: Lfm2RMSNorm.forward 59-64,
+// apply_rotary_pos_emb 163-185, sdpa/eager attention 200-223), which is what
+// the reference's fixtures were generated with (006_lfm25_baseline.py:115-117).
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+#include <stdarg.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <string.h>
+
+#include "b2_decode_attn.h"
+
+namespace {
+
+constexpr int kHq = 16;
+constexpr int kHkv = 8;
+constexpr int kDim = 64;
+constexpr int kBlock = 64;
+constexpr int kQkvWidth = (kHq + 2 * kHkv) * kDim;  // 2048
+
+// decode kernel geometry
+constexpr int kStages = 4;
+constexpr int kConsumerWarps = 4;
+constexpr int kDecodeThreads = (kConsumerWarps + 1) * 32;
+constexpr int kTileBytes = kBlock * kDim * 2;  // one (block, head) tile: 8 KiB
+constexpr int kStageBytes = 2 * kTileBytes;    // K tile + V tile
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s, then report and return
+
+struct __align__(8) DecodeTail {
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  float red[kConsumerWarps][2][2 + kDim];
+};
+constexpr int kDecodeSmem = kStages * kStageBytes + 1024 + (int)sizeof(DecodeTail);
+
+thread_local char g_err[512];
+
+int fail(int code, const char *fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int ok() {
+  g_err[0] = 0;
+  return B2_OK;
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ------------------------------------------------------------------ device helpers
+
+__device__ __forceinline__ void unpack8(const uint4 &w, float f[8]) {
+  const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(u[i] << 16);
+    f[2 * i + 1] = __uint_as_float(u[i] & 0xffff0000u);
+  }
+}
+
+// round-to-nearest-even fp32 -> bf16 bits (the rounding torch uses on CPU)
+__device__ __forceinline__ uint32_t bf16_bits(float x) {
+  return static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(x)));
+}
+
+__device__ __forceinline__ float bf16_round(float x) {
+  return __uint_as_float(bf16_bits(x) << 16);
+}
+
+__device__ __forceinline__ uint4 pack8(const float f[8]) {
+  uint4 w;
+  w.x = bf16_bits(f[0]) | (bf16_bits(f[1]) << 16);
+  w.y = bf16_bits(f[2]) | (bf16_bits(f[3]) << 16);
+  w.z = bf16_bits(f[4]) | (bf16_bits(f[5]) << 16);
+  w.w = bf16_bits(f[6]) | (bf16_bits(f[7]) << 16);
+  return w;
+}
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Wait for the phase with the given parity to complete; false after
+// kWaitLimitNs (the caller reports B2_DEV_TIMEOUT and unwinds).
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+  if (mbar_try(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (;;) {
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try(bar, parity)) return true;
+    if (global_ns() - t0 > kWaitLimitNs) return false;
+  }
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
+// 2-D tiled TMA load (no multicast) completing on an mbarrier; KV tiles are
+// read once per step, so they are marked evict-first in L2.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y,
+                                            uint32_t bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ uint64_t evict_first_policy() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+__device__ __forceinline__ void consumer_bar() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+}
+
+// ------------------------------------------------------------------ append + RoPE
+
+struct AppendArgs {
+  const uint16_t *qkv;
+  int64_t row_stride;
+  const uint16_t *gamma_q, *gamma_k;
+  float eps;
+  const uint16_t *cos, *sin;
+  int rope_rows;
+  const int32_t *past_lens;
+  const int32_t *block_tables;
+  int max_blocks;
+  uint16_t *k_pool, *v_pool;
+  int num_blocks;
+  uint16_t *q_out;
+  int mode;
+  int32_t *err;
+};
+
+// One CTA (8 warps) per sequence.  The 32 head vectors of a qkv row
+// (16 q, 8 k, 8 v) are split 4 per warp; 8 lanes own one vector, 8
+// consecutive bf16 (16 bytes) each, so loads and stores are 16-byte
+// vectors and a vector's rotate-half partner chunk (d +- 32) sits on lane^4.
+__global__ void __launch_bounds__(256) append_rope_kernel(const AppendArgs a) {
+  const int b = blockIdx.x;
+  const int lane = threadIdx.x & 31;
+  const int vec = (threadIdx.x >> 5) * 4 + (lane >> 3);  // 0..31
+  const int j = lane & 7;                                // 16-byte chunk
+  const bool is_q = vec < kHq;
+  const bool is_v = vec >= kHq + kHkv;
+  const int pos = a.past_lens[b];
+
+  float x[8];
+  unpack8(*reinterpret_cast<const uint4 *>(a.qkv + b * a.row_stride + vec * kDim + j * 8), x);
+
+  if (!is_v && (a.mode & B2_NORM_QK)) {
+    // Lfm2RMSNorm: gamma * bf16(x * 1/sqrt(mean(x^2) + eps)), fp32 math,
+    // IEEE-rounded sqrt and divide like torch's CPU rsqrt.
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss = fmaf(x[e], x[e], ss);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 4);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ss * (1.0f / kDim), a.eps)));
+    float g[8];
+    unpack8(*reinterpret_cast<const uint4 *>((is_q ? a.gamma_q : a.gamma_k) + j * 8), g);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) x[e] = bf16_round(__fmul_rn(g[e], bf16_round(__fmul_rn(x[e], inv))));
+  }
+
+  const bool pos_ok = pos >= 0 && pos < a.max_blocks * kBlock;
+  if (!is_v && (a.mode & B2_ROPE_QK)) {
+    // q*cos + rotate_half(q)*sin with bf16 rounding after each product and
+    // after the sum; rotate_half(x) = [-x[32:], x[:32]].
+    float p[8];
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+      const uint32_t w = bf16_bits(x[e]) | (bf16_bits(x[e + 1]) << 16);
+      const uint32_t o = __shfl_xor_sync(0xffffffffu, w, 4);
+      p[e] = __uint_as_float(o << 16);
+      p[e + 1] = __uint_as_float(o & 0xffff0000u);
+    }
+    const bool rope_ok = pos >= 0 && pos < a.rope_rows;
+    if (!rope_ok) {
+      if (j == 0 && vec == 0) atomicOr(a.err, B2_DEV_BAD_POSITION);
+    } else {
+      float c[8], s[8];
+      unpack8(*reinterpret_cast<const uint4 *>(a.cos + (int64_t)pos * kDim + j * 8), c);
+      unpack8(*reinterpret_cast<const uint4 *>(a.sin + (int64_t)pos * kDim + j * 8), s);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float rot = j < 4 ? -p[e] : p[e];
+        const float part1 = bf16_round(__fmul_rn(x[e], c[e]));
+        const float part2 = bf16_round(__fmul_rn(rot, s[e]));
+        x[e] = bf16_round(__fadd_rn(part1, part2));
+      }
+    }
+  }
+
+  if (is_q) {
+    if (a.q_out)
+      *reinterpret_cast<uint4 *>(a.q_out + ((int64_t)b * kHq + vec) * kDim + j * 8) = pack8(x);
+    return;
+  }
+  if (!(a.mode & B2_STORE_KV)) return;
+  if (!pos_ok) {
+    if (j == 0 && vec == kHq) atomicOr(a.err, B2_DEV_BAD_LENGTH);
+    return;
+  }
+  const int blk = a.block_tables[(int64_t)b * a.max_blocks + pos / kBlock];
+  if (blk < 0 || blk >= a.num_blocks) {
+    if (j == 0 && vec == kHq) atomicOr(a.err, B2_DEV_BAD_BLOCK);
+    return;
+  }
+  const int head = is_v ? vec - kHq - kHkv : vec - kHq;
+  const int64_t off = (((int64_t)blk * kHkv + head) * kBlock + (pos % kBlock)) * kDim + j * 8;
+  *reinterpret_cast<uint4 *>((is_v ? a.v_pool : a.k_pool) + off) = pack8(x);
+}
+
+// ------------------------------------------------------------------ split-KV decode
+
+struct DecodeArgs {
+  const uint16_t *q;
+  const int32_t *block_tables;
+  int max_blocks;
+  const int32_t *seq_lens;
+  int num_blocks;
+  int blocks_per_split;
+  int num_splits;
+  float scale_log2;
+  float *part_ml;
+  float *part_o;
+  int32_t *err;
+};
+
+// grid (num_splits, 8 kv heads, batch), 4 consumer warps + 1 producer warp.
+//
+// Producer (warp 4, lane 0): for each 64-token block of the split, TMA-loads
+// the K and V tiles of this KV head (8 KiB each, rows swizzled in 128-byte
+// groups) into a ring of kStages stages, each guarded by a full/empty
+// mbarrier pair.
+//
+// Consumers: warp w owns rows [16w, 16w+16) of every tile and keeps its own
+// online-softmax state (running max m and sum l per query head, log2 units).
+//  * q.K: lane (r = lane/2, half = lane%2) dots 32 dims of row r with both
+//    query heads (2kv, 2kv+1) and the pair is summed by one shuffle.
+//  * p.V: lane (c = lane%8, g = lane/8) accumulates 8 dims (chunk c) of rows
+//    4g..4g+3 for both heads in 16 fp32 registers.
+// The 128-byte swizzle makes both access patterns bank-conflict free.
+// Warps and lanes are merged once per CTA into the partial state.
+__global__ void __launch_bounds__(kDecodeThreads, 3)
+    paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
+                        const __grid_constant__ CUtensorMap tm_v, const DecodeArgs a) {
+  const int split = blockIdx.x;
+  const int kvh = blockIdx.y;
+  const int b = blockIdx.z;
+  const int seq_len = a.seq_lens[b];
+  if (seq_len < 0 || seq_len > a.max_blocks * kBlock) {
+    if (threadIdx.x == 0 && split == 0 && kvh == 0) atomicOr(a.err, B2_DEV_BAD_LENGTH);
+    return;
+  }
+  const int nblk = (seq_len + kBlock - 1) / kBlock;
+  const int b0 = split * a.blocks_per_split;
+  const int b1 = min(nblk, b0 + a.blocks_per_split);
+  if (b0 >= b1) return;  // this split lies past the end of the sequence
+  const int n = b1 - b0;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *tiles = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  DecodeTail *tail = reinterpret_cast<DecodeTail *>(tiles + kStages * kStageBytes);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(smem_u32(&tail->full[s]), 1);
+      mbar_init(smem_u32(&tail->empty[s]), kConsumerWarps);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+
+  if (warp == kConsumerWarps) {
+    if (lane != 0) return;
+    // ---------------- producer
+    const uint64_t policy = evict_first_policy();
+    const int32_t *tbl = a.block_tables + (int64_t)b * a.max_blocks + b0;
+    int issued = 0;
+    for (int i = 0; i < n; ++i) {
+      const int s = i % kStages;
+      const uint32_t ph = (i / kStages) & 1;
+      if (i >= kStages && !mbar_wait(smem_u32(&tail->empty[s]), ph ^ 1)) {
+        atomicOr(a.err, B2_DEV_TIMEOUT);
+        break;
+      }
+      int blk = tbl[i];
+      if (blk < 0 || blk >= a.num_blocks) {
+        atomicOr(a.err, B2_DEV_BAD_BLOCK);
+        blk = 0;  // read a valid tile instead; the result is flagged as bad
+      }
+      const int row = (blk * kHkv + kvh) * kBlock;
+      const uint32_t full = smem_u32(&tail->full[s]);
+      uint8_t *dst = tiles + s * kStageBytes;
+      mbar_expect_tx(full, kStageBytes);
+      tma_load_2d(smem_u32(dst), &tm_k, 0, row, full, policy);
+      tma_load_2d(smem_u32(dst + kTileBytes), &tm_v, 0, row, full, policy);
+      issued = i + 1;
+    }
+    // Do not leave while a copy into this CTA's shared memory is in flight:
+    // wait (bounded) for the last phase issued on every stage.
+    for (int s = 0; s < kStages && s < issued; ++s) {
+      const int last = s + kStages * ((issued - 1 - s) / kStages);
+      if (!mbar_wait(smem_u32(&tail->full[s]), (last / kStages) & 1)) atomicOr(a.err, B2_DEV_TIMEOUT);
+    }
+    return;
+  }
+
+  // ---------------- consumers
+  const int r = lane >> 1, half = lane & 1;  // q.K mapping
+  const int c = lane & 7, g = lane >> 3;     // p.V mapping
+  float q0[32], q1[32];
+  {
+    const uint16_t *qb = a.q + ((int64_t)b * kHq + 2 * kvh) * kDim + half * 32;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      unpack8(*reinterpret_cast<const uint4 *>(qb + k * 8), q0 + k * 8);
+      unpack8(*reinterpret_cast<const uint4 *>(qb + kDim + k * 8), q1 + k * 8);
+    }
+  }
+  float m0 = -1.0e30f, m1 = -1.0e30f;  // finite floor: exp2 of (floor - floor) stays 1
+  float lsum = 0.f;                    // this lane's sum for head `half`
+  float acc0[8], acc1[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) acc0[e] = acc1[e] = 0.f;
+
+  const int qrow = 16 * warp + r;
+  for (int i = 0; i < n; ++i) {
+    const int s = i % kStages;
+    const uint32_t ph = (i / kStages) & 1;
+    if (!mbar_wait(smem_u32(&tail->full[s]), ph)) {
+      if (lane == 0) atomicOr(a.err, B2_DEV_TIMEOUT);
+      break;
+    }
+    const uint8_t *kt = tiles + s * kStageBytes;
+    const uint8_t *vt = kt + kTileBytes;
+    const int valid = seq_len - ((b0 + i) * kBlock + 16 * warp);  // valid rows of this warp
+
+    float d0 = 0.f, d1 = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int pc = (half * 4 + k) ^ (qrow & 7);
+      float f[8];
+      unpack8(*reinterpret_cast<const uint4 *>(kt + qrow * 128 + pc * 16), f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        d0 = fmaf(q0[k * 8 + e], f[e], d0);
+        d1 = fmaf(q1[k * 8 + e], f[e], d1);
+      }
+    }
+    d0 += __shfl_xor_sync(0xffffffffu, d0, 1);
+    d1 += __shfl_xor_sync(0xffffffffu, d1, 1);
+    const bool tv = r < valid;
+    const float s0 = tv ? d0 * a.scale_log2 : -INFINITY;
+    const float s1 = tv ? d1 * a.scale_log2 : -INFINITY;
+    float bm0 = s0, bm1 = s1;
+#pragma unroll
+    for (int off = 2; off < 32; off <<= 1) {
+      bm0 = fmaxf(bm0, __shfl_xor_sync(0xffffffffu, bm0, off));
+      bm1 = fmaxf(bm1, __shfl_xor_sync(0xffffffffu, bm1, off));
+    }
+    const float mn0 = fmaxf(m0, bm0), mn1 = fmaxf(m1, bm1);
+    const float a0 = ex2(m0 - mn0), a1 = ex2(m1 - mn1);
+    m0 = mn0;
+    m1 = mn1;
+    const float p = ex2((half ? s1 : s0) - (half ? mn1 : mn0));  // 0 for masked rows
+    lsum = fmaf(lsum, half ? a1 : a0, p);
+
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      acc0[e] *= a0;
+      acc1[e] *= a1;
+    }
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) {
+      const int t = 4 * g + jj;
+      const float p0 = __shfl_sync(0xffffffffu, p, 2 * t);
+      const float p1 = __shfl_sync(0xffffffffu, p, 2 * t + 1);
+      if (t < valid) {
+        const int vrow = 16 * warp + t;
+        float f[8];
+        unpack8(*reinterpret_cast<const uint4 *>(vt + vrow * 128 + ((c ^ (vrow & 7)) * 16)), f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          acc0[e] = fmaf(p0, f[e], acc0[e]);
+          acc1[e] = fmaf(p1, f[e], acc1[e]);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(&tail->empty[s]));
+  }
+
+  // ---------------- merge lanes, then warps
+#pragma unroll
+  for (int off = 2; off < 32; off <<= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, off);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    acc0[e] += __shfl_xor_sync(0xffffffffu, acc0[e], 8);
+    acc0[e] += __shfl_xor_sync(0xffffffffu, acc0[e], 16);
+    acc1[e] += __shfl_xor_sync(0xffffffffu, acc1[e], 8);
+    acc1[e] += __shfl_xor_sync(0xffffffffu, acc1[e], 16);
+  }
+  if (lane < 8) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      tail->red[warp][0][2 + c * 8 + e] = acc0[e];
+      tail->red[warp][1][2 + c * 8 + e] = acc1[e];
+    }
+  }
+  if (lane < 2) {
+    tail->red[warp][lane][0] = lane ? m1 : m0;
+    tail->red[warp][lane][1] = lsum;
+  }
+  consumer_bar();
+  const int h = threadIdx.x >> 6;  // 0..1
+  const int d = threadIdx.x & 63;
+  float M = -1.0e30f;
+#pragma unroll
+  for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, tail->red[w][h][0]);
+  float L = 0.f, O = 0.f;
+#pragma unroll
+  for (int w = 0; w < kConsumerWarps; ++w) {
+    const float sc = ex2(tail->red[w][h][0] - M);
+    L = fmaf(tail->red[w][h][1], sc, L);
+    O = fmaf(tail->red[w][h][2 + d], sc, O);
+  }
+  const int64_t idx = ((int64_t)b * a.num_splits + split) * kHq + 2 * kvh + h;
+  a.part_o[idx * kDim + d] = O;
+  if (d == 0) {
+    a.part_ml[idx * 2] = M;
+    a.part_ml[idx * 2 + 1] = L;
+  }
+}
+
+// ------------------------------------------------------------------ combine
+
+struct CombineArgs {
+  const float *part_ml;
+  const float *part_o;
+  int num_parts;
+  const int32_t *seq_lens;
+  int blocks_per_split;
+  uint16_t *out;
+  float *state_ml;
+  float *state_o;
+};
+
+// grid (batch), block (16 heads x 64 dims); one thread per output element.
+__global__ void __launch_bounds__(1024) combine_kernel(const CombineArgs a) {
+  const int b = blockIdx.x;
+  const int h = threadIdx.x >> 6;
+  const int d = threadIdx.x & 63;
+  int parts = a.num_parts;
+  if (a.seq_lens) {
+    const int len = max(a.seq_lens[b], 0);
+    const int nblk = (len + kBlock - 1) / kBlock;
+    parts = min(parts, (nblk + a.blocks_per_split - 1) / a.blocks_per_split);
+  }
+  const float *ml = a.part_ml + ((int64_t)b * a.num_parts * kHq + h) * 2;
+  const float *po = a.part_o + ((int64_t)b * a.num_parts * kHq + h) * kDim + d;
+  float M = -1.0e30f;
+  for (int s = 0; s < parts; ++s) M = fmaxf(M, ml[s * kHq * 2]);
+  float L = 0.f, O = 0.f;
+  for (int s = 0; s < parts; ++s) {
+    const float sc = ex2(ml[s * kHq * 2] - M);
+    L = fmaf(ml[s * kHq * 2 + 1], sc, L);
+    O = fmaf(po[(int64_t)s * kHq * kDim], sc, O);
+  }
+  const int64_t oi = ((int64_t)b * kHq + h) * kDim + d;
+  if (a.out) a.out[oi] = static_cast<uint16_t>(bf16_bits(L > 0.f ? O / L : 0.f));
+  if (a.state_o) {
+    a.state_o[oi] = O;
+    if (d == 0) {
+      a.state_ml[((int64_t)b * kHq + h) * 2] = M;
+      a.state_ml[((int64_t)b * kHq + h) * 2 + 1] = L;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ host helpers
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// Pool viewed as a 2-D tensor: 64 bf16 per row, num_blocks*8*64 rows; a box
+// is one (block, head) tile of 64 rows, swizzled in 128-byte groups.
+int make_pool_map(CUtensorMap *map, const void *pool, int num_blocks) {
+  auto fn = encode_fn();
+  if (!fn) return fail(B2_ERR_NOSYM, "cuTensorMapEncodeTiled is not available from the driver");
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(kDim),
+                              static_cast<cuuint64_t>(num_blocks) * kHkv * kBlock};
+  const cuuint64_t strides[1] = {kDim * 2};
+  const cuuint32_t box[2] = {kDim, kBlock};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(pool), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(B2_ERR_ARG, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return B2_OK;
+}
+
+int launch_status(const char *what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(B2_ERR_CUDA, "%s launch failed: %s", what, cudaGetErrorString(e));
+  return ok();
+}
+
+bool decode_smem_ready() {
+  // cudaFuncSetAttribute is per device; remember which devices are set up.
+  static bool done[128] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return false;
+  if (!done[dev]) {
+    if (cudaFuncSetAttribute(paged_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kDecodeSmem) != cudaSuccess)
+      return false;
+    done[dev] = true;
+  }
+  return true;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ C ABI
+
+extern "C" int b2_version(void) { return 100; }
+
+extern "C" int b2_last_error(char *buf, int len) {
+  const int n = static_cast<int>(strlen(g_err));
+  if (buf && len > 0) {
+    const int m = n < len - 1 ? n : len - 1;
+    memcpy(buf, g_err, m);
+    buf[m] = 0;
+  }
+  return n;
+}
+
+extern "C" int b2_append_rope(const uint16_t *qkv, int64_t row_stride, const uint16_t *gamma_q,
+                              const uint16_t *gamma_k, float eps, const uint16_t *rope_cos,
+                              const uint16_t *rope_sin, int32_t rope_rows, const int32_t *past_lens,
+                              const int32_t *block_tables, int32_t max_blocks_per_seq,
+                              uint16_t *k_pool, uint16_t *v_pool, int32_t num_blocks, uint16_t *q_out,
+                              int32_t batch, int32_t mode, int32_t *dev_err, void *stream) {
+  if (batch < 0) return fail(B2_ERR_ARG, "batch must be >= 0 (got %d)", batch);
+  if (batch == 0) return ok();
+  if (!qkv || !past_lens || !dev_err) return fail(B2_ERR_ARG, "qkv, past_lens and dev_err are required");
+  if (mode & ~(B2_NORM_QK | B2_ROPE_QK | B2_STORE_KV)) return fail(B2_ERR_ARG, "unknown mode bits 0x%x", mode);
+  if (row_stride < kQkvWidth || row_stride % 8 != 0)
+    return fail(B2_ERR_ARG, "row_stride must be >= %d and a multiple of 8 (got %lld)", kQkvWidth,
+                (long long)row_stride);
+  if (!aligned16(qkv) || (q_out && !aligned16(q_out)))
+    return fail(B2_ERR_ARG, "qkv and q_out must be 16-byte aligned");
+  if ((mode & B2_NORM_QK) && (!gamma_q || !gamma_k || !aligned16(gamma_q) || !aligned16(gamma_k)))
+    return fail(B2_ERR_ARG, "B2_NORM_QK needs 16-byte aligned gamma_q and gamma_k");
+  if ((mode & B2_ROPE_QK) &&
+      (!rope_cos || !rope_sin || rope_rows <= 0 || !aligned16(rope_cos) || !aligned16(rope_sin)))
+    return fail(B2_ERR_ARG, "B2_ROPE_QK needs 16-byte aligned cos/sin tables with rope_rows > 0");
+  if (mode & B2_STORE_KV) {
+    if (!block_tables || !k_pool || !v_pool || max_blocks_per_seq <= 0 || num_blocks <= 0)
+      return fail(B2_ERR_ARG, "B2_STORE_KV needs block_tables, k_pool, v_pool and positive sizes");
+    if (!aligned16(k_pool) || !aligned16(v_pool)) return fail(B2_ERR_ARG, "pools must be 16-byte aligned");
+  }
+  AppendArgs a{qkv, row_stride, gamma_q, gamma_k, eps, rope_cos, rope_sin, rope_rows, past_lens,
+               block_tables, max_blocks_per_seq > 0 ? max_blocks_per_seq : 1, k_pool, v_pool,
+               num_blocks, q_out, mode, dev_err};
+  append_rope_kernel<<<batch, 256, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  return launch_status("append_rope_kernel");
+}
+
+extern "C" int b2_decode_attn(const uint16_t *q, const uint16_t *k_pool, const uint16_t *v_pool,
+                              int32_t num_blocks, const int32_t *block_tables,
+                              int32_t max_blocks_per_seq, const int32_t *seq_lens, int32_t batch,
+                              int32_t blocks_per_split, int32_t num_splits, float scale,
+                              float *part_ml, float *part_o, int32_t *dev_err, void *stream) {
+  if (batch < 0) return fail(B2_ERR_ARG, "batch must be >= 0 (got %d)", batch);
+  if (batch == 0) return ok();
+  if (!q || !k_pool || !v_pool || !block_tables || !seq_lens || !part_ml || !part_o || !dev_err)
+    return fail(B2_ERR_ARG, "null pointer argument");
+  if (num_blocks <= 0 || static_cast<int64_t>(num_blocks) * kHkv * kBlock >= (int64_t(1) << 31))
+    return fail(B2_ERR_ARG, "num_blocks must be in [1, 2^22) (got %d)", num_blocks);
+  if (max_blocks_per_seq <= 0 || blocks_per_split <= 0)
+    return fail(B2_ERR_ARG, "max_blocks_per_seq and blocks_per_split must be positive");
+  if (static_cast<int64_t>(num_splits) * blocks_per_split < max_blocks_per_seq)
+    return fail(B2_ERR_ARG, "num_splits * blocks_per_split (%d * %d) < max_blocks_per_seq (%d)",
+                num_splits, blocks_per_split, max_blocks_per_seq);
+  if (num_splits > 65535 || batch > 65535) return fail(B2_ERR_ARG, "num_splits and batch must be <= 65535");
+  if (!aligned16(q) || !aligned16(k_pool) || !aligned16(v_pool))
+    return fail(B2_ERR_ARG, "q and the pools must be 16-byte aligned");
+  if (!(scale > 0.f)) return fail(B2_ERR_ARG, "scale must be positive");
+  CUtensorMap mk, mv;
+  int rc = make_pool_map(&mk, k_pool, num_blocks);
+  if (rc) return rc;
+  rc = make_pool_map(&mv, v_pool, num_blocks);
+  if (rc) return rc;
+  if (!decode_smem_ready()) return fail(B2_ERR_CUDA, "cannot set the decode kernel's shared memory size");
+  DecodeArgs a{q, block_tables, max_blocks_per_seq, seq_lens, num_blocks, blocks_per_split, num_splits,
+               scale * 1.4426950408889634f, part_ml, part_o, dev_err};
+  const dim3 grid(num_splits, kHkv, batch);
+  paged_decode_kernel<<<grid, kDecodeThreads, kDecodeSmem, static_cast<cudaStream_t>(stream)>>>(mk, mv, a);
+  return launch_status("paged_decode_kernel");
+}
+
+extern "C" int b2_combine(const float *part_ml, const float *part_o, int32_t num_parts,
+                          const int32_t *seq_lens, int32_t blocks_per_split, int32_t batch,
+                          uint16_t *out, float *state_ml, float *state_o, void *stream) {
+  if (batch < 0) return fail(B2_ERR_ARG, "batch must be >= 0 (got %d)", batch);
+  if (batch == 0) return ok();
+  if (!part_ml || !part_o || num_parts <= 0) return fail(B2_ERR_ARG, "partial states and num_parts > 0 required");
+  if (seq_lens && blocks_per_split <= 0) return fail(B2_ERR_ARG, "blocks_per_split must be positive");
+  if (!out && !state_o) return fail(B2_ERR_ARG, "one of out or state_o is required");
+  if ((state_o == nullptr) != (state_ml == nullptr)) return fail(B2_ERR_ARG, "state_ml and state_o go together");
+  CombineArgs a{part_ml, part_o, num_parts, seq_lens, blocks_per_split, out, state_ml, state_o};
+  combine_kernel<<<batch, kHq * kDim, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  return launch_status("combine_kernel");
+}

@@ -1,0 +1,144 @@
+"""Generate the golden fixtures in this folder from the reference's CPU path.
+
+The reference computes LFM2.5 attention on the CPU with Hugging Face
+transformers' Lfm2Attention + DynamicCache in BF16
+(experiments/006_lfm25_baseline.py:115-127, experiments/010_cpu_greedy.py:43-63).
+This script runs that code itself (transformers, imported here; it is a
+third-party package, not part of the reference tree) on seeded random-init
+inputs and stores its outputs as uint16 bf16 bit patterns.  The real
+checkpoint and the reference's own .npz fixtures (cache/*.npz) are not
+available, so the inputs are the seeded generators of oracle/lfm2_attention.py;
+a sha256 of every regenerated input is stored to pin the generators.
+
+Run from the repository root:  python tests/golden/make_golden.py
+Nothing at test time imports transformers; tests read the .npz files.
+"""
+from __future__ import annotations
+
+import hashlib
+import pathlib
+import sys
+
+import numpy as np
+import torch
+
+ROOT = pathlib.Path(__file__).resolve().parents[2]
+sys.path.insert(0, str(ROOT))
+
+import transformers  # noqa: E402
+from transformers import Lfm2Config  # noqa: E402
+from transformers.cache_utils import DynamicCache  # noqa: E402
+from transformers.models.lfm2 import modeling_lfm2 as hf  # noqa: E402
+
+from oracle import lfm2_attention as orc  # noqa: E402
+
+OUT = pathlib.Path(__file__).resolve().parent
+BF16 = torch.bfloat16
+LAYER_TYPES = ["conv", "conv", "full_attention", "conv", "full_attention", "conv",
+               "full_attention", "conv", "full_attention", "conv", "full_attention", "conv",
+               "full_attention", "conv"]  # experiments/lfm25_x8.py:55-57
+CASES = [0, 1, 21, 63, 64, 65, 512, 1000]   # cached tokens before the step
+ROPE_POSITIONS = [0, 1, 2, 21, 63, 64, 511, 512, 1000, 4095, 8191, 16383, 65535,
+                  131071, 131072, 131136]
+WEIGHT_SEED = 0
+
+
+def config(impl: str) -> Lfm2Config:
+    cfg = Lfm2Config(hidden_size=1024, intermediate_size=3840, num_hidden_layers=14,
+                     num_attention_heads=16, num_key_value_heads=8, vocab_size=65536,
+                     norm_eps=1e-5, layer_types=LAYER_TYPES,
+                     rope_parameters={"rope_type": "default", "rope_theta": 1.0e6})
+    cfg._attn_implementation = impl
+    return cfg
+
+
+def sha(*tensors) -> str:
+    h = hashlib.sha256()
+    for t in tensors:
+        h.update(orc.bits(t).tobytes())
+    return h.hexdigest()
+
+
+def run_case(length: int, impl: str, weights: dict) -> dict:
+    cfg = config(impl)
+    attn = hf.Lfm2Attention(cfg, layer_idx=2).to(BF16).eval()
+    with torch.no_grad():
+        attn.q_proj.weight.copy_(weights["q_proj"])
+        attn.k_proj.weight.copy_(weights["k_proj"])
+        attn.v_proj.weight.copy_(weights["v_proj"])
+        attn.out_proj.weight.copy_(weights["out_proj"])
+        attn.q_layernorm.weight.copy_(weights["q_gamma"])
+        attn.k_layernorm.weight.copy_(weights["k_gamma"])
+    rotary = hf.Lfm2RotaryEmbedding(cfg)
+    k_past, v_past = orc.past_cache(1000 + length, length)
+    x = orc.hidden_input(2000 + length)
+    cache = DynamicCache()
+    if length:
+        cache.update(k_past, v_past, 2)
+    else:
+        cache.update(k_past[:, :, :0], v_past[:, :, :0], 2)
+    seen = {}
+    hooks = [
+        attn.q_proj.register_forward_hook(lambda m, i, o: seen.__setitem__("q_raw", o)),
+        attn.k_proj.register_forward_hook(lambda m, i, o: seen.__setitem__("k_raw", o)),
+        attn.v_proj.register_forward_hook(lambda m, i, o: seen.__setitem__("v_raw", o)),
+        attn.q_layernorm.register_forward_hook(lambda m, i, o: seen.__setitem__("q_norm", o)),
+        attn.k_layernorm.register_forward_hook(lambda m, i, o: seen.__setitem__("k_norm", o)),
+        attn.out_proj.register_forward_hook(lambda m, i, o: seen.__setitem__("context", i[0])),
+    ]
+    with torch.no_grad():
+        pos = torch.tensor([[length]])
+        cos, sin = rotary(x, pos)
+        out, _ = attn(x, (cos, sin), None, past_key_values=cache)
+        q_rot, k_rot = hf.apply_rotary_pos_emb(seen["q_norm"].transpose(1, 2),
+                                               seen["k_norm"].transpose(1, 2), cos, sin)
+    for h in hooks:
+        h.remove()
+    layer = cache.layers[2]
+    return {
+        "x": orc.bits(x.reshape(-1)),
+        "q_raw": orc.bits(seen["q_raw"].reshape(-1)),
+        "k_raw": orc.bits(seen["k_raw"].reshape(-1)),
+        "v_raw": orc.bits(seen["v_raw"].reshape(-1)),
+        "q_norm": orc.bits(seen["q_norm"].reshape(16, 64)),
+        "k_norm": orc.bits(seen["k_norm"].reshape(8, 64)),
+        "cos": orc.bits(cos.reshape(64)),
+        "sin": orc.bits(sin.reshape(64)),
+        "q_rot": orc.bits(q_rot.reshape(16, 64)),
+        "k_rot": orc.bits(k_rot.reshape(8, 64)),
+        "k_appended": orc.bits(layer.keys[0, :, length]),
+        "v_appended": orc.bits(layer.values[0, :, length]),
+        "cache_len": np.int64(layer.keys.shape[2]),
+        "context": orc.bits(seen["context"].reshape(16, 64)),
+        "output": orc.bits(out.reshape(-1)),
+        "past_sha256": sha(k_past, v_past),
+        "x_sha256": sha(x),
+    }
+
+
+def main() -> None:
+    torch.manual_seed(0)
+    weights = orc.attention_weights(WEIGHT_SEED)
+    meta = {"transformers": transformers.__version__, "torch": torch.__version__,
+            "weights_sha256": sha(*[weights[k] for k in sorted(weights)])}
+    for length in CASES:
+        rec = {}
+        for impl in ("sdpa", "eager"):
+            r = run_case(length, impl, weights)
+            for k, v in r.items():
+                if impl == "sdpa" or k in ("context", "output"):
+                    rec[f"{k}_{impl}" if k in ("context", "output") else k] = v
+        np.savez_compressed(OUT / f"lfm2_attn_L{length}.npz", **rec, **meta, length=np.int64(length),
+                            weight_seed=np.int64(WEIGHT_SEED))
+    cfg = config("sdpa")
+    rotary = hf.Lfm2RotaryEmbedding(cfg)
+    with torch.no_grad():
+        pos = torch.tensor([ROPE_POSITIONS])
+        cos, sin = rotary(torch.zeros(1, dtype=BF16), pos)
+    np.savez_compressed(OUT / "lfm2_rope.npz", positions=np.array(ROPE_POSITIONS, dtype=np.int64),
+                        cos=orc.bits(cos[0]), sin=orc.bits(sin[0]), **meta)
+    print("wrote", sorted(p.name for p in OUT.glob("*.npz")))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,46 @@
+"""CPU checks of the C ABI: the in-tree library loads without a GPU and
+exports every entry point include/b2_decode_attn.h declares."""
+import ctypes
+import pathlib
+import re
+
+from conftest import ROOT, load_pkg
+
+HEADER = ROOT / "include" / "b2_decode_attn.h"
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\bint\s+(b2_\w+)\s*\(", text)))
+
+
+def test_header_declares_entry_points():
+    names = declared_functions()
+    assert {"b2_append_rope", "b2_decode_attn", "b2_combine", "b2_last_error", "b2_version"} <= set(names)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = load_pkg("_lib")
+    cdll = lib.load()
+    for name in declared_functions():
+        assert hasattr(cdll, name), name
+        assert name in lib.SIGNATURES, f"{name} has no ctypes signature"
+
+
+def test_version_and_error_text_without_gpu():
+    lib = load_pkg("_lib")
+    assert lib.load().b2_version() >= 100
+    # argument checks run on the host before any CUDA call
+    rc = lib.load().b2_decode_attn(None, None, None, 1, None, 1, None, 1, 1, 1,
+                                   ctypes.c_float(0.125), None, None, None, None)
+    assert rc == lib.B2_ERR_ARG
+    assert "null pointer" in lib.last_error()
+    rc = lib.load().b2_append_rope(None, 2048, None, None, ctypes.c_float(1e-5), None, None, 0, None,
+                                   None, 0, None, None, 0, None, 0, 7, None, None)
+    assert rc == lib.B2_OK   # batch 0 is a no-op
+
+
+def test_library_lives_in_tree():
+    lib = load_pkg("_lib")
+    assert pathlib.Path(lib.LIB_PATH).parent.name == "ryzenai-npu-lab_b200"

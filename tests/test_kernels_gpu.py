@@ -1,0 +1,197 @@
+"""GPU parity: libb2attn.so kernels against the CPU oracle (reference semantics).
+
+Tolerances: KV append bit-exact; attention context
+max-abs <= 2e-2 and relative L2 error <= 1e-2 against the reference's
+PyTorch BF16 path (sdpa), fp32 accumulation on the GPU.
+"""
+import numpy as np
+import pytest
+import torch
+
+from conftest import load_pkg
+from oracle import lfm2_attention as orc
+
+pytestmark = pytest.mark.gpu
+
+ATOL = 2e-2
+RTOL = 1e-2
+
+
+def _lib():
+    return load_pkg("_lib")
+
+
+def _attn():
+    return load_pkg("attention")
+
+
+def _cache_mod():
+    return load_pkg("paged_cache")
+
+
+def check_close(got: torch.Tensor, ref: torch.Tensor, what: str):
+    got = got.float().cpu()
+    ref = ref.float().cpu()
+    assert torch.isfinite(got).all(), f"{what}: non-finite output"
+    err = (got - ref).abs().max().item()
+    rel = ((got - ref).norm() / ref.norm().clamp_min(1e-30)).item()
+    assert err <= ATOL and rel <= RTOL, f"{what}: max-abs {err:.3e}, rel {rel:.3e}"
+
+
+def ulp_diff(a: torch.Tensor, b: torch.Tensor) -> np.ndarray:
+    """Distance in bf16 ulps between two bf16 tensors (sign-magnitude order)."""
+    def key(t):
+        u = orc.bits(t.cpu()).astype(np.int32)
+        return np.where(u & 0x8000, 0x8000 - (u & 0x7FFF), 0x8000 + u)
+    return np.abs(key(a) - key(b))
+
+
+def build_batch(lengths, dev, seed=0, capacity=None, fill=float("nan"), num_blocks=None):
+    """Paged cache holding seeded N(0,1) histories of the given lengths."""
+    cm = _cache_mod()
+    cap = capacity or (max(lengths) + 1)
+    nb = num_blocks or sum(cm.blocks_for(cap) for _ in lengths) + 3
+    cache = cm.PagedKVCache(nb, cap, device=dev, shuffle_seed=seed, fill=fill)
+    hist = []
+    for i, n in enumerate(lengths):
+        cache.add_sequence(n)
+        k, v = orc.past_cache(100 * seed + i, n)
+        cache.write_dense(0, i, k[0], v[0])
+        hist.append((k[0], v[0]))
+    return cache, hist
+
+
+def rand_qkv(batch, seed, scale=0.6):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(batch, 2048, generator=g) * scale).to(torch.bfloat16)
+
+
+def test_library_loaded_from_tree():
+    lib = _lib().load()
+    assert lib.b2_version() >= 100
+    assert str(_lib().LIB_PATH).endswith("ryzenai-npu-lab_b200/libb2attn.so")
+
+
+@pytest.mark.parametrize("lengths", [[0], [0, 1, 63, 64, 65, 127, 128, 1000]])
+def test_append_rope_bit_exact_given_normed(cuda, lengths):
+    """RoPE + append of already-normalised q/k: bit-exact vs the oracle."""
+    lib = _lib()
+    cache, _ = build_batch(lengths, cuda, seed=1)
+    b = len(lengths)
+    w = orc.attention_weights(0)
+    raw = rand_qkv(b, 11)
+    q_raw, k_raw, v = orc.split_qkv(raw)
+    qn = orc.rms_norm(q_raw, w["q_gamma"])
+    kn = orc.rms_norm(k_raw, w["k_gamma"])
+    qkv = torch.cat([qn.reshape(b, -1), kn.reshape(b, -1), v.reshape(b, -1)], dim=1)
+    cos, sin = orc.rope_cos_sin(lengths)
+    q_ref, k_ref = orc.norm_rope_qk(qn, kn, None, None, cos, sin, norm=False)
+    rc, rs = load_pkg("rope").rope_table(2048, device=cuda)
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    q_out = torch.empty(b, 16, 64, dtype=torch.bfloat16, device=cuda)
+    kp, vp = cache.pool(0)
+    _attn().append_rope(qkv.to(cuda), torch.tensor(lengths, dtype=torch.int32, device=cuda), q_out=q_out,
+                        dev_err=err, mode=lib.B2_ROPE_QK | lib.B2_STORE_KV, cos=rc, sin=rs,
+                        k_pool=kp, v_pool=vp, block_tables=cache.block_tables())
+    torch.cuda.synchronize()
+    assert err.item() == 0
+    assert torch.equal(q_out.cpu(), q_ref)
+    for i, n in enumerate(lengths):
+        kd, vd = cache.read_dense(0, i, n + 1)
+        assert torch.equal(kd[:, n].cpu(), k_ref[i]), f"k row {n} of seq {i}"
+        assert torch.equal(vd[:, n].cpu(), v[i]), f"v row {n} of seq {i}"
+
+
+def test_append_with_norm_matches_oracle(cuda):
+    """RMSNorm in the kernel: reduction order may differ from torch's CPU sum,
+    so each element is within 1 bf16 ulp and >= 99% are bit-identical."""
+    lib = _lib()
+    lengths = list(range(0, 640, 5))
+    cache, _ = build_batch(lengths, cuda, seed=2)
+    b = len(lengths)
+    w = orc.attention_weights(0)
+    raw = rand_qkv(b, 12)
+    q_raw, k_raw, v = orc.split_qkv(raw)
+    cos, sin = orc.rope_cos_sin(lengths)
+    q_ref, k_ref = orc.norm_rope_qk(q_raw, k_raw, w["q_gamma"], w["k_gamma"], cos, sin)
+    rc, rs = load_pkg("rope").rope_table(1024, device=cuda)
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    q_out = torch.empty(b, 16, 64, dtype=torch.bfloat16, device=cuda)
+    kp, vp = cache.pool(0)
+    _attn().append_rope(raw.to(cuda), torch.tensor(lengths, dtype=torch.int32, device=cuda), q_out=q_out,
+                        dev_err=err, gamma_q=w["q_gamma"].to(cuda), gamma_k=w["k_gamma"].to(cuda),
+                        cos=rc, sin=rs, k_pool=kp, v_pool=vp, block_tables=cache.block_tables())
+    torch.cuda.synchronize()
+    assert err.item() == 0
+    k_got = torch.stack([cache.read_dense(0, i, n + 1)[0][:, n] for i, n in enumerate(lengths)])
+    v_got = torch.stack([cache.read_dense(0, i, n + 1)[1][:, n] for i, n in enumerate(lengths)])
+    assert torch.equal(v_got.cpu(), v)
+    for got, ref, name in [(q_out, q_ref, "q"), (k_got, k_ref, "k")]:
+        d = ulp_diff(got, ref)
+        assert d.max() <= 1, f"{name}: {d.max()} ulps"
+        assert (d == 0).mean() >= 0.99, f"{name}: exact fraction {(d == 0).mean():.4f}"
+
+
+@pytest.mark.parametrize("bps", [1, 2, 3, 16])
+def test_decode_ragged_vs_oracle(cuda, bps):
+    lengths = [1, 2, 63, 64, 65, 127, 128, 129, 1000, 4097]
+    cache, hist = build_batch([n - 1 for n in lengths], cuda, seed=3)
+    b = len(lengths)
+    w = orc.attention_weights(0)
+    raw = rand_qkv(b, 13)
+    runner = _attn().PagedDecodeAttention(cache, w["q_gamma"], w["k_gamma"], b, 8192, blocks_per_split=bps)
+    past = torch.tensor([n - 1 for n in lengths], dtype=torch.int32, device=cuda)
+    out = runner.step(0, raw.to(cuda), past, past + 1, cache.block_tables())
+    torch.cuda.synchronize()
+    runner.check()
+    for i, n in enumerate(lengths):
+        ctx, _, _, _ = orc.decode_step(raw[i], hist[i][0], hist[i][1], n - 1, w["q_gamma"], w["k_gamma"])
+        check_close(out[i], ctx, f"seq {i} len {n} bps {bps}")
+
+
+def test_bad_block_is_flagged_not_faulted(cuda):
+    lengths = [100, 200]
+    cache, _ = build_batch(lengths, cuda, seed=4)
+    w = orc.attention_weights(0)
+    runner = _attn().PagedDecodeAttention(cache, w["q_gamma"], w["k_gamma"], 2, 1024, blocks_per_split=2)
+    tables = cache.block_tables()
+    tables[1, 1] = cache.num_blocks + 5   # outside the pool
+    past = torch.tensor(lengths, dtype=torch.int32, device=cuda)
+    runner.step(0, rand_qkv(2, 14).to(cuda), past, past + 1, tables)
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError, match="outside the pool"):
+        runner.check()
+    # the context is still usable afterwards
+    tables = cache.block_tables()
+    runner.step(0, rand_qkv(2, 14).to(cuda), past, past + 1, tables)
+    torch.cuda.synchronize()
+    runner.check()
+
+
+def test_length_beyond_table_is_flagged(cuda):
+    cache, _ = build_batch([10], cuda, seed=5, capacity=64)
+    w = orc.attention_weights(0)
+    runner = _attn().PagedDecodeAttention(cache, w["q_gamma"], w["k_gamma"], 1, 1024, blocks_per_split=1)
+    past = torch.tensor([64], dtype=torch.int32, device=cuda)   # slot 64 is past the 1-block table
+    runner.step(0, rand_qkv(1, 15).to(cuda), past, past + 1, cache.block_tables())
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError, match="outside the block table"):
+        runner.check()
+
+
+def test_host_rejects_bad_arguments(cuda):
+    attn = _attn()
+    lib = _lib()
+    cache, _ = build_batch([10], cuda, seed=6)
+    kp, vp = cache.pool(0)
+    q = torch.zeros(1, 16, 64, dtype=torch.bfloat16, device=cuda)
+    ml = torch.empty(1, 1, 16, 2, device=cuda)
+    po = torch.empty(1, 1, 16, 64, device=cuda)
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    seq = torch.tensor([11], dtype=torch.int32, device=cuda)
+    with pytest.raises(ValueError):
+        attn.decode_attn(q.float(), kp, vp, cache.block_tables(), seq, blocks_per_split=1,
+                         part_ml=ml, part_o=po, dev_err=err)
+    with pytest.raises(lib.B2Error):
+        attn.decode_attn(q, kp, vp, cache.block_tables(), seq, blocks_per_split=1,
+                         part_ml=ml, part_o=po, dev_err=err, scale=-1.0)
