@@ -1,0 +1,416 @@
+"""Benchmark of the LFM2.5 decode-attention hot path on B200.
+
+    python bench.py --gpus N --steps K --warmup W [--impl b200|reference]
+
+Workload (batched paged decode): per GPU, 64 sequences
+with cached lengths uniform in [128, 8192] (seeded per rank), K/V ~ N(0, 1)
+bf16 in a pool of 64-token blocks handed out in shuffled order, 16 q heads /
+8 KV heads / head_dim 64.  One step = one decode token per sequence through
+one attention layer: fused q/k RMSNorm + RoPE + KV append, split-KV
+flash-decode, combine.  Sequences are sharded across GPUs with no collective
+(weak scaling: every rank holds its own 64 sequences); the step time is the
+max over ranks.  The K/V pool (~0.55 GB per GPU) is larger than L2 (126 MB),
+so no L2 flush is needed between steps.
+
+The timed region replays a CUDA graph of exactly K steps with inputs already
+in HBM; `e2e` times the same steps through the public API
+(PagedDecodeAttention.step) with the per-step inputs copied from pinned host
+memory and the context copied back inside the timed region.
+
+`--impl reference` times the reference's CPU path (the oracle's restatement
+of transformers' Lfm2Attention + DynamicCache in BF16) on this host's cores,
+on bounded samples of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import math
+import os
+import pathlib
+import statistics
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+PKG = "ryzenai-npu-lab_b200"
+METRIC = "decode-attn tokens/s & HBM GB/s (% of 8 TB/s) vs context at 1/2/4/8 B200"
+HQ, HKV, D, BLOCK = 16, 8, 64, 64
+KV_BYTES_PER_TOKEN = 2 * HKV * D * 2          # K + V, bf16: 2048 B
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    p = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=400)
+    p.add_argument("--warmup", type=int, default=10)
+    p.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    p.add_argument("--batch", type=int, default=64, help="sequences per GPU")
+    p.add_argument("--min-len", type=int, default=128)
+    p.add_argument("--max-len", type=int, default=8192)
+    p.add_argument("--bps", type=int, default=0, help="blocks per split (0 = heuristic)")
+    p.add_argument("--seed", type=int, default=3)
+    p.add_argument("--e2e-steps", type=int, default=100)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--cpu-seconds", type=float, default=12.0, help="bounded CPU baseline sample")
+    return p.parse_args()
+
+
+# ----------------------------------------------------------------- helpers
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def measured_hbm_peak():
+    path = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(path.read_text())["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profiled_traffic_per_kv_token():
+    """DRAM bytes per cached token of the decode kernel from the committed ncu
+    summary (profiles/paged_decode_kernel_c3.txt, line 'traffic_bytes_per_kv_token: X')."""
+    path = ROOT / "profiles" / "paged_decode_kernel_c3.txt"
+    try:
+        for line in path.read_text().splitlines():
+            if line.startswith("traffic_bytes_per_kv_token:"):
+                return float(line.split(":")[1])
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while running."""
+
+    REASONS = {
+        "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4,
+        "hw_slowdown": 0x8, "sync_boost": 0x10, "sw_thermal_slowdown": 0x20,
+        "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80,
+    }
+
+    def __init__(self, index: int, period: float = 0.002):
+        self.samples, self.reasons = [], 0
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._period = period
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nvml = None
+        self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self._nvml.nvmlDeviceGetClockInfo(self._h, self._nvml.NVML_CLOCK_SM))
+                self.reasons |= self._nvml.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+            except Exception:
+                pass
+            time.sleep(self._period)
+
+    def __enter__(self):
+        if self._nvml is not None:
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._nvml is not None:
+            self._t.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"], "samples": 0}
+        names = [n for n, bit in self.REASONS.items() if self.reasons & bit and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": names, "samples": len(self.samples)}
+
+
+# ----------------------------------------------------------------- workload
+
+def seq_lengths(args, rank: int) -> list[int]:
+    g = torch.Generator().manual_seed(args.seed * 1000 + rank)
+    return torch.randint(args.min_len, args.max_len + 1, (args.batch,), generator=g).tolist()
+
+
+def build_workload(args, rank: int, dev: torch.device):
+    attn = importlib.import_module(PKG + ".attention")
+    pc = importlib.import_module(PKG + ".paged_cache")
+    lengths = seq_lengths(args, rank)
+    caps = [n + 1 for n in lengths]
+    num_blocks = sum(pc.blocks_for(c) for c in caps)
+    cache = pc.PagedKVCache(num_blocks, max(caps), device=dev, shuffle_seed=args.seed * 1000 + rank + 17)
+    for n, c in zip(lengths, caps):
+        cache.add_sequence(n, capacity=c)
+    gen = torch.Generator(device=dev).manual_seed(args.seed * 1000 + rank + 29)
+    cache.k.normal_(generator=gen)
+    cache.v.normal_(generator=gen)
+    gg = torch.Generator().manual_seed(args.seed * 1000 + rank + 31)
+    gamma_q = (1.0 + 0.1 * torch.randn(D, generator=gg)).to(torch.bfloat16)
+    gamma_k = (1.0 + 0.1 * torch.randn(D, generator=gg)).to(torch.bfloat16)
+    work_blocks = sum(pc.blocks_for(c) for c in caps)
+    runner = attn.PagedDecodeAttention(cache, gamma_q, gamma_k, args.batch, args.max_len + 2,
+                                       blocks_per_split=args.bps or None, work_blocks=work_blocks)
+    ring = 8
+    qkv = (torch.randn(ring, args.batch, 2048, generator=gen, device=dev) * 0.6).to(torch.bfloat16)
+    past = torch.tensor(lengths, dtype=torch.int32, device=dev)
+    return {"lengths": lengths, "cache": cache, "runner": runner, "qkv": qkv, "past": past,
+            "seq": past + 1, "tables": cache.block_tables(), "ring": ring}
+
+
+def step_bytes(lengths) -> tuple[int, int]:
+    """Algorithmic HBM bytes: (whole step, decode kernel) for one step."""
+    nblk = [math.ceil((n + 1) / BLOCK) for n in lengths]
+    step = sum(KV_BYTES_PER_TOKEN * (n + 4) + 4 * b for n, b in zip(lengths, nblk))
+    decode = sum(KV_BYTES_PER_TOKEN * (n + 1) + HQ * D * 2 + 4 * b for n, b in zip(lengths, nblk))
+    return step, decode
+
+
+# ----------------------------------------------------------------- CPU reference path
+
+def cpu_reference_rate(lengths, seconds: float, seed: int = 0):
+    """tokens/s of the reference CPU path (oracle restatement of transformers'
+    Lfm2Attention decode + DynamicCache.update) over sequences of the given
+    lengths, one sequence at a time (the reference decode loop is batch-1),
+    with all host threads.  Runs until `seconds` have elapsed (at least one
+    pass over 4 sequences)."""
+    from oracle import lfm2_attention as orc
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    w = orc.attention_weights(seed)
+    g = torch.Generator().manual_seed(seed + 1)
+    sample = lengths[: max(4, min(len(lengths), 16))]
+    hist = [(torch.randn(HKV, n, D, generator=g).to(torch.bfloat16),
+             torch.randn(HKV, n, D, generator=g).to(torch.bfloat16)) for n in sample]
+    qkv = (torch.randn(len(sample), 2048, generator=g) * 0.6).to(torch.bfloat16)
+    cos, sin = orc.rope_cos_sin(sample)
+    # warm-up
+    orc.decode_step(qkv[0], hist[0][0], hist[0][1], sample[0], w["q_gamma"], w["k_gamma"],
+                    cos=cos[0:1], sin=sin[0:1])
+    done, t0 = 0, time.perf_counter()
+    while True:
+        for i, n in enumerate(sample):
+            orc.decode_step(qkv[i], hist[i][0], hist[i][1], n, w["q_gamma"], w["k_gamma"],
+                            cos=cos[i:i + 1], sin=sin[i:i + 1])
+            done += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return done / el, {"sequences": len(sample), "seq_steps": done, "seconds": round(el, 2),
+                       "mean_context": round(sum(sample) / len(sample), 1)}
+
+
+def run_reference(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return
+    lengths = seq_lengths(args, 0)
+    per_step = max(1.0, args.cpu_seconds / max(1, args.steps))
+    for _ in range(args.warmup):
+        cpu_reference_rate(lengths[:4], 0.0)
+    rates, info = [], None
+    for _ in range(args.steps):
+        r, info = cpu_reference_rate(lengths, per_step)
+        rates.append(r)
+    value = statistics.median(rates)
+    cores = torch.get_num_threads()
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * args.batch / value, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": config_block(args, lengths, None),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"median of {args.steps} samples, each {info}"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def config_block(args, lengths, bps):
+    return {
+        "workload": "C3 batched paged decode: 64 sequences per GPU, cached length ~U[128, 8192], "
+                    "64-token bf16 KV blocks in shuffled order, 16q/8kv heads x 64; one step = "
+                    "one decode token per sequence through one attention layer "
+                    "(q/k norm + RoPE + KV append, split-KV flash-decode, combine)",
+        "batch_per_gpu": args.batch, "global_batch": args.batch * args.gpus,
+        "context_min": args.min_len, "context_max": args.max_len,
+        "context_mean": round(sum(lengths) / len(lengths), 1),
+        "block_tokens": BLOCK, "blocks_per_split": bps, "parallelism": f"seq-shard x{args.gpus}",
+        "l2": "inputs larger than L2 (KV pool > 126 MB per GPU), no flush",
+    }
+
+
+# ----------------------------------------------------------------- B200 path
+
+def run_b200(args):
+    world, rank, local = dist_env()
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py: no CUDA device")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+        pg = torch.distributed.group.WORLD
+    wl = build_workload(args, rank, dev)
+    runner = wl["runner"]
+    K, W, ring = args.steps, args.warmup, wl["ring"]
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.synchronize()
+
+    def one_step(j, ev=None):
+        runner.step(0, wl["qkv"][j % ring], wl["past"], wl["seq"], wl["tables"])
+
+    # warm-up (untimed) also sets up the kernels' attributes before capture
+    with torch.cuda.stream(stream):
+        for j in range(max(W, 1)):
+            one_step(j)
+    stream.synchronize()
+    runner.check()
+
+    # CUDA graph of exactly K steps; external events bracket every decode launch
+    attn = importlib.import_module(PKG + ".attention")
+    ev0 = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(K)]
+    ev1 = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(K)]
+    graph = torch.cuda.CUDAGraph()
+    kp, vp = runner.cache.pool(0)
+    with torch.cuda.graph(graph, stream=stream):
+        for j in range(K):
+            b = args.batch
+            q = runner.q[:b]
+            attn.append_rope(wl["qkv"][j % ring], wl["past"], q_out=q, dev_err=runner.dev_err,
+                             gamma_q=runner.gamma_q, gamma_k=runner.gamma_k, cos=runner.cos, sin=runner.sin,
+                             k_pool=kp, v_pool=vp, block_tables=wl["tables"])
+            ev0[j].record()
+            splits = attn.decode_attn(q, kp, vp, wl["tables"], wl["seq"],
+                                      blocks_per_split=runner.blocks_per_split, part_ml=runner.part_ml,
+                                      part_o=runner.part_o, dev_err=runner.dev_err)
+            ev1[j].record()
+            attn.combine(runner.part_ml, runner.part_o, splits, b, seq_lens=wl["seq"],
+                         blocks_per_split=runner.blocks_per_split, out=runner.out[:b])
+    graph.replay()   # one untimed replay (graph upload)
+    torch.cuda.synchronize()
+    runner.check()
+
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    if pg is not None:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        with torch.cuda.stream(stream):
+            t_start.record()
+            graph.replay()
+            t_end.record()
+        torch.cuda.synchronize()
+    if pg is not None:
+        torch.distributed.barrier()
+    ms = t_start.elapsed_time(t_end)
+    decode_ms = sum(a.elapsed_time(b) for a, b in zip(ev0, ev1)) / K
+    runner.check()
+
+    # end-to-end through the public API: pinned host inputs in, context out, per step
+    e2e_steps = min(args.e2e_steps, K)
+    qkv_host = wl["qkv"].cpu().pin_memory()
+    lens_host = torch.stack([wl["past"].cpu(), wl["seq"].cpu()]).pin_memory()
+    out_host = torch.empty(e2e_steps, args.batch, HQ, D, dtype=torch.bfloat16).pin_memory()
+    qkv_dev = torch.empty_like(wl["qkv"][0])
+    lens_dev = torch.empty(2, args.batch, dtype=torch.int32, device=dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        for j in range(3):
+            qkv_dev.copy_(qkv_host[j % ring], non_blocking=True)
+            runner.step(0, qkv_dev, wl["past"], wl["seq"], wl["tables"])
+    torch.cuda.synchronize()
+    if pg is not None:
+        torch.distributed.barrier()
+    with torch.cuda.stream(stream):
+        e0.record()
+        for j in range(e2e_steps):
+            qkv_dev.copy_(qkv_host[j % ring], non_blocking=True)
+            lens_dev.copy_(lens_host, non_blocking=True)
+            o = runner.step(0, qkv_dev, lens_dev[0], lens_dev[1], wl["tables"])
+            out_host[j].copy_(o, non_blocking=True)
+        e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    runner.check()
+
+    times = torch.tensor([ms, decode_ms, e2e_ms], dtype=torch.float64, device=dev)
+    if pg is not None:
+        torch.distributed.all_reduce(times, op=torch.distributed.ReduceOp.MAX)
+    ms, decode_ms, e2e_ms = times.tolist()
+
+    lengths = wl["lengths"]
+    sbytes, dbytes = step_bytes(lengths)
+    peak, peak_kind = measured_hbm_peak()
+    ms_step = ms / K
+    tokens = args.batch * world
+    value = tokens * K / (ms / 1e3)
+    achieved = dbytes / (decode_ms / 1e3) / 1e9
+    tpt = profiled_traffic_per_kv_token()
+    kv_tokens = sum(n + 1 for n in lengths)
+    step_gbs = sbytes / (ms_step / 1e3) / 1e9
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
+        "warmup": W, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": config_block(args, lengths, runner.blocks_per_split),
+        "hbm_gbs_per_gpu": step_gbs, "hbm_pct_of_8tbs": 100.0 * step_gbs / 8000.0,
+        "roofline": {"bound": "hbm", "kernel": "paged_decode_kernel", "achieved": achieved,
+                     "peak": peak, "peak_source": peak_kind, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": None if tpt is None else tpt * kv_tokens,
+                     "algorithmic_bytes": dbytes, "avg_launch_ms": decode_ms},
+        "clocks": clocks.summary(),
+        "e2e": {"value": tokens * e2e_steps / (e2e_ms / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": args.batch * (2048 * 2 + 2 * 4),
+                "d2h_bytes_per_step": args.batch * HQ * D * 2, "steps": e2e_steps},
+        "gpu_launches": 3 * K,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rate, info = cpu_reference_rate(lengths, args.cpu_seconds)
+        line["cpu_baseline"] = {"value": rate, "unit": "tokens/s", "cores": torch.get_num_threads(),
+                                "kind": "port", "sample": f"reference CPU path (transformers Lfm2Attention "
+                                f"restated, DynamicCache cat + sdpa), batch-1 loop over {info}"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    del graph
+    if pg is not None:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+def main():
+    args = parse()
+    world, _, _ = dist_env()
+    if world != args.gpus and not (world == 1 and args.gpus == 1):
+        if world == 1 and args.gpus > 1:
+            raise SystemExit("--gpus N > 1 must be launched with torchrun (one process per GPU)")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()
