@@ -222,7 +222,7 @@ def run_reference(args):
     if rank != 0:
         return
     lengths = seq_lengths(args, 0)
-    per_step = max(1.0, args.cpu_seconds / max(1, args.steps))
+    per_step = max(0.02, min(1.0, 60.0 / max(1, args.steps)))   # whole run ~1 min
     for _ in range(args.warmup):
         cpu_reference_rate(lengths[:4], 0.0)
     rates, info = [], None
