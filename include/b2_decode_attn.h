@@ -153,6 +153,38 @@ int b2_combine(const float *part_ml, const float *part_o, int32_t num_parts,
                int32_t batch, uint16_t *out, float *state_ml, float *state_o,
                void *stream);
 
+/*
+ * Allocation-free decode: b2_decode_attn followed by b2_combine, with the
+ * partial softmax states kept in a static device array inside this library
+ * instead of caller-provided part_ml / part_o buffers.  It has no counterpart
+ * in the reference.
+ *
+ * It is meant for callers that hold device pointers but cannot allocate
+ * device memory of their own: a host written in another language that binds
+ * only this C ABI and has no CUDA allocator, or an embedder whose device
+ * memory is already committed to another framework's pool.
+ *
+ * Limit: batch * ceil(max_blocks_per_seq / blocks_per_split) must not exceed
+ * B2_NOALLOC_MAX_PARTS; larger calls return B2_ERR_ARG without launching.
+ * The array (B2_NOALLOC_MAX_PARTS x 16 heads x 66 floats = 4.125 MiB) is held
+ * on every GPU that loads the library until the process exits.  The first
+ * call on a device looks up that device's copy of the array
+ * (cudaGetSymbolAddress) with the device current; make that first call before
+ * any stream capture.  All calls on a device share the one array and it keeps
+ * the previous call's contents (every entry this call reads is written by
+ * this call first): calls that can overlap on the GPU, e.g. on two streams
+ * without ordering between them, race on it and must be serialised by the
+ * caller.  Nothing is allocated or freed, by this library or any other.
+ */
+#define B2_NOALLOC_MAX_PARTS 1024
+int b2_decode_attn_noalloc(const uint16_t *q,
+                           const uint16_t *k_pool, const uint16_t *v_pool,
+                           int32_t num_blocks,
+                           const int32_t *block_tables, int32_t max_blocks_per_seq,
+                           const int32_t *seq_lens, int32_t batch,
+                           int32_t blocks_per_split, float scale,
+                           uint16_t *out, int32_t *dev_err, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

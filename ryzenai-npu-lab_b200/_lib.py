@@ -25,6 +25,8 @@ B2_NORM_QK = 1
 B2_ROPE_QK = 2
 B2_STORE_KV = 4
 
+B2_NOALLOC_MAX_PARTS = 1024   # batch * num_splits limit of b2_decode_attn_noalloc
+
 DEV_ERR_NAMES = {
     B2_DEV_BAD_BLOCK: "block table entry outside the pool",
     B2_DEV_BAD_LENGTH: "length or position outside the block table",
@@ -58,6 +60,13 @@ SIGNATURES = {
         _i32, _i32, _f32,    # blocks_per_split, num_splits, scale
         _p, _p,              # part_ml, part_o
         _p, _p,              # dev_err, stream
+    ]),
+    "b2_decode_attn_noalloc": (ctypes.c_int, [
+        _p, _p, _p, _i32,    # q, k_pool, v_pool, num_blocks
+        _p, _i32,            # block_tables, max_blocks_per_seq
+        _p, _i32,            # seq_lens, batch
+        _i32, _f32,          # blocks_per_split, scale
+        _p, _p, _p,          # out, dev_err, stream
     ]),
     "b2_combine": (ctypes.c_int, [
         _p, _p, _i32,        # part_ml, part_o, num_parts

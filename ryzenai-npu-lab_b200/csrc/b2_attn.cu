@@ -19,6 +19,8 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <mutex>
+
 #include "b2_decode_attn.h"
 
 namespace {
@@ -685,4 +687,88 @@ extern "C" int b2_combine(const float *part_ml, const float *part_o, int32_t num
   CombineArgs a{part_ml, part_o, num_parts, seq_lens, blocks_per_split, out, state_ml, state_o};
   combine_kernel<<<batch, kHq * kDim, 0, static_cast<cudaStream_t>(stream)>>>(a);
   return launch_status("combine_kernel");
+}
+
+// ------------------------------------------------------------------ allocation-free decode
+
+namespace {
+
+constexpr int kNoAllocMlFloats = B2_NOALLOC_MAX_PARTS * kHq * 2;
+constexpr int kNoAllocOFloats = B2_NOALLOC_MAX_PARTS * kHq * kDim;
+
+// Partial states of b2_decode_attn_noalloc: [part_ml | part_o] for up to
+// B2_NOALLOC_MAX_PARTS (sequence, split) pairs.  One copy per device.
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocMlFloats + kNoAllocOFloats];
+
+std::mutex g_noalloc_mu;
+float *g_noalloc_ptr[128] = {};
+
+// Device address of this device's scratch array.  Host code may not use the
+// symbol itself (that names a host-side stand-in), so the address is looked
+// up once per device with the device current.
+float *noalloc_scratch(int *rc) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) {
+    *rc = fail(B2_ERR_CUDA, "b2_decode_attn_noalloc: no current CUDA device");
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void *p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p) {
+      *rc = fail(B2_ERR_CUDA, "b2_decode_attn_noalloc: cudaGetSymbolAddress failed: %s",
+                 cudaGetErrorString(e));
+      return nullptr;
+    }
+    g_noalloc_ptr[dev] = static_cast<float *>(p);
+  }
+  *rc = B2_OK;
+  return g_noalloc_ptr[dev];
+}
+
+}  // namespace
+
+extern "C" int b2_decode_attn_noalloc(const uint16_t *q, const uint16_t *k_pool, const uint16_t *v_pool,
+                                      int32_t num_blocks, const int32_t *block_tables,
+                                      int32_t max_blocks_per_seq, const int32_t *seq_lens, int32_t batch,
+                                      int32_t blocks_per_split, float scale, uint16_t *out,
+                                      int32_t *dev_err, void *stream) {
+  if (batch < 0) return fail(B2_ERR_ARG, "batch must be >= 0 (got %d)", batch);
+  if (batch == 0) return ok();
+  if (!q || !k_pool || !v_pool || !block_tables || !seq_lens || !out || !dev_err)
+    return fail(B2_ERR_ARG, "null pointer argument");
+  if (max_blocks_per_seq <= 0 || blocks_per_split <= 0)
+    return fail(B2_ERR_ARG, "max_blocks_per_seq and blocks_per_split must be positive");
+  const int64_t splits = (static_cast<int64_t>(max_blocks_per_seq) + blocks_per_split - 1) / blocks_per_split;
+  if (splits * batch > B2_NOALLOC_MAX_PARTS)
+    return fail(B2_ERR_ARG,
+                "b2_decode_attn_noalloc: batch * ceil(max_blocks_per_seq / blocks_per_split) = %lld exceeds "
+                "the static scratch limit B2_NOALLOC_MAX_PARTS = %d; raise blocks_per_split or split the batch",
+                (long long)(splits * batch), B2_NOALLOC_MAX_PARTS);
+  if (num_blocks <= 0 || static_cast<int64_t>(num_blocks) * kHkv * kBlock >= (int64_t(1) << 31))
+    return fail(B2_ERR_ARG, "num_blocks must be in [1, 2^22) (got %d)", num_blocks);
+  if (!aligned16(q) || !aligned16(k_pool) || !aligned16(v_pool))
+    return fail(B2_ERR_ARG, "q and the pools must be 16-byte aligned");
+  if (!(scale > 0.f)) return fail(B2_ERR_ARG, "scale must be positive");
+  int rc = B2_OK;
+  float *scratch = noalloc_scratch(&rc);
+  if (!scratch) return rc;
+  float *part_ml = scratch;
+  float *part_o = scratch + kNoAllocMlFloats;
+  CUtensorMap mk, mv;
+  rc = make_pool_map(&mk, k_pool, num_blocks);
+  if (rc) return rc;
+  rc = make_pool_map(&mv, v_pool, num_blocks);
+  if (rc) return rc;
+  if (!decode_smem_ready()) return fail(B2_ERR_CUDA, "cannot set the decode kernel's shared memory size");
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  DecodeArgs a{q, block_tables, max_blocks_per_seq, seq_lens, num_blocks, blocks_per_split,
+               static_cast<int>(splits), scale * 1.4426950408889634f, part_ml, part_o, dev_err};
+  paged_decode_kernel<<<dim3(static_cast<unsigned>(splits), kHkv, batch), kDecodeThreads, kDecodeSmem, s>>>(mk, mv, a);
+  rc = launch_status("paged_decode_kernel (noalloc)");
+  if (rc) return rc;
+  CombineArgs c{part_ml, part_o, static_cast<int>(splits), seq_lens, blocks_per_split, out, nullptr, nullptr};
+  combine_kernel<<<batch, kHq * kDim, 0, s>>>(c);
+  return launch_status("combine_kernel (noalloc)");
 }
