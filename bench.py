@@ -59,6 +59,9 @@ def parse():
     p.add_argument("--e2e-steps", type=int, default=100)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="bounded CPU baseline sample")
+    p.add_argument("--three-kernels", action="store_true",
+                   help="run append, decode and combine as three launches instead of the fused kernel")
+    p.add_argument("--max-ctas", type=int, default=0, help="cap on the fused kernel's persistent grid")
     return p.parse_args()
 
 
@@ -79,10 +82,10 @@ def measured_hbm_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def profiled_traffic_per_kv_token():
-    """DRAM bytes per cached token of the decode kernel from the committed ncu
-    summary (profiles/paged_decode_kernel_c3.txt, line 'traffic_bytes_per_kv_token: X')."""
-    path = ROOT / "profiles" / "paged_decode_kernel_c3.txt"
+def profiled_traffic_per_kv_token(kernel: str):
+    """DRAM bytes per cached token of `kernel` from its committed ncu summary
+    (profiles/<kernel>_c3.txt, line 'traffic_bytes_per_kv_token: X')."""
+    path = ROOT / "profiles" / f"{kernel}_c3.txt"
     try:
         for line in path.read_text().splitlines():
             if line.startswith("traffic_bytes_per_kv_token:"):
@@ -167,7 +170,8 @@ def build_workload(args, rank: int, dev: torch.device):
     gamma_k = (1.0 + 0.1 * torch.randn(D, generator=gg)).to(torch.bfloat16)
     work_blocks = sum(pc.blocks_for(c) for c in caps)
     runner = attn.PagedDecodeAttention(cache, gamma_q, gamma_k, args.batch, args.max_len + 2,
-                                       blocks_per_split=args.bps or None, work_blocks=work_blocks)
+                                       blocks_per_split=args.bps or None, work_blocks=work_blocks,
+                                       fused=not args.three_kernels, max_ctas=args.max_ctas)
     ring = 8
     qkv = (torch.randn(ring, args.batch, 2048, generator=gen, device=dev) * 0.6).to(torch.bfloat16)
     past = torch.tensor(lengths, dtype=torch.int32, device=dev)
@@ -287,15 +291,22 @@ def run_b200(args):
     stream.synchronize()
     runner.check()
 
-    # CUDA graph of exactly K steps; external events bracket every decode launch
+    # CUDA graph of exactly K steps; external events bracket the dominant
+    # kernel of every step (the fused kernel is the whole step; with three
+    # kernels, the decode launch)
     attn = importlib.import_module(PKG + ".attention")
     ev0 = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(K)]
     ev1 = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(K)]
     graph = torch.cuda.CUDAGraph()
     kp, vp = runner.cache.pool(0)
+    b = args.batch
     with torch.cuda.graph(graph, stream=stream):
         for j in range(K):
-            b = args.batch
+            if runner.fused:
+                ev0[j].record()
+                runner.step(0, wl["qkv"][j % ring], wl["past"], wl["seq"], wl["tables"])
+                ev1[j].record()
+                continue
             q = runner.q[:b]
             attn.append_rope(wl["qkv"][j % ring], wl["past"], q_out=q, dev_err=runner.dev_err,
                              gamma_q=runner.gamma_q, gamma_k=runner.gamma_k, cos=runner.cos, sin=runner.sin,
@@ -363,12 +374,15 @@ def run_b200(args):
 
     lengths = wl["lengths"]
     sbytes, dbytes = step_bytes(lengths)
+    kernel = "paged_decode_kernel"
+    if runner.fused:
+        dbytes, kernel = sbytes, "decode_step_kernel"
     peak, peak_kind = measured_hbm_peak()
     ms_step = ms / K
     tokens = args.batch * world
     value = tokens * K / (ms / 1e3)
     achieved = dbytes / (decode_ms / 1e3) / 1e9
-    tpt = profiled_traffic_per_kv_token()
+    tpt = profiled_traffic_per_kv_token(kernel)
     kv_tokens = sum(n + 1 for n in lengths)
     step_gbs = sbytes / (ms_step / 1e3) / 1e9
     line = {
@@ -377,7 +391,7 @@ def run_b200(args):
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": config_block(args, lengths, runner.blocks_per_split),
         "hbm_gbs_per_gpu": step_gbs, "hbm_pct_of_8tbs": 100.0 * step_gbs / 8000.0,
-        "roofline": {"bound": "hbm", "kernel": "paged_decode_kernel", "achieved": achieved,
+        "roofline": {"bound": "hbm", "kernel": kernel, "achieved": achieved,
                      "peak": peak, "peak_source": peak_kind, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": None if tpt is None else tpt * kv_tokens,
                      "algorithmic_bytes": dbytes, "avg_launch_ms": decode_ms},
@@ -385,7 +399,7 @@ def run_b200(args):
         "e2e": {"value": tokens * e2e_steps / (e2e_ms / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": args.batch * (2048 * 2 + 2 * 4),
                 "d2h_bytes_per_step": args.batch * HQ * D * 2, "steps": e2e_steps},
-        "gpu_launches": 3 * K,
+        "gpu_launches": (1 if runner.fused else 3) * K,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, info = cpu_reference_rate(lengths, args.cpu_seconds)

@@ -154,6 +154,42 @@ int b2_combine(const float *part_ml, const float *part_o, int32_t num_parts,
                void *stream);
 
 /*
+ * One fused decode step in a single persistent launch: q/k RMSNorm + RoPE,
+ * append of the new k/v into slot past_lens[b] of the pool, split-KV
+ * attention over past_lens[b] + 1 tokens and the merge of the splits, for
+ * the whole batch.  Same results as b2_append_rope + b2_decode_attn +
+ * b2_combine (the same device arithmetic); replaces, together, the
+ * reference's per-layer chain norm_rope -> append -> context
+ * (experiments/kernels/x8/x8_core.cc:89-121 attn_prep/attn_block/attn_final,
+ * experiments/lfm25_attention_context_cache_kernel.py:54-71).
+ *
+ * A persistent grid (3 CTAs per SM, or max_ctas if smaller and > 0) takes
+ * work items (sequence, split, kv head) from a counter; a sequence that fits
+ * one split is written to out directly, the others leave partial states in
+ * part_ml/part_o that a second, small kernel (launched by this call as a
+ * programmatic dependent) merges into out.
+ *
+ * counters     int32 [b2_decode_step_counters(batch)] (= 2); must be zero
+ *              before the first call; every call that completes leaves it
+ *              zero again (after a device error, zero it again).
+ * part_ml/o    as b2_decode_attn with num_splits = ceil(max_blocks / bps).
+ * blocks_per_split  1 .. 32.
+ * out          bf16 [batch][16][64]; q_out optional bf16 [batch][16][64].
+ * Calls sharing `counters` must not overlap on the GPU.
+ */
+int b2_decode_step_counters(int32_t batch);
+int b2_decode_step(const uint16_t *qkv, int64_t row_stride,
+                   const uint16_t *gamma_q, const uint16_t *gamma_k, float eps,
+                   const uint16_t *rope_cos, const uint16_t *rope_sin,
+                   int32_t rope_rows, const int32_t *past_lens,
+                   const int32_t *block_tables, int32_t max_blocks_per_seq,
+                   uint16_t *k_pool, uint16_t *v_pool, int32_t num_blocks,
+                   int32_t batch, int32_t blocks_per_split, float scale,
+                   int32_t mode, uint16_t *out, uint16_t *q_out,
+                   float *part_ml, float *part_o, int32_t *counters,
+                   int32_t max_ctas, int32_t *dev_err, void *stream);
+
+/*
  * Allocation-free decode: b2_decode_attn followed by b2_combine, with the
  * partial softmax states kept in a static device array inside this library
  * instead of caller-provided part_ml / part_o buffers.  It has no counterpart

@@ -163,21 +163,80 @@ def combine(part_ml: torch.Tensor, part_o: torch.Tensor, num_parts: int, batch: 
     _lib.check(rc, "b2_combine")
 
 
+def decode_step(qkv: torch.Tensor, past_lens: torch.Tensor, *, k_pool: torch.Tensor, v_pool: torch.Tensor,
+                block_tables: torch.Tensor, blocks_per_split: int, out: torch.Tensor, part_ml: torch.Tensor,
+                part_o: torch.Tensor, counters: torch.Tensor, dev_err: torch.Tensor,
+                gamma_q: torch.Tensor | None = None, gamma_k: torch.Tensor | None = None,
+                cos: torch.Tensor | None = None, sin: torch.Tensor | None = None, q_out: torch.Tensor | None = None,
+                mode: int = _lib.B2_NORM_QK | _lib.B2_ROPE_QK | _lib.B2_STORE_KV, eps: float = EPS,
+                scale: float = SCALE, max_ctas: int = 0, stream: torch.cuda.Stream | None = None) -> int:
+    """Fused decode step in one persistent launch (b2_decode_step): norm + RoPE,
+    append at past_lens[b], attention over past_lens[b] + 1 tokens, merge.
+    `counters` (int32[2]) must be zero on the first call; the kernel leaves
+    it zero.  Returns num_splits."""
+    dev = qkv.device
+    if qkv.dim() != 2 or qkv.shape[1] < QKV_WIDTH:
+        raise ValueError(f"qkv must be [batch, >= {QKV_WIDTH}], got {tuple(qkv.shape)}")
+    _need(qkv, "qkv", torch.bfloat16, dev)
+    b = qkv.shape[0]
+    _need(past_lens, "past_lens", torch.int32, dev, (b,))
+    _need(k_pool, "k_pool", torch.bfloat16, dev)
+    _need(v_pool, "v_pool", torch.bfloat16, dev, tuple(k_pool.shape))
+    if k_pool.dim() != 4 or tuple(k_pool.shape[1:]) != (HKV, BLOCK, D):
+        raise ValueError("pools must be [num_blocks, 8, 64, 64]")
+    _need(block_tables, "block_tables", torch.int32, dev)
+    if block_tables.dim() != 2 or block_tables.shape[0] != b:
+        raise ValueError("block_tables must be [batch, max_blocks_per_seq]")
+    _need(out, "out", torch.bfloat16, dev)
+    if out.numel() != b * HQ * D:
+        raise ValueError("out must hold batch x 16 x 64 elements")
+    if q_out is not None:
+        _need(q_out, "q_out", torch.bfloat16, dev, (b, HQ, D))
+    _need(counters, "counters", torch.int32, dev)
+    if counters.numel() < 2:
+        raise ValueError("counters must hold 2 int32")
+    _need(dev_err, "dev_err", torch.int32, dev)
+    rope_rows = 0
+    if mode & _lib.B2_NORM_QK:
+        _need(gamma_q, "gamma_q", torch.bfloat16, dev, (D,))
+        _need(gamma_k, "gamma_k", torch.bfloat16, dev, (D,))
+    if mode & _lib.B2_ROPE_QK:
+        _need(cos, "cos", torch.bfloat16, dev)
+        _need(sin, "sin", torch.bfloat16, dev, tuple(cos.shape))
+        rope_rows = cos.shape[0]
+    max_blocks = block_tables.shape[1]
+    splits = num_splits_for(max_blocks, blocks_per_split)
+    _need(part_ml, "part_ml", torch.float32, dev)
+    _need(part_o, "part_o", torch.float32, dev)
+    if part_ml.numel() < b * splits * HQ * 2 or part_o.numel() < b * splits * HQ * D:
+        raise ValueError(f"partial-state buffers too small for {b} x {splits} splits")
+    rc = _lib.load().b2_decode_step(
+        _ptr(qkv), qkv.stride(0), _ptr(gamma_q), _ptr(gamma_k), ctypes.c_float(eps), _ptr(cos), _ptr(sin),
+        rope_rows, _ptr(past_lens), _ptr(block_tables), max_blocks, _ptr(k_pool), _ptr(v_pool), k_pool.shape[0],
+        b, blocks_per_split, ctypes.c_float(scale), mode, _ptr(out), _ptr(q_out), _ptr(part_ml), _ptr(part_o),
+        _ptr(counters), max_ctas, _ptr(dev_err), _stream(dev, stream))
+    _lib.check(rc, "b2_decode_step")
+    return splits
+
+
 class PagedDecodeAttention:
     """Decode attention of one new token per sequence over a PagedKVCache.
 
-    step(layer, qkv, past_lens, seq_lens) runs, on the current stream:
+    step(layer, qkv, past_lens, seq_lens) runs, on the current stream, either
+    the fused persistent kernel (b2_decode_step, the default) or the three
+    separate kernels (fused=False):
       b2_append_rope  (q/k norm + RoPE, k/v into slot past_lens[b])
       b2_decode_attn  (split-KV flash-decode over seq_lens[b] tokens)
       b2_combine      (partial states -> bf16 context [B, 16, 64])
-    seq_lens must equal past_lens + 1 (the new token is attended).  All
-    buffers are allocated here once; step() allocates nothing, so it can be
-    captured in a CUDA graph.
+    seq_lens must equal past_lens + 1 (the new token is attended; the fused
+    kernel derives it from past_lens).  All buffers are allocated here once;
+    step() allocates nothing, so it can be captured in a CUDA graph.
     """
 
     def __init__(self, cache: PagedKVCache, gamma_q: torch.Tensor, gamma_k: torch.Tensor,
                  max_batch: int, rope_positions: int, *, eps: float = EPS,
-                 blocks_per_split: int | None = None, work_blocks: int | None = None):
+                 blocks_per_split: int | None = None, work_blocks: int | None = None,
+                 fused: bool = True, max_ctas: int = 0):
         self.cache = cache
         dev = cache.device
         self.device = dev
@@ -188,7 +247,11 @@ class PagedDecodeAttention:
         if blocks_per_split is None:
             wb = work_blocks if work_blocks is not None else max_batch * cache.max_blocks
             blocks_per_split = choose_blocks_per_split(max_batch, wb)
+        if fused:
+            blocks_per_split = min(blocks_per_split, 32)
         self.blocks_per_split = blocks_per_split
+        self.fused = fused
+        self.max_ctas = max_ctas
         self.num_splits = num_splits_for(cache.max_blocks, blocks_per_split)
         self.max_batch = max_batch
         self.q = torch.empty(max_batch, HQ, D, dtype=torch.bfloat16, device=dev)
@@ -196,6 +259,7 @@ class PagedDecodeAttention:
         self.part_o = torch.empty(max_batch, self.num_splits, HQ, D, dtype=torch.float32, device=dev)
         self.out = torch.empty(max_batch, HQ, D, dtype=torch.bfloat16, device=dev)
         self.dev_err = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.counters = torch.zeros(2, dtype=torch.int32, device=dev)
 
     def step(self, layer: int, qkv: torch.Tensor, past_lens: torch.Tensor, seq_lens: torch.Tensor,
              block_tables: torch.Tensor, out: torch.Tensor | None = None,
@@ -205,6 +269,13 @@ class PagedDecodeAttention:
             raise ValueError(f"batch {b} > max_batch {self.max_batch}")
         kp, vp = self.cache.pool(layer)
         q = self.q[:b]
+        if self.fused:
+            o = self.out[:b] if out is None else out
+            decode_step(qkv, past_lens, k_pool=kp, v_pool=vp, block_tables=block_tables,
+                        blocks_per_split=self.blocks_per_split, out=o, part_ml=self.part_ml, part_o=self.part_o,
+                        counters=self.counters, dev_err=self.dev_err, gamma_q=self.gamma_q, gamma_k=self.gamma_k,
+                        cos=self.cos, sin=self.sin, q_out=q, eps=self.eps, max_ctas=self.max_ctas, stream=stream)
+            return o
         append_rope(qkv, past_lens, q_out=q, dev_err=self.dev_err, gamma_q=self.gamma_q,
                     gamma_k=self.gamma_k, cos=self.cos, sin=self.sin, k_pool=kp, v_pool=vp,
                     block_tables=block_tables, eps=self.eps, stream=stream)
@@ -221,4 +292,5 @@ class PagedDecodeAttention:
         word = int(self.dev_err.item())
         if word:
             self.dev_err.zero_()
+            self.counters.zero_()   # an aborted fused step may leave counts behind
             raise RuntimeError("decode attention device error: " + "; ".join(_lib.decode_dev_err(word)))

@@ -190,6 +190,52 @@ struct AppendArgs {
   int32_t *err;
 };
 
+// Per-head RMSNorm (optional) and rotate-half RoPE (optional) of one 64-wide
+// head vector spread over an aligned group of 8 lanes: chunk j = lane % 8
+// holds x[8] = elements 8j..8j+7.  Every lane of the warp must call this
+// (it shuffles with the full mask); `norm` / `rope` may differ per group.
+//  * Lfm2RMSNorm: gamma * bf16(x * 1/sqrt(mean(x^2) + eps)) with fp32 math and
+//    IEEE-rounded sqrt and divide, as torch's CPU rsqrt computes 1/sqrt.
+//  * RoPE: bf16(bf16(x*cos) + bf16(rotate_half(x)*sin)), rotate_half(x) =
+//    [-x[32:], x[:32]]; the partner chunk j^4 sits on lane^4.
+__device__ __forceinline__ void norm_rope8(float x[8], int j, bool norm, bool rope,
+                                           const uint16_t *gamma, float eps,
+                                           const uint16_t *cos_row, const uint16_t *sin_row) {
+  float ss = 0.f;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) ss = fmaf(x[e], x[e], ss);
+  ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+  ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+  ss += __shfl_xor_sync(0xffffffffu, ss, 4);
+  if (norm) {
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ss * (1.0f / kDim), eps)));
+    float g[8];
+    unpack8(*reinterpret_cast<const uint4 *>(gamma + j * 8), g);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) x[e] = bf16_round(__fmul_rn(g[e], bf16_round(__fmul_rn(x[e], inv))));
+  }
+  float p[8];
+#pragma unroll
+  for (int e = 0; e < 8; e += 2) {
+    const uint32_t w = bf16_bits(x[e]) | (bf16_bits(x[e + 1]) << 16);
+    const uint32_t o = __shfl_xor_sync(0xffffffffu, w, 4);
+    p[e] = __uint_as_float(o << 16);
+    p[e + 1] = __uint_as_float(o & 0xffff0000u);
+  }
+  if (rope) {
+    float c[8], s[8];
+    unpack8(*reinterpret_cast<const uint4 *>(cos_row + j * 8), c);
+    unpack8(*reinterpret_cast<const uint4 *>(sin_row + j * 8), s);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float rot = j < 4 ? -p[e] : p[e];
+      const float part1 = bf16_round(__fmul_rn(x[e], c[e]));
+      const float part2 = bf16_round(__fmul_rn(rot, s[e]));
+      x[e] = bf16_round(__fadd_rn(part1, part2));
+    }
+  }
+}
+
 // One CTA (8 warps) per sequence.  The 32 head vectors of a qkv row
 // (16 q, 8 k, 8 v) are split 4 per warp; 8 lanes own one vector, 8
 // consecutive bf16 (16 bytes) each, so loads and stores are 16-byte
@@ -205,51 +251,12 @@ __global__ void __launch_bounds__(256) append_rope_kernel(const AppendArgs a) {
 
   float x[8];
   unpack8(*reinterpret_cast<const uint4 *>(a.qkv + b * a.row_stride + vec * kDim + j * 8), x);
-
-  if (!is_v && (a.mode & B2_NORM_QK)) {
-    // Lfm2RMSNorm: gamma * bf16(x * 1/sqrt(mean(x^2) + eps)), fp32 math,
-    // IEEE-rounded sqrt and divide like torch's CPU rsqrt.
-    float ss = 0.f;
-#pragma unroll
-    for (int e = 0; e < 8; ++e) ss = fmaf(x[e], x[e], ss);
-    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-    ss += __shfl_xor_sync(0xffffffffu, ss, 2);
-    ss += __shfl_xor_sync(0xffffffffu, ss, 4);
-    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ss * (1.0f / kDim), a.eps)));
-    float g[8];
-    unpack8(*reinterpret_cast<const uint4 *>((is_q ? a.gamma_q : a.gamma_k) + j * 8), g);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) x[e] = bf16_round(__fmul_rn(g[e], bf16_round(__fmul_rn(x[e], inv))));
-  }
-
   const bool pos_ok = pos >= 0 && pos < a.max_blocks * kBlock;
-  if (!is_v && (a.mode & B2_ROPE_QK)) {
-    // q*cos + rotate_half(q)*sin with bf16 rounding after each product and
-    // after the sum; rotate_half(x) = [-x[32:], x[:32]].
-    float p[8];
-#pragma unroll
-    for (int e = 0; e < 8; e += 2) {
-      const uint32_t w = bf16_bits(x[e]) | (bf16_bits(x[e + 1]) << 16);
-      const uint32_t o = __shfl_xor_sync(0xffffffffu, w, 4);
-      p[e] = __uint_as_float(o << 16);
-      p[e + 1] = __uint_as_float(o & 0xffff0000u);
-    }
-    const bool rope_ok = pos >= 0 && pos < a.rope_rows;
-    if (!rope_ok) {
-      if (j == 0 && vec == 0) atomicOr(a.err, B2_DEV_BAD_POSITION);
-    } else {
-      float c[8], s[8];
-      unpack8(*reinterpret_cast<const uint4 *>(a.cos + (int64_t)pos * kDim + j * 8), c);
-      unpack8(*reinterpret_cast<const uint4 *>(a.sin + (int64_t)pos * kDim + j * 8), s);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const float rot = j < 4 ? -p[e] : p[e];
-        const float part1 = bf16_round(__fmul_rn(x[e], c[e]));
-        const float part2 = bf16_round(__fmul_rn(rot, s[e]));
-        x[e] = bf16_round(__fadd_rn(part1, part2));
-      }
-    }
-  }
+  const bool rope_ok = pos >= 0 && pos < a.rope_rows;
+  if ((a.mode & B2_ROPE_QK) && !rope_ok && j == 0 && vec == 0) atomicOr(a.err, B2_DEV_BAD_POSITION);
+  const bool rope = !is_v && (a.mode & B2_ROPE_QK) && rope_ok;
+  norm_rope8(x, j, !is_v && (a.mode & B2_NORM_QK), rope, is_q ? a.gamma_q : a.gamma_k, a.eps,
+             rope ? a.cos + (int64_t)pos * kDim : nullptr, rope ? a.sin + (int64_t)pos * kDim : nullptr);
 
   if (is_q) {
     if (a.q_out)
@@ -509,18 +516,27 @@ struct CombineArgs {
   uint16_t *out;
   float *state_ml;
   float *state_o;
+  int len_offset;   // 1 when seq_lens holds past lengths (the new token is added)
+  int skip_single;  // sequences with one part were written by the decode kernel
+  int max_tokens;   // num_parts * blocks_per_split * 64: longer lengths are invalid
 };
 
 // grid (batch), block (16 heads x 64 dims); one thread per output element.
+// When launched as a programmatic dependent of the decode-step kernel it may
+// start early; griddepcontrol.wait holds it until that kernel has completed
+// and its memory is visible (a no-op for an ordinary launch).
 __global__ void __launch_bounds__(1024) combine_kernel(const CombineArgs a) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int b = blockIdx.x;
   const int h = threadIdx.x >> 6;
   const int d = threadIdx.x & 63;
   int parts = a.num_parts;
   if (a.seq_lens) {
-    const int len = max(a.seq_lens[b], 0);
-    const int nblk = (len + kBlock - 1) / kBlock;
+    const int len = a.seq_lens[b] + a.len_offset;
+    if (len > a.max_tokens) return;  // flagged by the decode kernel
+    const int nblk = len > 0 ? (len + kBlock - 1) / kBlock : 0;
     parts = min(parts, (nblk + a.blocks_per_split - 1) / a.blocks_per_split);
+    if (a.skip_single && parts == 1) return;  // written by the decode kernel
   }
   const float *ml = a.part_ml + ((int64_t)b * a.num_parts * kHq + h) * 2;
   const float *po = a.part_o + ((int64_t)b * a.num_parts * kHq + h) * kDim + d;
@@ -539,6 +555,458 @@ __global__ void __launch_bounds__(1024) combine_kernel(const CombineArgs a) {
     if (d == 0) {
       a.state_ml[((int64_t)b * kHq + h) * 2] = M;
       a.state_ml[((int64_t)b * kHq + h) * 2 + 1] = L;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ fused persistent decode step
+
+// One launch per decode step: q/k norm + RoPE + KV append + split-KV
+// attention + merge.  A persistent grid (3 CTAs per SM) takes work items
+// (split, sequence, kv head) from a global counter; the producer warp keeps
+// the TMA ring full across item boundaries, so the pipeline never drains
+// between items and the end-of-launch tail is at most one short item per CTA.
+constexpr int kFlagFirst = 1;  // first block of an item: load q, reset state
+constexpr int kFlagLast = 2;   // last block of an item: epilogue
+constexpr int kFlagFinal = 4;  // the item is the whole sequence: write the context directly
+constexpr int kFlagEnd = 8;    // no more work
+
+struct __align__(16) StageMeta {
+  int b, kvh, split, rows;   // rows: valid rows of this block (may exceed 64)
+  int flags, nsplit, pad0, pad1;
+  uint16_t q[2 * kDim];      // bf16 q of heads 2kvh, 2kvh+1 (first block of an item)
+};
+
+// Batches up to this size enumerate only real work items: the producer
+// warp builds the prefix sum of splits per sequence in shared memory at start.
+// Larger batches walk the dense (split, sequence, head) space and skip the
+// splits that lie past a sequence's end.
+constexpr int kMaxCompactBatch = 512;
+
+struct __align__(16) StepTail {
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t ebar;  // consumer-warp barrier of the epilogue (bounded waits)
+  StageMeta meta[kStages];
+  float red[2][kConsumerWarps][2][2 + kDim];  // double-buffered by epilogue parity
+  int prefix[kMaxCompactBatch + 1];  // prefix[b] = splits of sequences 0..b-1
+};
+constexpr int kStepSmem = kStages * kStageBytes + 1024 + (int)sizeof(StepTail);
+
+struct StepArgs {
+  const uint16_t *qkv;
+  int64_t row_stride;
+  const uint16_t *gamma_q, *gamma_k;
+  float eps;
+  const uint16_t *cos, *sin;
+  int rope_rows;
+  const int32_t *past_lens;
+  const int32_t *block_tables;
+  int max_blocks;
+  uint16_t *k_pool, *v_pool;
+  int num_blocks;
+  int batch, blocks_per_split, num_splits, total_items;
+  float scale_log2;
+  int mode;
+  uint16_t *out, *q_out;
+  float *part_ml, *part_o;
+  int32_t *counters;  // [0] work counter, [1] finished-CTA counter
+  int32_t *err;
+};
+
+// Barrier of the 4 consumer warps on an mbarrier, with a bounded wait (a
+// hardware named barrier could not give up if a warp had left on a timeout).
+__device__ __forceinline__ void consumers_sync(StepTail *tail, int lane, uint32_t &phase, int32_t *err) {
+  __syncwarp();
+  if (lane == 0) mbar_arrive(smem_u32(&tail->ebar));
+  const bool ok = mbar_wait(smem_u32(&tail->ebar), phase & 1);
+  ++phase;
+  if (!ok && lane == 0) atomicOr(err, B2_DEV_TIMEOUT);
+  __syncwarp();
+}
+
+// One work item as the producer sees it, with its loads already issued.
+struct ProducerItem {
+  int valid, b, kvh, split, past, nsplit, blk0, n;
+  int my_blk;   // block table entry blk0 + lane (lane < n)
+  uint4 raw;    // this lane's 16 bytes of the item's q/k/v vectors
+};
+
+// Decode work index w and issue its loads.  Compact enumeration: w = p * 8 +
+// kvh over the real (sequence, split) pairs p; dense: w = (split * batch + b)
+// * 8 + kvh, returning valid = 0 for a split past the sequence's end (the
+// caller skips it) and -1 past the end of the work.
+__device__ __forceinline__ ProducerItem producer_load(const StepArgs &a, const StepTail *tail, bool compact,
+                                                      int total, int w, int lane) {
+  ProducerItem it;
+  it.valid = -1;
+  if (w >= total) return it;
+  it.valid = 1;
+  it.kvh = w & 7;
+  const int p = w >> 3;
+  if (compact) {
+    int lo = 0, hi = a.batch;  // largest b with prefix[b] <= p
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (tail->prefix[mid] <= p) lo = mid; else hi = mid;
+    }
+    it.b = lo;
+    it.split = p - tail->prefix[lo];
+  } else {
+    it.split = p / a.batch;
+    it.b = p - it.split * a.batch;
+  }
+  it.past = __ldg(a.past_lens + it.b);
+  const bool len_ok = it.past >= 0 && it.past < a.max_blocks * kBlock;
+  const int seq_len = it.past + 1;
+  const int nblk = (seq_len + kBlock - 1) / kBlock;
+  it.nsplit = (nblk + a.blocks_per_split - 1) / a.blocks_per_split;
+  if (!len_ok || it.split >= it.nsplit) {
+    if (!len_ok && lane == 0 && it.kvh == 0 && it.split == 0) atomicOr(a.err, B2_DEV_BAD_LENGTH);
+    it.valid = 0;
+    return it;
+  }
+  it.blk0 = it.split * a.blocks_per_split;
+  it.n = min(a.blocks_per_split, nblk - it.blk0);
+  it.my_blk = lane < it.n ? __ldg(a.block_tables + (int64_t)it.b * a.max_blocks + it.blk0 + lane) : 0;
+  const int grp = lane >> 3;
+  const int vec = grp < 2 ? 2 * it.kvh + grp : (grp == 2 ? kHq + it.kvh : kHq + kHkv + it.kvh);
+  it.raw = __ldg(reinterpret_cast<const uint4 *>(a.qkv + it.b * a.row_stride + vec * kDim + (lane & 7) * 8));
+  return it;
+}
+
+// Producer warp: takes items from the work counter one ahead of the item it
+// is issuing (the next item's counter update and loads are in flight while
+// this item's copies wait for free stages), prepares q (and the appended k/v
+// on the item holding the new token) with all 32 lanes, and lane 0 issues
+// the TMA loads.  Lanes 0-15 hold the two q heads, 16-23 k, 24-31 v.
+__device__ __forceinline__ void step_producer(const StepArgs &a, StepTail *tail, uint8_t *tiles,
+                                              const CUtensorMap *tm_k, const CUtensorMap *tm_v,
+                                              int lane) {
+  int32_t *work_ctr = a.counters;
+  const uint64_t policy = evict_first_policy();
+  const int grp = lane >> 3, j = lane & 7;
+  const bool compact = a.batch <= kMaxCompactBatch;
+  int total = a.total_items;
+  if (compact) {
+    // prefix[b + 1] = sum of splits of sequences 0..b (inclusive warp scan per 32)
+    int running = 0;
+    for (int base = 0; base < a.batch; base += 32) {
+      const int b = base + lane;
+      int ns = 0;
+      if (b < a.batch) {
+        const int past = __ldg(a.past_lens + b);
+        if (past >= 0 && past < a.max_blocks * kBlock) {
+          const int nblk = (past + 1 + kBlock - 1) / kBlock;
+          ns = (nblk + a.blocks_per_split - 1) / a.blocks_per_split;
+        } else if (blockIdx.x == 0) {
+          atomicOr(a.err, B2_DEV_BAD_LENGTH);
+        }
+      }
+      int incl = ns;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += v;
+      }
+      if (b < a.batch) tail->prefix[b + 1] = running + incl;
+      running += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) tail->prefix[0] = 0;
+    __syncwarp();
+    total = running * kHkv;
+  }
+  int issued = 0;
+  bool ok = true;
+  auto next_item = [&]() {
+    ProducerItem it;
+    do {
+      int w = 0;
+      if (lane == 0) w = atomicAdd(work_ctr, 1);
+      w = __shfl_sync(0xffffffffu, w, 0);
+      it = producer_load(a, tail, compact, total, w, lane);
+    } while (it.valid == 0);
+    return it;
+  };
+  ProducerItem nxt = next_item();
+  while (nxt.valid > 0) {
+    const ProducerItem cur = nxt;
+    // start the next item's counter update before this item's work
+    int w_next = 0;
+    if (lane == 0) w_next = atomicAdd(work_ctr, 1);
+
+    float x[8];
+    unpack8(cur.raw, x);
+    const bool rope_ok = cur.past < a.rope_rows;
+    if ((a.mode & B2_ROPE_QK) && !rope_ok && lane == 0 && cur.split == 0 && cur.kvh == 0)
+      atomicOr(a.err, B2_DEV_BAD_POSITION);
+    const bool rope = grp < 3 && (a.mode & B2_ROPE_QK) && rope_ok;
+    norm_rope8(x, j, grp < 3 && (a.mode & B2_NORM_QK), rope, grp < 2 ? a.gamma_q : a.gamma_k, a.eps,
+               rope ? a.cos + (int64_t)cur.past * kDim : nullptr,
+               rope ? a.sin + (int64_t)cur.past * kDim : nullptr);
+    const uint4 packed = pack8(x);
+    if (cur.split == 0 && grp < 2 && a.q_out)
+      *reinterpret_cast<uint4 *>(a.q_out + ((int64_t)cur.b * kHq + 2 * cur.kvh + grp) * kDim + j * 8) = packed;
+    if (cur.split == cur.nsplit - 1 && (a.mode & B2_STORE_KV)) {
+      // The new token's row lies in this item's last block: write it, then
+      // fence so the TMA (async proxy) read of that tile sees the store.
+      const int blk = __shfl_sync(0xffffffffu, cur.my_blk, cur.past / kBlock - cur.blk0);
+      if (blk < 0 || blk >= a.num_blocks) {
+        if (lane == 0) atomicOr(a.err, B2_DEV_BAD_BLOCK);
+      } else if (grp >= 2) {
+        uint16_t *pool = grp == 2 ? a.k_pool : a.v_pool;
+        *reinterpret_cast<uint4 *>(
+            pool + (((int64_t)blk * kHkv + cur.kvh) * kBlock + cur.past % kBlock) * kDim + j * 8) = packed;
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+      }
+    }
+    __syncwarp();
+    for (int jj = 0; jj < cur.n; ++jj, ++issued) {
+      const int s = issued % kStages;
+      const uint32_t ph = (issued / kStages) & 1;
+      int wait_ok = 1;
+      if (issued >= kStages && lane == 0) wait_ok = mbar_wait(smem_u32(&tail->empty[s]), ph ^ 1);
+      wait_ok = __shfl_sync(0xffffffffu, wait_ok, 0);
+      if (!wait_ok) {
+        if (lane == 0) atomicOr(a.err, B2_DEV_TIMEOUT);
+        ok = false;
+        break;
+      }
+      int blk = __shfl_sync(0xffffffffu, cur.my_blk, jj);
+      StageMeta &m = tail->meta[s];
+      if (jj == 0 && grp < 2) *reinterpret_cast<uint4 *>(m.q + grp * kDim + j * 8) = packed;
+      if (lane == 0) {
+        if (blk < 0 || blk >= a.num_blocks) {
+          atomicOr(a.err, B2_DEV_BAD_BLOCK);
+          blk = 0;  // read a valid tile instead; the result is flagged as bad
+        }
+        m.b = cur.b;
+        m.kvh = cur.kvh;
+        m.split = cur.split;
+        m.rows = cur.past + 1 - (cur.blk0 + jj) * kBlock;
+        m.nsplit = cur.nsplit;
+        m.flags = (jj == 0 ? kFlagFirst : 0) | (jj == cur.n - 1 ? kFlagLast : 0) |
+                  (cur.nsplit == 1 ? kFlagFinal : 0);
+      }
+      __syncwarp();
+      if (lane == 0) {
+        const uint32_t full = smem_u32(&tail->full[s]);
+        const int row = (blk * kHkv + cur.kvh) * kBlock;
+        uint8_t *dst = tiles + s * kStageBytes;
+        mbar_expect_tx(full, kStageBytes);
+        tma_load_2d(smem_u32(dst), tm_k, 0, row, full, policy);
+        tma_load_2d(smem_u32(dst + kTileBytes), tm_v, 0, row, full, policy);
+      }
+      if (jj == 0) {
+        // the first copy of this item is queued: load the next item now
+        w_next = __shfl_sync(0xffffffffu, w_next, 0);
+        nxt = producer_load(a, tail, compact, total, w_next, lane);
+      }
+    }
+    if (!ok) break;
+    if (nxt.valid == 0) nxt = next_item();
+  }
+  if (lane != 0) return;
+  if (ok) {
+    // end-of-work marker: a plain arrival completes the stage's phase
+    const int s = issued % kStages;
+    const uint32_t ph = (issued / kStages) & 1;
+    if (issued < kStages || mbar_wait(smem_u32(&tail->empty[s]), ph ^ 1)) {
+      tail->meta[s].flags = kFlagEnd;
+      mbar_arrive(smem_u32(&tail->full[s]));
+      return;  // consumers wait for every issued copy before they see the marker
+    }
+    atomicOr(a.err, B2_DEV_TIMEOUT);
+  }
+  // Aborting: wait (bounded) for the copies this CTA issued, then leave.
+  for (int s = 0; s < kStages && s < issued; ++s) {
+    const int last = s + kStages * ((issued - 1 - s) / kStages);
+    if (!mbar_wait(smem_u32(&tail->full[s]), (last / kStages) & 1)) atomicOr(a.err, B2_DEV_TIMEOUT);
+  }
+}
+
+// End of an item: merge lanes, then the 4 warps, into the item's state.  A
+// whole-sequence item writes the context; otherwise the partial state goes
+// to part_ml/part_o for the combine kernel that follows.  red[] is
+// double-buffered by epilogue parity, so a single barrier separates its
+// writes from its reads and the next epilogue cannot overwrite it early.
+__device__ __forceinline__ void step_epilogue(const StepArgs &a, StepTail *tail, int warp, int lane, int b,
+                                              int kvh, int split, bool final_item, float m0, float m1,
+                                              float lsum, float acc0[8], float acc1[8], uint32_t &ephase,
+                                              int rbuf) {
+  float(*red)[2][2 + kDim] = tail->red[rbuf];
+#pragma unroll
+  for (int off = 2; off < 32; off <<= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, off);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    acc0[e] += __shfl_xor_sync(0xffffffffu, acc0[e], 8);
+    acc0[e] += __shfl_xor_sync(0xffffffffu, acc0[e], 16);
+    acc1[e] += __shfl_xor_sync(0xffffffffu, acc1[e], 8);
+    acc1[e] += __shfl_xor_sync(0xffffffffu, acc1[e], 16);
+  }
+  const int c = lane & 7;
+  if (lane < 8) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      red[warp][0][2 + c * 8 + e] = acc0[e];
+      red[warp][1][2 + c * 8 + e] = acc1[e];
+    }
+  }
+  if (lane < 2) {
+    red[warp][lane][0] = lane ? m1 : m0;
+    red[warp][lane][1] = lsum;
+  }
+  consumers_sync(tail, lane, ephase, a.err);
+  const int t = threadIdx.x;  // 0..127
+  const int h = t >> 6, d = t & 63;
+  float M = -1.0e30f;
+#pragma unroll
+  for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, red[w][h][0]);
+  float L = 0.f, O = 0.f;
+#pragma unroll
+  for (int w = 0; w < kConsumerWarps; ++w) {
+    const float sc = ex2(red[w][h][0] - M);
+    L = fmaf(red[w][h][1], sc, L);
+    O = fmaf(red[w][h][2 + d], sc, O);
+  }
+  if (final_item) {
+    a.out[((int64_t)b * kHq + 2 * kvh + h) * kDim + d] = static_cast<uint16_t>(bf16_bits(O / L));
+    return;
+  }
+  const int64_t idx = ((int64_t)b * a.num_splits + split) * kHq + 2 * kvh + h;
+  a.part_o[idx * kDim + d] = O;
+  if (d == 0) {
+    a.part_ml[idx * 2] = M;
+    a.part_ml[idx * 2 + 1] = L;
+  }
+}
+
+__global__ void __launch_bounds__(kDecodeThreads, 3)
+    decode_step_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                       const StepArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *tiles = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  StepTail *tail = reinterpret_cast<StepTail *>(tiles + kStages * kStageBytes);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(smem_u32(&tail->full[s]), 1);
+      mbar_init(smem_u32(&tail->empty[s]), kConsumerWarps);
+    }
+    mbar_init(smem_u32(&tail->ebar), kConsumerWarps);
+    mbar_fence_init();
+  }
+  __syncthreads();
+  // Let the combine kernel be scheduled as soon as CTAs of this grid retire;
+  // it waits for this grid's completion before reading the partial states.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+  if (warp == kConsumerWarps) {
+    step_producer(a, tail, tiles, &tm_k, &tm_v, lane);
+  } else {
+    const int r = lane >> 1, half = lane & 1;
+    const int c = lane & 7, g = lane >> 3;
+    const int qrow = 16 * warp + r;
+    float q0[32], q1[32];
+    float m0 = -1.0e30f, m1 = -1.0e30f, lsum = 0.f;
+    float acc0[8], acc1[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc0[e] = acc1[e] = 0.f;
+    uint32_t ephase = 0;  // completed phases of the epilogue barrier
+    int epilogues = 0;    // red[] buffer parity
+    for (int it = 0;; ++it) {
+      const int s = it % kStages;
+      const uint32_t ph = (it / kStages) & 1;
+      if (!mbar_wait(smem_u32(&tail->full[s]), ph)) {
+        if (lane == 0) atomicOr(a.err, B2_DEV_TIMEOUT);
+        break;
+      }
+      const StageMeta &meta = tail->meta[s];
+      const int flags = meta.flags;
+      if (flags & kFlagEnd) break;
+      const int b = meta.b, kvh = meta.kvh, split = meta.split;
+      const int valid = meta.rows - 16 * warp;
+      if (flags & kFlagFirst) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          unpack8(*reinterpret_cast<const uint4 *>(meta.q + half * 32 + k * 8), q0 + k * 8);
+          unpack8(*reinterpret_cast<const uint4 *>(meta.q + kDim + half * 32 + k * 8), q1 + k * 8);
+        }
+        m0 = m1 = -1.0e30f;
+        lsum = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc0[e] = acc1[e] = 0.f;
+      }
+      const uint8_t *kt = tiles + s * kStageBytes;
+      const uint8_t *vt = kt + kTileBytes;
+      float d0 = 0.f, d1 = 0.f;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int pc = (half * 4 + k) ^ (qrow & 7);
+        float f[8];
+        unpack8(*reinterpret_cast<const uint4 *>(kt + qrow * 128 + pc * 16), f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          d0 = fmaf(q0[k * 8 + e], f[e], d0);
+          d1 = fmaf(q1[k * 8 + e], f[e], d1);
+        }
+      }
+      d0 += __shfl_xor_sync(0xffffffffu, d0, 1);
+      d1 += __shfl_xor_sync(0xffffffffu, d1, 1);
+      const bool tv = r < valid;
+      const float s0 = tv ? d0 * a.scale_log2 : -INFINITY;
+      const float s1 = tv ? d1 * a.scale_log2 : -INFINITY;
+      float bm0 = s0, bm1 = s1;
+#pragma unroll
+      for (int off = 2; off < 32; off <<= 1) {
+        bm0 = fmaxf(bm0, __shfl_xor_sync(0xffffffffu, bm0, off));
+        bm1 = fmaxf(bm1, __shfl_xor_sync(0xffffffffu, bm1, off));
+      }
+      const float mn0 = fmaxf(m0, bm0), mn1 = fmaxf(m1, bm1);
+      const float a0 = ex2(m0 - mn0), a1 = ex2(m1 - mn1);
+      m0 = mn0;
+      m1 = mn1;
+      const float p = ex2((half ? s1 : s0) - (half ? mn1 : mn0));
+      lsum = fmaf(lsum, half ? a1 : a0, p);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        acc0[e] *= a0;
+        acc1[e] *= a1;
+      }
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        const int t = 4 * g + jj;
+        const float p0 = __shfl_sync(0xffffffffu, p, 2 * t);
+        const float p1 = __shfl_sync(0xffffffffu, p, 2 * t + 1);
+        if (t < valid) {
+          const int vrow = 16 * warp + t;
+          float f[8];
+          unpack8(*reinterpret_cast<const uint4 *>(vt + vrow * 128 + ((c ^ (vrow & 7)) * 16)), f);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            acc0[e] = fmaf(p0, f[e], acc0[e]);
+            acc1[e] = fmaf(p1, f[e], acc1[e]);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&tail->empty[s]));
+      if (flags & kFlagLast)
+        step_epilogue(a, tail, warp, lane, b, kvh, split, (flags & kFlagFinal) != 0, m0, m1, lsum, acc0, acc1,
+                      ephase, (epilogues++) & 1);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    // The last CTA to finish resets the work counter for the next launch.
+    int32_t *work_ctr = a.counters;
+    __threadfence();
+    if (atomicAdd(work_ctr + 1, 1) == (int)gridDim.x - 1) {
+      atomicExch(work_ctr, 0);
+      atomicExch(work_ctr + 1, 0);
     }
   }
 }
@@ -592,6 +1060,31 @@ bool decode_smem_ready() {
     done[dev] = true;
   }
   return true;
+}
+
+bool step_smem_ready() {
+  static bool done[128] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return false;
+  if (!done[dev]) {
+    if (cudaFuncSetAttribute(decode_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kStepSmem) !=
+        cudaSuccess)
+      return false;
+    done[dev] = true;
+  }
+  return true;
+}
+
+int sm_count() {
+  static int count[128] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return 148;
+  if (!count[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    count[dev] = n;
+  }
+  return count[dev];
 }
 
 }  // namespace
@@ -684,9 +1177,83 @@ extern "C" int b2_combine(const float *part_ml, const float *part_o, int32_t num
   if (seq_lens && blocks_per_split <= 0) return fail(B2_ERR_ARG, "blocks_per_split must be positive");
   if (!out && !state_o) return fail(B2_ERR_ARG, "one of out or state_o is required");
   if ((state_o == nullptr) != (state_ml == nullptr)) return fail(B2_ERR_ARG, "state_ml and state_o go together");
-  CombineArgs a{part_ml, part_o, num_parts, seq_lens, blocks_per_split, out, state_ml, state_o};
+  CombineArgs a{part_ml, part_o, num_parts, seq_lens, blocks_per_split, out, state_ml, state_o, 0, 0,
+                num_parts * (seq_lens ? blocks_per_split : 1) * kBlock};
   combine_kernel<<<batch, kHq * kDim, 0, static_cast<cudaStream_t>(stream)>>>(a);
   return launch_status("combine_kernel");
+}
+
+extern "C" int b2_decode_step_counters(int32_t batch) { return batch < 0 ? 0 : 2; }
+
+extern "C" int b2_decode_step(const uint16_t *qkv, int64_t row_stride, const uint16_t *gamma_q,
+                              const uint16_t *gamma_k, float eps, const uint16_t *rope_cos,
+                              const uint16_t *rope_sin, int32_t rope_rows, const int32_t *past_lens,
+                              const int32_t *block_tables, int32_t max_blocks_per_seq, uint16_t *k_pool,
+                              uint16_t *v_pool, int32_t num_blocks, int32_t batch, int32_t blocks_per_split,
+                              float scale, int32_t mode, uint16_t *out, uint16_t *q_out, float *part_ml,
+                              float *part_o, int32_t *counters, int32_t max_ctas, int32_t *dev_err,
+                              void *stream) {
+  if (batch < 0) return fail(B2_ERR_ARG, "batch must be >= 0 (got %d)", batch);
+  if (batch == 0) return ok();
+  if (!qkv || !past_lens || !block_tables || !k_pool || !v_pool || !out || !part_ml || !part_o || !counters ||
+      !dev_err)
+    return fail(B2_ERR_ARG, "null pointer argument");
+  if (mode & ~(B2_NORM_QK | B2_ROPE_QK | B2_STORE_KV)) return fail(B2_ERR_ARG, "unknown mode bits 0x%x", mode);
+  if (row_stride < kQkvWidth || row_stride % 8 != 0)
+    return fail(B2_ERR_ARG, "row_stride must be >= %d and a multiple of 8", kQkvWidth);
+  if (!aligned16(qkv) || !aligned16(out) || (q_out && !aligned16(q_out)) || !aligned16(k_pool) ||
+      !aligned16(v_pool))
+    return fail(B2_ERR_ARG, "qkv, out, q_out and the pools must be 16-byte aligned");
+  if ((mode & B2_NORM_QK) && (!gamma_q || !gamma_k || !aligned16(gamma_q) || !aligned16(gamma_k)))
+    return fail(B2_ERR_ARG, "B2_NORM_QK needs 16-byte aligned gamma_q and gamma_k");
+  if ((mode & B2_ROPE_QK) &&
+      (!rope_cos || !rope_sin || rope_rows <= 0 || !aligned16(rope_cos) || !aligned16(rope_sin)))
+    return fail(B2_ERR_ARG, "B2_ROPE_QK needs 16-byte aligned cos/sin tables with rope_rows > 0");
+  if (num_blocks <= 0 || static_cast<int64_t>(num_blocks) * kHkv * kBlock >= (int64_t(1) << 31))
+    return fail(B2_ERR_ARG, "num_blocks must be in [1, 2^22) (got %d)", num_blocks);
+  if (max_blocks_per_seq <= 0) return fail(B2_ERR_ARG, "max_blocks_per_seq must be positive");
+  if (blocks_per_split < 1 || blocks_per_split > 32)
+    return fail(B2_ERR_ARG, "blocks_per_split must be in [1, 32] (got %d)", blocks_per_split);
+  if (!(scale > 0.f)) return fail(B2_ERR_ARG, "scale must be positive");
+  const int64_t splits = (static_cast<int64_t>(max_blocks_per_seq) + blocks_per_split - 1) / blocks_per_split;
+  const int64_t total = splits * batch * kHkv;
+  if (total >= (int64_t(1) << 31)) return fail(B2_ERR_ARG, "too many work items");
+  CUtensorMap mk, mv;
+  int rc = make_pool_map(&mk, k_pool, num_blocks);
+  if (rc) return rc;
+  rc = make_pool_map(&mv, v_pool, num_blocks);
+  if (rc) return rc;
+  if (!step_smem_ready()) return fail(B2_ERR_CUDA, "cannot set the decode-step kernel's shared memory size");
+  StepArgs a{qkv, row_stride, gamma_q, gamma_k, eps, rope_cos, rope_sin, rope_rows, past_lens, block_tables,
+             max_blocks_per_seq, k_pool, v_pool, num_blocks, batch, blocks_per_split, static_cast<int>(splits),
+             static_cast<int>(total), scale * 1.4426950408889634f, mode, out, q_out, part_ml, part_o, counters,
+             dev_err};
+  int64_t ctas = static_cast<int64_t>(sm_count()) * 3;
+  if (max_ctas > 0 && max_ctas < ctas) ctas = max_ctas;
+  if (ctas > total) ctas = total;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  decode_step_kernel<<<static_cast<unsigned>(ctas), kDecodeThreads, kStepSmem, st>>>(mk, mv, a);
+  rc = launch_status("decode_step_kernel");
+  if (rc) return rc;
+  // Merge the split sequences; launched as a programmatic dependent so that
+  // its launch overlaps the decode kernel's last CTAs.
+  CombineArgs c{part_ml, part_o, static_cast<int>(splits), past_lens, blocks_per_split, out, nullptr, nullptr,
+                1, 1, static_cast<int>(splits) * blocks_per_split * kBlock};
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(batch));
+  cfg.blockDim = dim3(kHq * kDim);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, combine_kernel, c) != cudaSuccess) {
+    const cudaError_t e = cudaGetLastError();
+    return fail(B2_ERR_CUDA, "combine_kernel launch failed: %s", cudaGetErrorString(e));
+  }
+  return launch_status("combine_kernel (decode step)");
 }
 
 // ------------------------------------------------------------------ allocation-free decode
@@ -768,7 +1335,8 @@ extern "C" int b2_decode_attn_noalloc(const uint16_t *q, const uint16_t *k_pool,
   paged_decode_kernel<<<dim3(static_cast<unsigned>(splits), kHkv, batch), kDecodeThreads, kDecodeSmem, s>>>(mk, mv, a);
   rc = launch_status("paged_decode_kernel (noalloc)");
   if (rc) return rc;
-  CombineArgs c{part_ml, part_o, static_cast<int>(splits), seq_lens, blocks_per_split, out, nullptr, nullptr};
+  CombineArgs c{part_ml, part_o, static_cast<int>(splits), seq_lens, blocks_per_split, out, nullptr, nullptr,
+                0, 0, static_cast<int>(splits) * blocks_per_split * kBlock};
   combine_kernel<<<batch, kHq * kDim, 0, s>>>(c);
   return launch_status("combine_kernel (noalloc)");
 }

@@ -132,14 +132,16 @@ def test_append_with_norm_matches_oracle(cuda):
         assert (d == 0).mean() >= 0.99, f"{name}: exact fraction {(d == 0).mean():.4f}"
 
 
+@pytest.mark.parametrize("fused", [True, False], ids=["fused", "three_kernels"])
 @pytest.mark.parametrize("bps", [1, 2, 3, 16])
-def test_decode_ragged_vs_oracle(cuda, bps):
+def test_decode_ragged_vs_oracle(cuda, bps, fused):
     lengths = [1, 2, 63, 64, 65, 127, 128, 129, 1000, 4097]
     cache, hist = build_batch([n - 1 for n in lengths], cuda, seed=3)
     b = len(lengths)
     w = orc.attention_weights(0)
     raw = rand_qkv(b, 13)
-    runner = _attn().PagedDecodeAttention(cache, w["q_gamma"], w["k_gamma"], b, 8192, blocks_per_split=bps)
+    runner = _attn().PagedDecodeAttention(cache, w["q_gamma"], w["k_gamma"], b, 8192, blocks_per_split=bps,
+                                          fused=fused)
     past = torch.tensor([n - 1 for n in lengths], dtype=torch.int32, device=cuda)
     out = runner.step(0, raw.to(cuda), past, past + 1, cache.block_tables())
     torch.cuda.synchronize()
@@ -149,11 +151,13 @@ def test_decode_ragged_vs_oracle(cuda, bps):
         check_close(out[i], ctx, f"seq {i} len {n} bps {bps}")
 
 
-def test_bad_block_is_flagged_not_faulted(cuda):
+@pytest.mark.parametrize("fused", [True, False], ids=["fused", "three_kernels"])
+def test_bad_block_is_flagged_not_faulted(cuda, fused):
     lengths = [100, 200]
     cache, _ = build_batch(lengths, cuda, seed=4)
     w = orc.attention_weights(0)
-    runner = _attn().PagedDecodeAttention(cache, w["q_gamma"], w["k_gamma"], 2, 1024, blocks_per_split=2)
+    runner = _attn().PagedDecodeAttention(cache, w["q_gamma"], w["k_gamma"], 2, 1024, blocks_per_split=2,
+                                          fused=fused)
     tables = cache.block_tables()
     tables[1, 1] = cache.num_blocks + 5   # outside the pool
     past = torch.tensor(lengths, dtype=torch.int32, device=cuda)
@@ -168,10 +172,12 @@ def test_bad_block_is_flagged_not_faulted(cuda):
     runner.check()
 
 
-def test_length_beyond_table_is_flagged(cuda):
+@pytest.mark.parametrize("fused", [True, False], ids=["fused", "three_kernels"])
+def test_length_beyond_table_is_flagged(cuda, fused):
     cache, _ = build_batch([10], cuda, seed=5, capacity=64)
     w = orc.attention_weights(0)
-    runner = _attn().PagedDecodeAttention(cache, w["q_gamma"], w["k_gamma"], 1, 1024, blocks_per_split=1)
+    runner = _attn().PagedDecodeAttention(cache, w["q_gamma"], w["k_gamma"], 1, 1024, blocks_per_split=1,
+                                          fused=fused)
     past = torch.tensor([64], dtype=torch.int32, device=cuda)   # slot 64 is past the 1-block table
     runner.step(0, rand_qkv(1, 15).to(cuda), past, past + 1, cache.block_tables())
     torch.cuda.synchronize()
@@ -195,3 +201,62 @@ def test_host_rejects_bad_arguments(cuda):
     with pytest.raises(lib.B2Error):
         attn.decode_attn(q, kp, vp, cache.block_tables(), seq, blocks_per_split=1,
                          part_ml=ml, part_o=po, dev_err=err, scale=-1.0)
+
+
+@pytest.mark.parametrize("max_ctas", [1, 3, 0])
+def test_fused_step_equals_three_kernels(cuda, max_ctas):
+    """The fused persistent kernel performs the same arithmetic as
+    append + decode + combine: outputs, pools and q must be bit-identical,
+    whatever the number of CTAs sharing the work; the arrival and work
+    counters are back to zero after every call."""
+    lengths = [0, 5, 63, 64, 200, 1000, 3000, 64 * 20 - 1]
+    b = len(lengths)
+    w = orc.attention_weights(0)
+    outs = []
+    for fused in (False, True):
+        cache, _ = build_batch(lengths, cuda, seed=8, capacity=64 * 50)
+        runner = _attn().PagedDecodeAttention(cache, w["q_gamma"], w["k_gamma"], b, 4096, blocks_per_split=4,
+                                              fused=fused, max_ctas=max_ctas)
+        past = torch.tensor(lengths, dtype=torch.int32, device=cuda)
+        res = []
+        for step in range(3):   # three consecutive decode steps
+            o = runner.step(0, rand_qkv(b, 30 + step).to(cuda), past + step, past + step + 1, cache.block_tables())
+            res.append(o.clone())
+        torch.cuda.synchronize()
+        runner.check()
+        if fused:
+            assert int(runner.counters.abs().sum().item()) == 0
+        outs.append((res, runner.q.clone(), cache.k.clone(), cache.v.clone()))
+    (r0, q0, k0, v0), (r1, q1, k1, v1) = outs
+    for a, c in zip(r0, r1):
+        assert torch.equal(a, c)
+    assert torch.equal(q0, q1)
+    assert torch.equal(k0.nan_to_num(7.0), k1.nan_to_num(7.0))
+    assert torch.equal(v0.nan_to_num(7.0), v1.nan_to_num(7.0))
+
+
+def test_fused_multi_step_decode_vs_oracle(cuda):
+    """Eight consecutive decode steps crossing a block edge, each attending
+    over the tokens appended by the previous steps."""
+    lengths = [60, 127, 2]
+    cache, hist = build_batch(lengths, cuda, seed=9, capacity=200)
+    b = len(lengths)
+    w = orc.attention_weights(0)
+    runner = _attn().PagedDecodeAttention(cache, w["q_gamma"], w["k_gamma"], b, 4096, blocks_per_split=1)
+    ks = [h[0] for h in hist]
+    vs = [h[1] for h in hist]
+    for step in range(8):
+        raw = rand_qkv(b, 50 + step)
+        past = torch.tensor([n + step for n in lengths], dtype=torch.int32, device=cuda)
+        out = runner.step(0, raw.to(cuda), past, past + 1, cache.block_tables())
+        torch.cuda.synchronize()
+        runner.check()
+        for i, n in enumerate(lengths):
+            ctx, k_all, v_all, _ = orc.decode_step(raw[i], ks[i], vs[i], n + step, w["q_gamma"], w["k_gamma"])
+            check_close(out[i], ctx, f"step {step} seq {i}")
+            # carry the GPU's appended k (which may differ by 1 ulp in rare
+            # norm cases) so the histories stay identical
+            kd, vd = cache.read_dense(0, i, n + step + 1)
+            ks[i] = kd.cpu()
+            vs[i] = vd.cpu()
+            assert torch.equal(vs[i], v_all)
