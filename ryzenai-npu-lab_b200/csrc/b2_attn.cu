@@ -825,40 +825,73 @@ __device__ __forceinline__ void step_producer(const StepArgs &a, StepTail *tail,
   }
 }
 
-// End of an item: merge lanes, then the 4 warps, into the item's state.  A
-// whole-sequence item writes the context; otherwise the partial state goes
-// to part_ml/part_o for the combine kernel that follows.  red[] is
-// double-buffered by epilogue parity, so a single barrier separates its
-// writes from its reads and the next epilogue cannot overwrite it early.
+// ---- warp-level tensor-core helpers (mma.sync m16n8k16 bf16 -> fp32)
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void mma_bf16(float c[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) { return bf16_bits(lo) | (bf16_bits(hi) << 16); }
+
+// Zero the bf16 halves of a fragment register whose token index is >= valid.
+__device__ __forceinline__ uint32_t mask_pair(uint32_t v, int tok, int valid) {
+  const uint32_t lo = tok < valid ? 0x0000ffffu : 0u;
+  const uint32_t hi = tok + 1 < valid ? 0xffff0000u : 0u;
+  return v & (lo | hi);
+}
+
+// End of an item: merge the 4 warps' states (max and sum per head, output in
+// the accumulator layout below).  A whole-sequence item writes the context;
+// otherwise the partial state goes to part_ml/part_o for the combine kernel
+// that follows.  red[] is double-buffered by epilogue parity, so a single
+// barrier separates its writes from its reads and the next epilogue cannot
+// overwrite it early.
 __device__ __forceinline__ void step_epilogue(const StepArgs &a, StepTail *tail, int warp, int lane, int b,
                                               int kvh, int split, bool final_item, float m0, float m1,
-                                              float lsum, float acc0[8], float acc1[8], uint32_t &ephase,
+                                              float l0, float l1, const float o[4][4], uint32_t &ephase,
                                               int rbuf) {
   float(*red)[2][2 + kDim] = tail->red[rbuf];
 #pragma unroll
-  for (int off = 2; off < 32; off <<= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, off);
-#pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    acc0[e] += __shfl_xor_sync(0xffffffffu, acc0[e], 8);
-    acc0[e] += __shfl_xor_sync(0xffffffffu, acc0[e], 16);
-    acc1[e] += __shfl_xor_sync(0xffffffffu, acc1[e], 8);
-    acc1[e] += __shfl_xor_sync(0xffffffffu, acc1[e], 16);
+  for (int off = 4; off < 32; off <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, off);
   }
-  const int c = lane & 7;
-  if (lane < 8) {
+  const int g = lane >> 2, t = lane & 3;
+  if (t == 0) {
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      red[warp][0][2 + c * 8 + e] = acc0[e];
-      red[warp][1][2 + c * 8 + e] = acc1[e];
+    for (int mt = 0; mt < 4; ++mt) {
+      red[warp][0][2 + 16 * mt + g] = o[mt][0];
+      red[warp][1][2 + 16 * mt + g] = o[mt][1];
+      red[warp][0][2 + 16 * mt + g + 8] = o[mt][2];
+      red[warp][1][2 + 16 * mt + g + 8] = o[mt][3];
     }
   }
-  if (lane < 2) {
-    red[warp][lane][0] = lane ? m1 : m0;
-    red[warp][lane][1] = lsum;
+  if (lane == 0) {
+    red[warp][0][0] = m0;
+    red[warp][0][1] = l0;
+    red[warp][1][0] = m1;
+    red[warp][1][1] = l1;
   }
   consumers_sync(tail, lane, ephase, a.err);
-  const int t = threadIdx.x;  // 0..127
-  const int h = t >> 6, d = t & 63;
+  const int tid = threadIdx.x;  // 0..127
+  const int h = tid >> 6, d = tid & 63;
   float M = -1.0e30f;
 #pragma unroll
   for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, red[w][h][0]);
@@ -878,6 +911,136 @@ __device__ __forceinline__ void step_epilogue(const StepArgs &a, StepTail *tail,
   if (d == 0) {
     a.part_ml[idx * 2] = M;
     a.part_ml[idx * 2 + 1] = L;
+  }
+}
+
+// Consumer warp w owns token rows [16w, 16w+16) of every 64-token tile.  Both
+// products run on the tensor cores with mma.sync m16n8k16 (bf16 in, fp32
+// accumulate), operands fetched from the 128-byte-swizzled tiles with
+// ldmatrix; the N = 8 side carries the 2 query heads of the GQA pair (6
+// columns are zero):
+//   S[16 x 8]  = K_rows[16 x 64] . Q^T[64 x 8]             (4 k-steps)
+//   O^T[64 x 8] += V_rows^T[64 x 16] . P^T[16 x 8]           (4 m-tiles)
+// Online softmax in fp32 (log2 units); P is rounded to bf16 for the second
+// product, as the reference's eager path rounds its probabilities.  Lane
+// (g, t) = (lane / 4, lane % 4): scores of rows g and g+8 for both heads live
+// in lanes with t == 0; the output accumulator o[mt] holds dims 16mt+g and
+// 16mt+g+8 (heads 2t, 2t+1: only t == 0 carries real heads).
+__device__ __forceinline__ void step_consumer(const StepArgs &a, StepTail *tail, const uint8_t *tiles, int warp,
+                                              int lane) {
+  const int g = lane >> 2, t = lane & 3;
+  const int j = lane >> 3;  // ldmatrix sub-matrix this lane addresses
+  uint32_t bq[4][2];        // Q^T fragments of the current item
+  float m0 = -1.0e30f, m1 = -1.0e30f, l0 = 0.f, l1 = 0.f;
+  float o[4][4];
+#pragma unroll
+  for (int mt = 0; mt < 4; ++mt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[mt][e] = 0.f;
+#pragma unroll
+  for (int ks = 0; ks < 4; ++ks) bq[ks][0] = bq[ks][1] = 0u;
+  uint32_t ephase = 0;  // completed phases of the epilogue barrier
+  int epilogues = 0;    // red[] buffer parity
+  // ldmatrix row addresses (without the stage base): rows of this lane's
+  // sub-matrix, the 16-byte chunk index is added per k-step / m-tile.
+  const int qk_row = 16 * warp + (lane & 7) + 8 * (j & 1);
+  const int pv_row = 16 * warp + (lane & 7) + 8 * (j >> 1);
+  for (int it = 0;; ++it) {
+    const int s = it % kStages;
+    const uint32_t ph = (it / kStages) & 1;
+    if (!mbar_wait(smem_u32(&tail->full[s]), ph)) {
+      if (lane == 0) atomicOr(a.err, B2_DEV_TIMEOUT);
+      break;
+    }
+    const StageMeta &meta = tail->meta[s];
+    const int flags = meta.flags;
+    if (flags & kFlagEnd) break;
+    const int b = meta.b, kvh = meta.kvh, split = meta.split;
+    const int valid = meta.rows - 16 * warp;  // valid rows of this warp (may be <= 0 or >= 16)
+    if (flags & kFlagFirst) {
+      // B fragment of Q^T: (k = 2t, 2t+1 | 2t+8, 2t+9 of the k-step, n = g)
+      // = q[head g][16ks + ...] for g < 2, zero for the padding columns.
+      const uint32_t *q32 = reinterpret_cast<const uint32_t *>(meta.q);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        bq[ks][0] = g < 2 ? q32[(g * kDim + 16 * ks + 2 * t) >> 1] : 0u;
+        bq[ks][1] = g < 2 ? q32[(g * kDim + 16 * ks + 2 * t + 8) >> 1] : 0u;
+      }
+      m0 = m1 = -1.0e30f;
+      l0 = l1 = 0.f;
+#pragma unroll
+      for (int mt = 0; mt < 4; ++mt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[mt][e] = 0.f;
+    }
+    const uint32_t kt = smem_u32(tiles + s * kStageBytes);
+    const uint32_t vt = kt + kTileBytes;
+
+    // S = K . Q^T
+    float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      const int chunk = 2 * ks + (j >> 1);
+      uint32_t a0, a1, a2, a3;
+      ldsm_x4(kt + qk_row * 128 + ((chunk ^ (qk_row & 7)) << 4), a0, a1, a2, a3);
+      mma_bf16(c, a0, a1, a2, a3, bq[ks][0], bq[ks][1]);
+    }
+    // online softmax over this warp's 16 rows (rows >= valid masked)
+    const bool head_lane = t == 0;
+    const float s00 = head_lane && g < valid ? c[0] * a.scale_log2 : -INFINITY;      // row g,   head 0
+    const float s01 = head_lane && g < valid ? c[1] * a.scale_log2 : -INFINITY;      // row g,   head 1
+    const float s10 = head_lane && g + 8 < valid ? c[2] * a.scale_log2 : -INFINITY;  // row g+8, head 0
+    const float s11 = head_lane && g + 8 < valid ? c[3] * a.scale_log2 : -INFINITY;  // row g+8, head 1
+    float bm0 = fmaxf(s00, s10), bm1 = fmaxf(s01, s11);
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      bm0 = fmaxf(bm0, __shfl_xor_sync(0xffffffffu, bm0, off));
+      bm1 = fmaxf(bm1, __shfl_xor_sync(0xffffffffu, bm1, off));
+    }
+    const float mn0 = fmaxf(m0, bm0), mn1 = fmaxf(m1, bm1);
+    const float a0s = ex2(m0 - mn0), a1s = ex2(m1 - mn1);
+    m0 = mn0;
+    m1 = mn1;
+    const float p00 = ex2(s00 - mn0), p10 = ex2(s10 - mn0);
+    const float p01 = ex2(s01 - mn1), p11 = ex2(s11 - mn1);
+    l0 = fmaf(l0, a0s, p00 + p10);
+    l1 = fmaf(l1, a1s, p01 + p11);
+#pragma unroll
+    for (int mt = 0; mt < 4; ++mt) {
+      o[mt][0] *= a0s;
+      o[mt][1] *= a1s;
+      o[mt][2] *= a0s;
+      o[mt][3] *= a1s;
+    }
+    // P^T as the B fragment: (k = tokens 2t, 2t+1 | 2t+8, 2t+9, n = head g)
+    const uint32_t pk0 = pack_bf16x2(p00, p01);  // row g:   (head 0, head 1)
+    const uint32_t pk1 = pack_bf16x2(p10, p11);  // row g+8
+    const uint32_t v0 = __shfl_sync(0xffffffffu, pk0, 8 * t);
+    const uint32_t v1 = __shfl_sync(0xffffffffu, pk0, 8 * t + 4);
+    const uint32_t v2 = __shfl_sync(0xffffffffu, pk1, 8 * t);
+    const uint32_t v3 = __shfl_sync(0xffffffffu, pk1, 8 * t + 4);
+    const uint32_t sel = g == 0 ? 0x5410u : 0x7632u;
+    const uint32_t bp0 = g < 2 ? __byte_perm(v0, v1, sel) : 0u;
+    const uint32_t bp1 = g < 2 ? __byte_perm(v2, v3, sel) : 0u;
+    // O^T += V^T . P^T
+#pragma unroll
+    for (int mt = 0; mt < 4; ++mt) {
+      const int chunk = 2 * mt + (j & 1);
+      uint32_t a0, a1, a2, a3;
+      ldsm_x4_t(vt + pv_row * 128 + ((chunk ^ (pv_row & 7)) << 4), a0, a1, a2, a3);
+      if (valid < 16) {  // stale or NaN rows past the end must not meet P = 0
+        a0 = mask_pair(a0, 2 * t, valid);
+        a1 = mask_pair(a1, 2 * t, valid);
+        a2 = mask_pair(a2, 2 * t + 8, valid);
+        a3 = mask_pair(a3, 2 * t + 8, valid);
+      }
+      mma_bf16(o[mt], a0, a1, a2, a3, bp0, bp1);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(&tail->empty[s]));
+    if (flags & kFlagLast)
+      step_epilogue(a, tail, warp, lane, b, kvh, split, (flags & kFlagFinal) != 0, m0, m1, l0, l1, o, ephase,
+                    (epilogues++) & 1);
   }
 }
 
@@ -904,101 +1067,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 3)
   // it waits for this grid's completion before reading the partial states.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
-  if (warp == kConsumerWarps) {
+  if (warp == kConsumerWarps)
     step_producer(a, tail, tiles, &tm_k, &tm_v, lane);
-  } else {
-    const int r = lane >> 1, half = lane & 1;
-    const int c = lane & 7, g = lane >> 3;
-    const int qrow = 16 * warp + r;
-    float q0[32], q1[32];
-    float m0 = -1.0e30f, m1 = -1.0e30f, lsum = 0.f;
-    float acc0[8], acc1[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) acc0[e] = acc1[e] = 0.f;
-    uint32_t ephase = 0;  // completed phases of the epilogue barrier
-    int epilogues = 0;    // red[] buffer parity
-    for (int it = 0;; ++it) {
-      const int s = it % kStages;
-      const uint32_t ph = (it / kStages) & 1;
-      if (!mbar_wait(smem_u32(&tail->full[s]), ph)) {
-        if (lane == 0) atomicOr(a.err, B2_DEV_TIMEOUT);
-        break;
-      }
-      const StageMeta &meta = tail->meta[s];
-      const int flags = meta.flags;
-      if (flags & kFlagEnd) break;
-      const int b = meta.b, kvh = meta.kvh, split = meta.split;
-      const int valid = meta.rows - 16 * warp;
-      if (flags & kFlagFirst) {
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          unpack8(*reinterpret_cast<const uint4 *>(meta.q + half * 32 + k * 8), q0 + k * 8);
-          unpack8(*reinterpret_cast<const uint4 *>(meta.q + kDim + half * 32 + k * 8), q1 + k * 8);
-        }
-        m0 = m1 = -1.0e30f;
-        lsum = 0.f;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc0[e] = acc1[e] = 0.f;
-      }
-      const uint8_t *kt = tiles + s * kStageBytes;
-      const uint8_t *vt = kt + kTileBytes;
-      float d0 = 0.f, d1 = 0.f;
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int pc = (half * 4 + k) ^ (qrow & 7);
-        float f[8];
-        unpack8(*reinterpret_cast<const uint4 *>(kt + qrow * 128 + pc * 16), f);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          d0 = fmaf(q0[k * 8 + e], f[e], d0);
-          d1 = fmaf(q1[k * 8 + e], f[e], d1);
-        }
-      }
-      d0 += __shfl_xor_sync(0xffffffffu, d0, 1);
-      d1 += __shfl_xor_sync(0xffffffffu, d1, 1);
-      const bool tv = r < valid;
-      const float s0 = tv ? d0 * a.scale_log2 : -INFINITY;
-      const float s1 = tv ? d1 * a.scale_log2 : -INFINITY;
-      float bm0 = s0, bm1 = s1;
-#pragma unroll
-      for (int off = 2; off < 32; off <<= 1) {
-        bm0 = fmaxf(bm0, __shfl_xor_sync(0xffffffffu, bm0, off));
-        bm1 = fmaxf(bm1, __shfl_xor_sync(0xffffffffu, bm1, off));
-      }
-      const float mn0 = fmaxf(m0, bm0), mn1 = fmaxf(m1, bm1);
-      const float a0 = ex2(m0 - mn0), a1 = ex2(m1 - mn1);
-      m0 = mn0;
-      m1 = mn1;
-      const float p = ex2((half ? s1 : s0) - (half ? mn1 : mn0));
-      lsum = fmaf(lsum, half ? a1 : a0, p);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        acc0[e] *= a0;
-        acc1[e] *= a1;
-      }
-#pragma unroll
-      for (int jj = 0; jj < 4; ++jj) {
-        const int t = 4 * g + jj;
-        const float p0 = __shfl_sync(0xffffffffu, p, 2 * t);
-        const float p1 = __shfl_sync(0xffffffffu, p, 2 * t + 1);
-        if (t < valid) {
-          const int vrow = 16 * warp + t;
-          float f[8];
-          unpack8(*reinterpret_cast<const uint4 *>(vt + vrow * 128 + ((c ^ (vrow & 7)) * 16)), f);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            acc0[e] = fmaf(p0, f[e], acc0[e]);
-            acc1[e] = fmaf(p1, f[e], acc1[e]);
-          }
-        }
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&tail->empty[s]));
-      if (flags & kFlagLast)
-        step_epilogue(a, tail, warp, lane, b, kvh, split, (flags & kFlagFinal) != 0, m0, m1, lsum, acc0, acc1,
-                      ephase, (epilogues++) & 1);
-    }
-  }
+  else
+    step_consumer(a, tail, tiles, warp, lane);
   __syncthreads();
   if (threadIdx.x == 0) {
     // The last CTA to finish resets the work counter for the next launch.

@@ -204,11 +204,13 @@ def test_host_rejects_bad_arguments(cuda):
 
 
 @pytest.mark.parametrize("max_ctas", [1, 3, 0])
-def test_fused_step_equals_three_kernels(cuda, max_ctas):
-    """The fused persistent kernel performs the same arithmetic as
-    append + decode + combine: outputs, pools and q must be bit-identical,
-    whatever the number of CTAs sharing the work; the arrival and work
-    counters are back to zero after every call."""
+def test_fused_step_matches_three_kernels(cuda, max_ctas):
+    """The fused persistent kernel against append + decode + combine: the
+    appended pools and q are bit-identical (same norm/RoPE arithmetic), the
+    contexts agree within the attention tolerance (the fused kernel's
+    products run on the tensor cores with bf16 probabilities), whatever the
+    number of CTAs sharing the work; the work counters are back to zero after
+    every call."""
     lengths = [0, 5, 63, 64, 200, 1000, 3000, 64 * 20 - 1]
     b = len(lengths)
     w = orc.attention_weights(0)
@@ -228,8 +230,8 @@ def test_fused_step_equals_three_kernels(cuda, max_ctas):
             assert int(runner.counters.abs().sum().item()) == 0
         outs.append((res, runner.q.clone(), cache.k.clone(), cache.v.clone()))
     (r0, q0, k0, v0), (r1, q1, k1, v1) = outs
-    for a, c in zip(r0, r1):
-        assert torch.equal(a, c)
+    for step, (a, c) in enumerate(zip(r0, r1)):
+        check_close(c, a, f"step {step}")
     assert torch.equal(q0, q1)
     assert torch.equal(k0.nan_to_num(7.0), k1.nan_to_num(7.0))
     assert torch.equal(v0.nan_to_num(7.0), v1.nan_to_num(7.0))
