@@ -62,6 +62,9 @@ def parse():
     p.add_argument("--three-kernels", action="store_true",
                    help="run append, decode and combine as three launches instead of the fused kernel")
     p.add_argument("--max-ctas", type=int, default=0, help="cap on the fused kernel's persistent grid")
+    p.add_argument("--config", choices=["c3", "c4"], default="c3",
+                   help="c3: batched paged decode (default); c4: one long sequence split over the GPUs")
+    p.add_argument("--context", type=int, default=131072, help="c4: cached tokens of the sequence")
     return p.parse_args()
 
 
@@ -414,6 +417,95 @@ def run_b200(args):
         torch.distributed.destroy_process_group()
 
 
+def run_c4(args):
+    """Config C4: one sequence of --context cached tokens split along the token
+    axis over the ranks; per step each rank appends (last rank) and attends over
+    its tokens, the partial states are all-gathered (NCCL) and merged."""
+    import datetime
+    world, rank, local = dist_env()
+    if "RANK" not in os.environ:   # single process without torchrun: a world of one
+        import socket
+        with socket.socket() as sock:
+            sock.bind(("127.0.0.1", 0))
+            port = sock.getsockname()[1]
+        os.environ.update(RANK="0", WORLD_SIZE="1", LOCAL_RANK="0", MASTER_ADDR="127.0.0.1",
+                          MASTER_PORT=str(port))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    torch.distributed.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    dmod = importlib.import_module(PKG + ".distributed")
+    K, W = args.steps, args.warmup
+    gg = torch.Generator().manual_seed(args.seed + 31)
+    gamma_q = (1.0 + 0.1 * torch.randn(D, generator=gg)).to(torch.bfloat16)
+    gamma_k = (1.0 + 0.1 * torch.randn(D, generator=gg)).to(torch.bfloat16)
+    lc = dmod.LongContextDecode(args.context + 1, gamma_q, gamma_k, device=dev,
+                                blocks_per_split=args.bps or None, growth=64)
+    gen = torch.Generator(device=dev).manual_seed(args.seed * 1000 + rank + 29)
+    lc.fill_random(args.context, gen)
+    lc.set_lengths(args.context)
+    qkv = (torch.randn(8, 1, 2048, generator=gen, device=dev) * 0.6).to(torch.bfloat16)
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        for j in range(max(W, 1)):
+            lc.step(qkv[j % 8])
+    stream.synchronize()
+    lc.check()
+    ev0 = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(K)]
+    ev1 = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(K)]
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for j in range(K):
+            ev0[j].record()
+            lc.partial(qkv[j % 8])
+            ev1[j].record()
+            lc.merge()
+    graph.replay()
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    torch.distributed.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        with torch.cuda.stream(stream):
+            t0.record()
+            graph.replay()
+            t1.record()
+        torch.cuda.synchronize()
+    torch.distributed.barrier()
+    lc.check()
+    ms = t0.elapsed_time(t1)
+    part_ms = sum(a.elapsed_time(b) for a, b in zip(ev0, ev1)) / K
+    local_tokens = lc.local_len + (1 if lc.is_tail else 0)
+    local_bytes = KV_BYTES_PER_TOKEN * local_tokens + 2048 * 2 + 2 * 1024
+    times = torch.tensor([ms, part_ms], dtype=torch.float64, device=dev)
+    torch.distributed.all_reduce(times, op=torch.distributed.ReduceOp.MAX)
+    ms, part_ms = times.tolist()
+    peak, peak_kind = measured_hbm_peak()
+    total_bytes = KV_BYTES_PER_TOKEN * (args.context + 1) + 2048 * 2 + 2 * 1024
+    line = {
+        "metric": METRIC, "value": K / (ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": K,
+        "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"C4 long-context decode: one sequence of {args.context} cached tokens "
+                               f"split along the token axis over {world} GPU(s), partial states "
+                               f"all-gathered over NCCL and merged", "context": args.context,
+                   "global_batch": 1, "blocks_per_split": lc.bps, "parallelism": f"split-kv x{world}",
+                   "l2": "inputs larger than L2 (268 MB of K/V), no flush"},
+        "hbm_gbs_aggregate": total_bytes / (ms / K / 1e3) / 1e9,
+        "roofline": {"bound": "hbm", "kernel": "paged_decode_kernel (+append, local merge)",
+                     "achieved": local_bytes / (part_ms / 1e3) / 1e9, "peak": peak, "peak_source": peak_kind,
+                     "unit": "GB/s", "frac": local_bytes / (part_ms / 1e3) / 1e9 / peak, "traffic": None,
+                     "algorithmic_bytes": local_bytes, "avg_launch_ms": part_ms},
+        "clocks": clocks.summary(),
+        "gpu_launches": K * 3,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    del graph
+    torch.distributed.barrier()
+    torch.distributed.destroy_process_group()
+
+
 def main():
     args = parse()
     world, _, _ = dist_env()
@@ -422,6 +514,8 @@ def main():
             raise SystemExit("--gpus N > 1 must be launched with torchrun (one process per GPU)")
     if args.impl == "reference":
         run_reference(args)
+    elif args.config == "c4":
+        run_c4(args)
     else:
         run_b200(args)
 

@@ -169,12 +169,21 @@ int b2_combine(const float *part_ml, const float *part_o, int32_t num_parts,
  * part_ml/part_o that a second, small kernel (launched by this call as a
  * programmatic dependent) merges into out.
  *
+ * seq_lens     NULL: attend over past_lens[b] + 1 tokens (the usual decode
+ *              step).  Otherwise tokens attended per sequence; with
+ *              B2_STORE_KV it must equal past_lens[b] + 1, without it
+ *              past_lens[b] is only the RoPE position (a GPU that holds a
+ *              slice of a long sequence's tokens, see b2_combine).
+ * out          bf16 [batch][16][64] context, or NULL when state_ml/state_o
+ *              (fp32 [batch][16][2] / [batch][16][64], as b2_combine) are
+ *              given: the merged state of the attended tokens, for a
+ *              further merge across GPUs.
  * counters     int32 [b2_decode_step_counters(batch)] (= 2); must be zero
  *              before the first call; every call that completes leaves it
  *              zero again (after a device error, zero it again).
  * part_ml/o    as b2_decode_attn with num_splits = ceil(max_blocks / bps).
  * blocks_per_split  1 .. 32.
- * out          bf16 [batch][16][64]; q_out optional bf16 [batch][16][64].
+ * q_out        optional bf16 [batch][16][64] normalised + rotated q.
  * Calls sharing `counters` must not overlap on the GPU.
  */
 int b2_decode_step_counters(int32_t batch);
@@ -182,12 +191,26 @@ int b2_decode_step(const uint16_t *qkv, int64_t row_stride,
                    const uint16_t *gamma_q, const uint16_t *gamma_k, float eps,
                    const uint16_t *rope_cos, const uint16_t *rope_sin,
                    int32_t rope_rows, const int32_t *past_lens,
+                   const int32_t *seq_lens,
                    const int32_t *block_tables, int32_t max_blocks_per_seq,
                    uint16_t *k_pool, uint16_t *v_pool, int32_t num_blocks,
                    int32_t batch, int32_t blocks_per_split, float scale,
                    int32_t mode, uint16_t *out, uint16_t *q_out,
+                   float *state_ml, float *state_o,
                    float *part_ml, float *part_o, int32_t *counters,
                    int32_t max_ctas, int32_t *dev_err, void *stream);
+
+/*
+ * Merge states gathered from several GPUs (config C4: one sequence split
+ * along the token axis).  `states` holds num_parts blocks of
+ * batch * 16 * 66 fp32, each laid out [state_ml batch*16*2 | state_o
+ * batch*16*64] - what b2_decode_step / b2_combine write when state_o =
+ * state_ml + batch * 32, i.e. the buffer one all-gather collects.  Output as
+ * b2_combine (bf16 context and/or a merged state).
+ */
+int b2_merge_states(const float *states, int32_t num_parts, int32_t batch,
+                    uint16_t *out, float *state_ml, float *state_o,
+                    void *stream);
 
 /*
  * Allocation-free decode: b2_decode_attn followed by b2_combine, with the

@@ -66,13 +66,18 @@ SIGNATURES = {
         _p, _i64,            # qkv, row_stride
         _p, _p, _f32,        # gamma_q, gamma_k, eps
         _p, _p, _i32,        # rope_cos, rope_sin, rope_rows
-        _p,                  # past_lens
+        _p, _p,              # past_lens, seq_lens
         _p, _i32,            # block_tables, max_blocks_per_seq
         _p, _p, _i32,        # k_pool, v_pool, num_blocks
         _i32, _i32, _f32,    # batch, blocks_per_split, scale
         _i32, _p, _p,        # mode, out, q_out
+        _p, _p,              # state_ml, state_o
         _p, _p, _p,          # part_ml, part_o, counters
         _i32, _p, _p,        # max_ctas, dev_err, stream
+    ]),
+    "b2_merge_states": (ctypes.c_int, [
+        _p, _i32, _i32,      # states, num_parts, batch
+        _p, _p, _p, _p,      # out, state_ml, state_o, stream
     ]),
     "b2_decode_attn_noalloc": (ctypes.c_int, [
         _p, _p, _p, _i32,    # q, k_pool, v_pool, num_blocks

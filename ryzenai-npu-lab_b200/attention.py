@@ -169,14 +169,17 @@ def combine(part_ml: torch.Tensor, part_o: torch.Tensor, num_parts: int, batch: 
 
 
 def decode_step(qkv: torch.Tensor, past_lens: torch.Tensor, *, k_pool: torch.Tensor, v_pool: torch.Tensor,
-                block_tables: torch.Tensor, blocks_per_split: int, out: torch.Tensor, part_ml: torch.Tensor,
-                part_o: torch.Tensor, counters: torch.Tensor, dev_err: torch.Tensor,
+                block_tables: torch.Tensor, blocks_per_split: int, out: torch.Tensor | None,
+                part_ml: torch.Tensor, part_o: torch.Tensor, counters: torch.Tensor, dev_err: torch.Tensor,
                 gamma_q: torch.Tensor | None = None, gamma_k: torch.Tensor | None = None,
                 cos: torch.Tensor | None = None, sin: torch.Tensor | None = None, q_out: torch.Tensor | None = None,
+                seq_lens: torch.Tensor | None = None, state_ml: torch.Tensor | None = None,
+                state_o: torch.Tensor | None = None,
                 mode: int = _lib.B2_NORM_QK | _lib.B2_ROPE_QK | _lib.B2_STORE_KV, eps: float = EPS,
                 scale: float = SCALE, max_ctas: int = 0, stream: torch.cuda.Stream | None = None) -> int:
     """Fused decode step in one persistent launch (b2_decode_step): norm + RoPE,
-    append at past_lens[b], attention over past_lens[b] + 1 tokens, merge.
+    append at past_lens[b], attention over past_lens[b] + 1 tokens (or
+    seq_lens[b]), merge into `out` or into fp32 states (state_ml, state_o).
     `counters` (int32[2]) must be zero on the first call; the kernel leaves
     it zero.  Returns num_splits."""
     dev = qkv.device
@@ -192,9 +195,15 @@ def decode_step(qkv: torch.Tensor, past_lens: torch.Tensor, *, k_pool: torch.Ten
     _need(block_tables, "block_tables", torch.int32, dev)
     if block_tables.dim() != 2 or block_tables.shape[0] != b:
         raise ValueError("block_tables must be [batch, max_blocks_per_seq]")
-    _need(out, "out", torch.bfloat16, dev)
-    if out.numel() != b * HQ * D:
-        raise ValueError("out must hold batch x 16 x 64 elements")
+    if out is not None:
+        _need(out, "out", torch.bfloat16, dev)
+        if out.numel() != b * HQ * D:
+            raise ValueError("out must hold batch x 16 x 64 elements")
+    if state_o is not None or out is None:
+        _need(state_ml, "state_ml", torch.float32, dev, (b, HQ, 2))
+        _need(state_o, "state_o", torch.float32, dev, (b, HQ, D))
+    if seq_lens is not None:
+        _need(seq_lens, "seq_lens", torch.int32, dev, (b,))
     if q_out is not None:
         _need(q_out, "q_out", torch.bfloat16, dev, (b, HQ, D))
     _need(counters, "counters", torch.int32, dev)
@@ -217,11 +226,33 @@ def decode_step(qkv: torch.Tensor, past_lens: torch.Tensor, *, k_pool: torch.Ten
         raise ValueError(f"partial-state buffers too small for {b} x {splits} splits")
     rc = _lib.load().b2_decode_step(
         _ptr(qkv), qkv.stride(0), _ptr(gamma_q), _ptr(gamma_k), ctypes.c_float(eps), _ptr(cos), _ptr(sin),
-        rope_rows, _ptr(past_lens), _ptr(block_tables), max_blocks, _ptr(k_pool), _ptr(v_pool), k_pool.shape[0],
-        b, blocks_per_split, ctypes.c_float(scale), mode, _ptr(out), _ptr(q_out), _ptr(part_ml), _ptr(part_o),
-        _ptr(counters), max_ctas, _ptr(dev_err), _stream(dev, stream))
+        rope_rows, _ptr(past_lens), _ptr(seq_lens), _ptr(block_tables), max_blocks, _ptr(k_pool), _ptr(v_pool),
+        k_pool.shape[0], b, blocks_per_split, ctypes.c_float(scale), mode, _ptr(out), _ptr(q_out),
+        _ptr(state_ml), _ptr(state_o), _ptr(part_ml), _ptr(part_o), _ptr(counters), max_ctas, _ptr(dev_err),
+        _stream(dev, stream))
     _lib.check(rc, "b2_decode_step")
     return splits
+
+
+def merge_states(states: torch.Tensor, num_parts: int, batch: int, *, out: torch.Tensor | None = None,
+                 state_ml: torch.Tensor | None = None, state_o: torch.Tensor | None = None,
+                 stream: torch.cuda.Stream | None = None) -> None:
+    """Merge states gathered from num_parts GPUs (b2_merge_states): `states`
+    is fp32 [num_parts, batch * 16 * 66], each part [ml batch*16*2 | o batch*16*64]."""
+    dev = states.device
+    _need(states, "states", torch.float32, dev)
+    if states.numel() != num_parts * batch * HQ * (2 + D):
+        raise ValueError("states must hold num_parts x batch x 16 x 66 floats")
+    if out is not None:
+        _need(out, "out", torch.bfloat16, dev)
+        if out.numel() != batch * HQ * D:
+            raise ValueError("out must hold batch x 16 x 64 elements")
+    if state_o is not None:
+        _need(state_ml, "state_ml", torch.float32, dev, (batch, HQ, 2))
+        _need(state_o, "state_o", torch.float32, dev, (batch, HQ, D))
+    rc = _lib.load().b2_merge_states(_ptr(states), num_parts, batch, _ptr(out), _ptr(state_ml), _ptr(state_o),
+                                     _stream(dev, stream))
+    _lib.check(rc, "b2_merge_states")
 
 
 class PagedDecodeAttention:

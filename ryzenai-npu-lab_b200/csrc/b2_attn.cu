@@ -150,7 +150,7 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
                : "memory");
 }
 
-// 2-D tiled TMA load (no multicast) completing on an mbarrier; KV tiles are
+// 2-D tiled TMA load into this CTA alone, completing on an mbarrier; KV tiles are
 // read once per step, so they are marked evict-first in L2.
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y,
                                             uint32_t bar, uint64_t policy) {
@@ -519,16 +519,35 @@ struct CombineArgs {
   int len_offset;   // 1 when seq_lens holds past lengths (the new token is added)
   int skip_single;  // sequences with one part were written by the decode kernel
   int max_tokens;   // num_parts * blocks_per_split * 64: longer lengths are invalid
+  // float strides between sequences (b) and parts (s); 0 = the default
+  // [batch][num_parts][16][2 | 64] layout
+  int64_t ml_b, ml_s, o_b, o_s;
+  int groups;  // part groups per CTA (blockDim.x / 64), 1..16
 };
 
-// grid (batch), block (16 heads x 64 dims); one thread per output element.
+// Part groups for a merge of up to num_parts parts: enough threads to merge
+// hundreds of parts quickly, few for the usual handful (small CTAs launch fast).
+int combine_groups(int num_parts) {
+  int g = 1;
+  while (g < 16 && g * 8 < num_parts) g *= 2;
+  return g;
+}
+
+// grid (batch, 16 heads), block (groups x 64 dims).  Group g merges parts
+// g, g + groups, ... with a running (max, sum, output); the group states
+// are then merged in shared memory, so a sequence split into hundreds of
+// parts is still merged by many threads in one pass.
 // When launched as a programmatic dependent of the decode-step kernel it may
 // start early; griddepcontrol.wait holds it until that kernel has completed
 // and its memory is visible (a no-op for an ordinary launch).
-__global__ void __launch_bounds__(1024) combine_kernel(const CombineArgs a) {
+constexpr int kCombineGroups = 16;
+
+__global__ void __launch_bounds__(kCombineGroups * kDim) combine_kernel(const CombineArgs a) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  __shared__ float sm[kCombineGroups], sl[kCombineGroups], so[kCombineGroups][kDim];
   const int b = blockIdx.x;
-  const int h = threadIdx.x >> 6;
+  const int h = blockIdx.y;
+  const int grp = threadIdx.x >> 6;
   const int d = threadIdx.x & 63;
   int parts = a.num_parts;
   if (a.seq_lens) {
@@ -538,23 +557,44 @@ __global__ void __launch_bounds__(1024) combine_kernel(const CombineArgs a) {
     parts = min(parts, (nblk + a.blocks_per_split - 1) / a.blocks_per_split);
     if (a.skip_single && parts == 1) return;  // written by the decode kernel
   }
-  const float *ml = a.part_ml + ((int64_t)b * a.num_parts * kHq + h) * 2;
-  const float *po = a.part_o + ((int64_t)b * a.num_parts * kHq + h) * kDim + d;
-  float M = -1.0e30f;
-  for (int s = 0; s < parts; ++s) M = fmaxf(M, ml[s * kHq * 2]);
-  float L = 0.f, O = 0.f;
-  for (int s = 0; s < parts; ++s) {
-    const float sc = ex2(ml[s * kHq * 2] - M);
-    L = fmaf(ml[s * kHq * 2 + 1], sc, L);
-    O = fmaf(po[(int64_t)s * kHq * kDim], sc, O);
+  const int64_t ml_s = a.ml_s ? a.ml_s : kHq * 2;
+  const int64_t ml_b = a.ml_b ? a.ml_b : a.num_parts * ml_s;
+  const int64_t o_s = a.o_s ? a.o_s : kHq * kDim;
+  const int64_t o_b = a.o_b ? a.o_b : a.num_parts * o_s;
+  const float *ml = a.part_ml + b * ml_b + h * 2;
+  const float *po = a.part_o + b * o_b + h * kDim + d;
+  float M = -1.0e30f, L = 0.f, O = 0.f;
+#pragma unroll 4
+  for (int s = grp; s < parts; s += a.groups) {
+    const float ms = ml[s * ml_s], ls = ml[s * ml_s + 1], os = po[s * o_s];
+    const float nm = fmaxf(M, ms);
+    const float c1 = ex2(M - nm), c2 = ex2(ms - nm);
+    L = L * c1 + ls * c2;
+    O = O * c1 + os * c2;
+    M = nm;
+  }
+  if (d == 0) {
+    sm[grp] = M;
+    sl[grp] = L;
+  }
+  so[grp][d] = O;
+  __syncthreads();
+  if (grp != 0) return;
+  float MM = -1.0e30f;
+  for (int g = 0; g < a.groups; ++g) MM = fmaxf(MM, sm[g]);
+  float LL = 0.f, OO = 0.f;
+  for (int g = 0; g < a.groups; ++g) {
+    const float c = ex2(sm[g] - MM);
+    LL = fmaf(sl[g], c, LL);
+    OO = fmaf(so[g][d], c, OO);
   }
   const int64_t oi = ((int64_t)b * kHq + h) * kDim + d;
-  if (a.out) a.out[oi] = static_cast<uint16_t>(bf16_bits(L > 0.f ? O / L : 0.f));
+  if (a.out) a.out[oi] = static_cast<uint16_t>(bf16_bits(LL > 0.f ? OO / LL : 0.f));
   if (a.state_o) {
-    a.state_o[oi] = O;
+    a.state_o[oi] = OO;
     if (d == 0) {
-      a.state_ml[((int64_t)b * kHq + h) * 2] = M;
-      a.state_ml[((int64_t)b * kHq + h) * 2 + 1] = L;
+      a.state_ml[((int64_t)b * kHq + h) * 2] = MM;
+      a.state_ml[((int64_t)b * kHq + h) * 2 + 1] = LL;
     }
   }
 }
@@ -601,11 +641,13 @@ struct StepArgs {
   const uint16_t *cos, *sin;
   int rope_rows;
   const int32_t *past_lens;
+  const int32_t *seq_lens;  // tokens attended; NULL: past_lens + 1
   const int32_t *block_tables;
   int max_blocks;
   uint16_t *k_pool, *v_pool;
   int num_blocks;
   int batch, blocks_per_split, num_splits, total_items;
+  int direct_out;  // whole-sequence items write the bf16 context themselves
   float scale_log2;
   int mode;
   uint16_t *out, *q_out;
@@ -625,9 +667,20 @@ __device__ __forceinline__ void consumers_sync(StepTail *tail, int lane, uint32_
   __syncwarp();
 }
 
+// Lengths of sequence b: past (RoPE position and, with B2_STORE_KV, the
+// append slot) and seq_len (tokens attended).  False for lengths the block
+// table cannot hold, or an append slot that is not the last attended token.
+__device__ __forceinline__ bool step_lengths(const StepArgs &a, int b, int &past, int &seq_len) {
+  past = __ldg(a.past_lens + b);
+  seq_len = a.seq_lens ? __ldg(a.seq_lens + b) : past + 1;
+  bool ok = past >= 0 && seq_len >= 0 && seq_len <= a.max_blocks * kBlock;
+  if (a.mode & B2_STORE_KV) ok = ok && seq_len == past + 1;
+  return ok;
+}
+
 // One work item as the producer sees it, with its loads already issued.
 struct ProducerItem {
-  int valid, b, kvh, split, past, nsplit, blk0, n;
+  int valid, b, kvh, split, past, seq_len, nsplit, blk0, n;
   int my_blk;   // block table entry blk0 + lane (lane < n)
   uint4 raw;    // this lane's 16 bytes of the item's q/k/v vectors
 };
@@ -656,10 +709,8 @@ __device__ __forceinline__ ProducerItem producer_load(const StepArgs &a, const S
     it.split = p / a.batch;
     it.b = p - it.split * a.batch;
   }
-  it.past = __ldg(a.past_lens + it.b);
-  const bool len_ok = it.past >= 0 && it.past < a.max_blocks * kBlock;
-  const int seq_len = it.past + 1;
-  const int nblk = (seq_len + kBlock - 1) / kBlock;
+  const bool len_ok = step_lengths(a, it.b, it.past, it.seq_len);
+  const int nblk = (it.seq_len + kBlock - 1) / kBlock;
   it.nsplit = (nblk + a.blocks_per_split - 1) / a.blocks_per_split;
   if (!len_ok || it.split >= it.nsplit) {
     if (!len_ok && lane == 0 && it.kvh == 0 && it.split == 0) atomicOr(a.err, B2_DEV_BAD_LENGTH);
@@ -695,9 +746,9 @@ __device__ __forceinline__ void step_producer(const StepArgs &a, StepTail *tail,
       const int b = base + lane;
       int ns = 0;
       if (b < a.batch) {
-        const int past = __ldg(a.past_lens + b);
-        if (past >= 0 && past < a.max_blocks * kBlock) {
-          const int nblk = (past + 1 + kBlock - 1) / kBlock;
+        int past, seq_len;
+        if (step_lengths(a, b, past, seq_len)) {
+          const int nblk = (seq_len + kBlock - 1) / kBlock;
           ns = (nblk + a.blocks_per_split - 1) / a.blocks_per_split;
         } else if (blockIdx.x == 0) {
           atomicOr(a.err, B2_DEV_BAD_LENGTH);
@@ -783,10 +834,10 @@ __device__ __forceinline__ void step_producer(const StepArgs &a, StepTail *tail,
         m.b = cur.b;
         m.kvh = cur.kvh;
         m.split = cur.split;
-        m.rows = cur.past + 1 - (cur.blk0 + jj) * kBlock;
+        m.rows = cur.seq_len - (cur.blk0 + jj) * kBlock;
         m.nsplit = cur.nsplit;
         m.flags = (jj == 0 ? kFlagFirst : 0) | (jj == cur.n - 1 ? kFlagLast : 0) |
-                  (cur.nsplit == 1 ? kFlagFinal : 0);
+                  (cur.nsplit == 1 && a.direct_out ? kFlagFinal : 0);
       }
       __syncwarp();
       if (lane == 0) {
@@ -1250,8 +1301,8 @@ extern "C" int b2_combine(const float *part_ml, const float *part_o, int32_t num
   if (!out && !state_o) return fail(B2_ERR_ARG, "one of out or state_o is required");
   if ((state_o == nullptr) != (state_ml == nullptr)) return fail(B2_ERR_ARG, "state_ml and state_o go together");
   CombineArgs a{part_ml, part_o, num_parts, seq_lens, blocks_per_split, out, state_ml, state_o, 0, 0,
-                num_parts * (seq_lens ? blocks_per_split : 1) * kBlock};
-  combine_kernel<<<batch, kHq * kDim, 0, static_cast<cudaStream_t>(stream)>>>(a);
+                num_parts * (seq_lens ? blocks_per_split : 1) * kBlock, 0, 0, 0, 0, combine_groups(num_parts)};
+  combine_kernel<<<dim3(batch, kHq), a.groups * kDim, 0, static_cast<cudaStream_t>(stream)>>>(a);
   return launch_status("combine_kernel");
 }
 
@@ -1260,20 +1311,21 @@ extern "C" int b2_decode_step_counters(int32_t batch) { return batch < 0 ? 0 : 2
 extern "C" int b2_decode_step(const uint16_t *qkv, int64_t row_stride, const uint16_t *gamma_q,
                               const uint16_t *gamma_k, float eps, const uint16_t *rope_cos,
                               const uint16_t *rope_sin, int32_t rope_rows, const int32_t *past_lens,
-                              const int32_t *block_tables, int32_t max_blocks_per_seq, uint16_t *k_pool,
-                              uint16_t *v_pool, int32_t num_blocks, int32_t batch, int32_t blocks_per_split,
-                              float scale, int32_t mode, uint16_t *out, uint16_t *q_out, float *part_ml,
-                              float *part_o, int32_t *counters, int32_t max_ctas, int32_t *dev_err,
-                              void *stream) {
+                              const int32_t *seq_lens, const int32_t *block_tables, int32_t max_blocks_per_seq,
+                              uint16_t *k_pool, uint16_t *v_pool, int32_t num_blocks, int32_t batch,
+                              int32_t blocks_per_split, float scale, int32_t mode, uint16_t *out,
+                              uint16_t *q_out, float *state_ml, float *state_o, float *part_ml, float *part_o,
+                              int32_t *counters, int32_t max_ctas, int32_t *dev_err, void *stream) {
   if (batch < 0) return fail(B2_ERR_ARG, "batch must be >= 0 (got %d)", batch);
   if (batch == 0) return ok();
-  if (!qkv || !past_lens || !block_tables || !k_pool || !v_pool || !out || !part_ml || !part_o || !counters ||
-      !dev_err)
+  if (!qkv || !past_lens || !block_tables || !k_pool || !v_pool || !part_ml || !part_o || !counters || !dev_err)
     return fail(B2_ERR_ARG, "null pointer argument");
+  if (!out && !state_o) return fail(B2_ERR_ARG, "one of out or state_o is required");
+  if ((state_o == nullptr) != (state_ml == nullptr)) return fail(B2_ERR_ARG, "state_ml and state_o go together");
   if (mode & ~(B2_NORM_QK | B2_ROPE_QK | B2_STORE_KV)) return fail(B2_ERR_ARG, "unknown mode bits 0x%x", mode);
   if (row_stride < kQkvWidth || row_stride % 8 != 0)
     return fail(B2_ERR_ARG, "row_stride must be >= %d and a multiple of 8", kQkvWidth);
-  if (!aligned16(qkv) || !aligned16(out) || (q_out && !aligned16(q_out)) || !aligned16(k_pool) ||
+  if (!aligned16(qkv) || (out && !aligned16(out)) || (q_out && !aligned16(q_out)) || !aligned16(k_pool) ||
       !aligned16(v_pool))
     return fail(B2_ERR_ARG, "qkv, out, q_out and the pools must be 16-byte aligned");
   if ((mode & B2_NORM_QK) && (!gamma_q || !gamma_k || !aligned16(gamma_q) || !aligned16(gamma_k)))
@@ -1296,10 +1348,11 @@ extern "C" int b2_decode_step(const uint16_t *qkv, int64_t row_stride, const uin
   rc = make_pool_map(&mv, v_pool, num_blocks);
   if (rc) return rc;
   if (!step_smem_ready()) return fail(B2_ERR_CUDA, "cannot set the decode-step kernel's shared memory size");
-  StepArgs a{qkv, row_stride, gamma_q, gamma_k, eps, rope_cos, rope_sin, rope_rows, past_lens, block_tables,
-             max_blocks_per_seq, k_pool, v_pool, num_blocks, batch, blocks_per_split, static_cast<int>(splits),
-             static_cast<int>(total), scale * 1.4426950408889634f, mode, out, q_out, part_ml, part_o, counters,
-             dev_err};
+  const int direct_out = state_o == nullptr;
+  StepArgs a{qkv, row_stride, gamma_q, gamma_k, eps, rope_cos, rope_sin, rope_rows, past_lens, seq_lens,
+             block_tables, max_blocks_per_seq, k_pool, v_pool, num_blocks, batch, blocks_per_split,
+             static_cast<int>(splits), static_cast<int>(total), direct_out, scale * 1.4426950408889634f, mode, out,
+             q_out, part_ml, part_o, counters, dev_err};
   int64_t ctas = static_cast<int64_t>(sm_count()) * 3;
   if (max_ctas > 0 && max_ctas < ctas) ctas = max_ctas;
   if (ctas > total) ctas = total;
@@ -1309,11 +1362,12 @@ extern "C" int b2_decode_step(const uint16_t *qkv, int64_t row_stride, const uin
   if (rc) return rc;
   // Merge the split sequences; launched as a programmatic dependent so that
   // its launch overlaps the decode kernel's last CTAs.
-  CombineArgs c{part_ml, part_o, static_cast<int>(splits), past_lens, blocks_per_split, out, nullptr, nullptr,
-                1, 1, static_cast<int>(splits) * blocks_per_split * kBlock};
+  CombineArgs c{part_ml, part_o, static_cast<int>(splits), seq_lens ? seq_lens : past_lens, blocks_per_split, out,
+                state_ml, state_o, seq_lens ? 0 : 1, direct_out, static_cast<int>(splits) * blocks_per_split * kBlock,
+                0, 0, 0, 0, combine_groups(static_cast<int>(splits))};
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(batch));
-  cfg.blockDim = dim3(kHq * kDim);
+  cfg.gridDim = dim3(static_cast<unsigned>(batch), kHq);
+  cfg.blockDim = dim3(c.groups * kDim);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -1326,6 +1380,20 @@ extern "C" int b2_decode_step(const uint16_t *qkv, int64_t row_stride, const uin
     return fail(B2_ERR_CUDA, "combine_kernel launch failed: %s", cudaGetErrorString(e));
   }
   return launch_status("combine_kernel (decode step)");
+}
+
+extern "C" int b2_merge_states(const float *states, int32_t num_parts, int32_t batch, uint16_t *out,
+                               float *state_ml, float *state_o, void *stream) {
+  if (batch < 0) return fail(B2_ERR_ARG, "batch must be >= 0 (got %d)", batch);
+  if (batch == 0) return ok();
+  if (!states || num_parts <= 0) return fail(B2_ERR_ARG, "states and num_parts > 0 required");
+  if (!out && !state_o) return fail(B2_ERR_ARG, "one of out or state_o is required");
+  if ((state_o == nullptr) != (state_ml == nullptr)) return fail(B2_ERR_ARG, "state_ml and state_o go together");
+  const int64_t part = static_cast<int64_t>(batch) * kHq * (2 + kDim);  // floats per part
+  CombineArgs a{states, states + static_cast<int64_t>(batch) * kHq * 2, num_parts, nullptr, 1, out, state_ml,
+                state_o, 0, 0, 0, kHq * 2, part, kHq * kDim, part, combine_groups(num_parts)};
+  combine_kernel<<<dim3(batch, kHq), a.groups * kDim, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  return launch_status("combine_kernel (merge states)");
 }
 
 // ------------------------------------------------------------------ allocation-free decode
@@ -1408,7 +1476,8 @@ extern "C" int b2_decode_attn_noalloc(const uint16_t *q, const uint16_t *k_pool,
   rc = launch_status("paged_decode_kernel (noalloc)");
   if (rc) return rc;
   CombineArgs c{part_ml, part_o, static_cast<int>(splits), seq_lens, blocks_per_split, out, nullptr, nullptr,
-                0, 0, static_cast<int>(splits) * blocks_per_split * kBlock};
-  combine_kernel<<<batch, kHq * kDim, 0, s>>>(c);
+                0, 0, static_cast<int>(splits) * blocks_per_split * kBlock, 0, 0, 0, 0,
+                combine_groups(static_cast<int>(splits))};
+  combine_kernel<<<dim3(batch, kHq), c.groups * kDim, 0, s>>>(c);
   return launch_status("combine_kernel (noalloc)");
 }

@@ -1,0 +1,88 @@
+"""Host-side multi-GPU logic on CPU: sequence sharding, token ranges, and the
+long-context state exchange over a world-size-2 gloo group (the partial
+states come from the CPU oracle; on GPUs they come from libb2attn.so)."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from conftest import load_pkg
+from oracle import lfm2_attention as orc
+
+
+def test_shard_sequences_balances_tokens():
+    dist_mod = load_pkg("distributed")
+    g = torch.Generator().manual_seed(3)
+    lengths = torch.randint(128, 8193, (64,), generator=g).tolist()
+    for world in (1, 2, 4, 8):
+        shards = dist_mod.shard_sequences(lengths, world)
+        assert sorted(i for s in shards for i in s) == list(range(64))
+        loads = [sum(lengths[i] + 1 for i in s) for s in shards]
+        assert max(loads) - min(loads) <= max(lengths) + 1
+    with pytest.raises(ValueError):
+        dist_mod.shard_sequences(lengths, 0)
+
+
+@pytest.mark.parametrize("total", [0, 1, 63, 64, 65, 1000, 131072, 131073])
+@pytest.mark.parametrize("world", [1, 2, 3, 8])
+def test_token_ranges_cover_and_align(total, world):
+    dist_mod = load_pkg("distributed")
+    r = dist_mod.token_ranges(total, world)
+    assert len(r) == world
+    assert r[0][0] == 0 and r[-1][1] == total
+    for (a, b), (c, _) in zip(r, r[1:]):
+        assert b == c and a <= b
+    for a, b in r:
+        assert a % 64 == 0 or a == b == total   # empty trailing ranges sit at the end
+    sizes = [b - a for a, b in r]
+    assert max(sizes) - min(sizes) <= 64 * 2
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _long_context_worker(rank, world, port, total, q, k, v, result):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        dist_mod = load_pkg("distributed")
+        lo, hi = dist_mod.token_ranges(total, world)[rank]
+        m, l, o = orc.partial_state(q, k[:, lo:hi], v[:, lo:hi])
+        state = torch.cat([m[:, None], l[:, None], o], dim=1)[None]      # [1, 16, 66]
+        allst = dist_mod.gather_states(state)                              # [world, 1, 16, 66]
+        parts = [(s[0, :, 0], s[0, :, 1], s[0, :, 2:]) for s in allst]
+        result[rank] = orc.merge_states(parts)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("total", [300, 1000])
+def test_long_context_state_exchange_gloo(total):
+    world = 2
+    g = torch.Generator().manual_seed(11)
+    q = torch.randn(16, 64, generator=g).to(torch.bfloat16)
+    k = torch.randn(8, total, 64, generator=g).to(torch.bfloat16)
+    v = torch.randn(8, total, 64, generator=g).to(torch.bfloat16)
+    full = orc.attend(q[None, :, None, :], k[None], v[None], "fp32").reshape(16, 64)
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as mgr:
+        result = mgr.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_long_context_worker, args=(r, world, port, total, q, k, v, result))
+                 for r in range(world)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(120)
+            assert p.exitcode == 0
+        for r in range(world):
+            assert torch.allclose(result[r], full, atol=1e-5, rtol=1e-5)

@@ -262,3 +262,57 @@ def test_fused_multi_step_decode_vs_oracle(cuda):
             ks[i] = kd.cpu()
             vs[i] = vd.cpu()
             assert torch.equal(vs[i], v_all)
+
+
+@pytest.mark.parametrize("total,cut", [(300, 128), (5000, 2048), (64, 64), (10, 64)])
+def test_split_sequence_states_merge(cuda, total, cut):
+    """One sequence split along the token axis as two GPUs would hold it,
+    emulated on one GPU: the head part attends over its tokens only (seq_lens,
+    RoPE at the global position through an offset table), the tail part also
+    appends the new token; both return fp32 states that b2_combine merges."""
+    attn = _attn()
+    rope = load_pkg("rope")
+    w = orc.attention_weights(0)
+    k, v = orc.past_cache(91, total)
+    k, v = k[0], v[0]
+    raw = rand_qkv(1, 92)
+    ctx_ref, _, _, _ = orc.decode_step(raw[0], k, v, total, w["q_gamma"], w["k_gamma"])
+    cos, sin = rope.rope_table(total + 8, device=cuda)
+    cm = _cache_mod()
+    parts = [(0, min(cut, total), False), (min(cut, total), total, True)]
+    states = []
+    for lo, hi, tail in parts:
+        n = hi - lo
+        cache = cm.PagedKVCache(cm.blocks_for(n + 1) + 1, n + 1, device=cuda, fill=float("nan"))
+        cache.add_sequence(n)
+        if n:
+            cache.write_dense(0, 0, k[:, lo:hi], v[:, lo:hi])
+        kp, vp = cache.pool(0)
+        past = torch.tensor([total - lo], dtype=torch.int32, device=cuda)
+        seq = torch.tensor([n], dtype=torch.int32, device=cuda)
+        splits = attn.num_splits_for(cache.max_blocks, 2)
+        ml = torch.empty(1, splits, 16, 2, device=cuda)
+        po = torch.empty(1, splits, 16, 64, device=cuda)
+        sml = torch.empty(1, 16, 2, device=cuda)
+        so = torch.empty(1, 16, 64, device=cuda)
+        err = torch.zeros(1, dtype=torch.int32, device=cuda)
+        mode = _lib().B2_NORM_QK | _lib().B2_ROPE_QK | (_lib().B2_STORE_KV if tail else 0)
+        attn.decode_step(raw.to(cuda), past, k_pool=kp, v_pool=vp, block_tables=cache.block_tables(),
+                         blocks_per_split=2, out=None, part_ml=ml, part_o=po,
+                         counters=torch.zeros(2, dtype=torch.int32, device=cuda), dev_err=err,
+                         gamma_q=w["q_gamma"].to(cuda), gamma_k=w["k_gamma"].to(cuda), cos=cos[lo:], sin=sin[lo:],
+                         seq_lens=None if tail else seq, state_ml=sml, state_o=so, mode=mode)
+        torch.cuda.synchronize()
+        assert err.item() == 0
+        states.append((sml, so))
+    ml = torch.stack([s[0] for s in states], dim=1).contiguous()   # [1, 2, 16, 2]
+    po = torch.stack([s[1] for s in states], dim=1).contiguous()   # [1, 2, 16, 64]
+    out = torch.empty(1, 16, 64, dtype=torch.bfloat16, device=cuda)
+    attn.combine(ml, po, 2, 1, out=out)
+    # the same merge from the packed layout one all-gather produces
+    packed = torch.stack([torch.cat([s[0].reshape(-1), s[1].reshape(-1)]) for s in states])
+    out2 = torch.empty(1, 16, 64, dtype=torch.bfloat16, device=cuda)
+    attn.merge_states(packed, 2, 1, out=out2)
+    torch.cuda.synchronize()
+    check_close(out[0], ctx_ref, f"split at {cut} of {total}")
+    assert torch.equal(out, out2)
