@@ -3,7 +3,8 @@
     python bench.py --gpus N --steps K --warmup W [--impl b200|reference]
 
 Workload (batched paged decode): per GPU, 64 sequences
-with cached lengths uniform in [128, 8192] (seeded per rank), K/V ~ N(0, 1)
+with cached lengths uniform in [128, 8192] (one seeded global batch of
+64 x N sequences, sharded over the N GPUs by token count), K/V ~ N(0, 1)
 bf16 in a pool of 64-token blocks handed out in shuffled order, 16 q heads /
 8 KV heads / head_dim 64.  One step = one decode token per sequence through
 one attention layer: fused q/k RMSNorm + RoPE + KV append, split-KV
@@ -62,8 +63,9 @@ def parse():
     p.add_argument("--three-kernels", action="store_true",
                    help="run append, decode and combine as three launches instead of the fused kernel")
     p.add_argument("--max-ctas", type=int, default=0, help="cap on the fused kernel's persistent grid")
-    p.add_argument("--config", choices=["c3", "c4"], default="c3",
-                   help="c3: batched paged decode (default); c4: one long sequence split over the GPUs")
+    p.add_argument("--config", choices=["c3", "c4", "c2"], default="c3",
+                   help="c3: batched paged decode (default); c4: one long sequence split over the GPUs; "
+                        "c2: 6 attention layers x 64 consecutive decode steps of one sequence")
     p.add_argument("--context", type=int, default=131072, help="c4: cached tokens of the sequence")
     return p.parse_args()
 
@@ -151,15 +153,23 @@ class ClockSampler:
 
 # ----------------------------------------------------------------- workload
 
-def seq_lengths(args, rank: int) -> list[int]:
-    g = torch.Generator().manual_seed(args.seed * 1000 + rank)
-    return torch.randint(args.min_len, args.max_len + 1, (args.batch,), generator=g).tolist()
+def seq_lengths(args, rank: int, world: int = 1) -> list[int]:
+    """Cached lengths of this rank's sequences.  The global batch (batch per GPU
+    x world) is drawn from one seeded generator and sharded over the ranks by
+    token count (longest-first bin packing), so every GPU gets the same
+    amount of work; with one GPU it is the 64-sequence C3 batch."""
+    g = torch.Generator().manual_seed(args.seed * 1000)
+    lengths = torch.randint(args.min_len, args.max_len + 1, (args.batch * world,), generator=g).tolist()
+    if world == 1:
+        return lengths
+    dmod = importlib.import_module(PKG + ".distributed")
+    return [lengths[i] for i in dmod.shard_sequences(lengths, world)[rank]]
 
 
-def build_workload(args, rank: int, dev: torch.device):
+def build_workload(args, rank: int, dev: torch.device, world: int = 1):
     attn = importlib.import_module(PKG + ".attention")
     pc = importlib.import_module(PKG + ".paged_cache")
-    lengths = seq_lengths(args, rank)
+    lengths = seq_lengths(args, rank, world)
     caps = [n + 1 for n in lengths]
     num_blocks = sum(pc.blocks_for(c) for c in caps)
     cache = pc.PagedKVCache(num_blocks, max(caps), device=dev, shuffle_seed=args.seed * 1000 + rank + 17)
@@ -172,11 +182,11 @@ def build_workload(args, rank: int, dev: torch.device):
     gamma_q = (1.0 + 0.1 * torch.randn(D, generator=gg)).to(torch.bfloat16)
     gamma_k = (1.0 + 0.1 * torch.randn(D, generator=gg)).to(torch.bfloat16)
     work_blocks = sum(pc.blocks_for(c) for c in caps)
-    runner = attn.PagedDecodeAttention(cache, gamma_q, gamma_k, args.batch, args.max_len + 2,
+    runner = attn.PagedDecodeAttention(cache, gamma_q, gamma_k, len(lengths), args.max_len + 2,
                                        blocks_per_split=args.bps or None, work_blocks=work_blocks,
                                        fused=not args.three_kernels, max_ctas=args.max_ctas)
     ring = 8
-    qkv = (torch.randn(ring, args.batch, 2048, generator=gen, device=dev) * 0.6).to(torch.bfloat16)
+    qkv = (torch.randn(ring, len(lengths), 2048, generator=gen, device=dev) * 0.6).to(torch.bfloat16)
     past = torch.tensor(lengths, dtype=torch.int32, device=dev)
     return {"lengths": lengths, "cache": cache, "runner": runner, "qkv": qkv, "past": past,
             "seq": past + 1, "tables": cache.block_tables(), "ring": ring}
@@ -278,7 +288,7 @@ def run_b200(args):
         import datetime
         torch.distributed.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
         pg = torch.distributed.group.WORLD
-    wl = build_workload(args, rank, dev)
+    wl = build_workload(args, rank, dev, world)
     runner = wl["runner"]
     K, W, ring = args.steps, args.warmup, wl["ring"]
     stream = torch.cuda.Stream(dev)
@@ -302,7 +312,7 @@ def run_b200(args):
     ev1 = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(K)]
     graph = torch.cuda.CUDAGraph()
     kp, vp = runner.cache.pool(0)
-    b = args.batch
+    b = len(wl["lengths"])
     with torch.cuda.graph(graph, stream=stream):
         for j in range(K):
             if runner.fused:
@@ -346,9 +356,10 @@ def run_b200(args):
     e2e_steps = min(args.e2e_steps, K)
     qkv_host = wl["qkv"].cpu().pin_memory()
     lens_host = torch.stack([wl["past"].cpu(), wl["seq"].cpu()]).pin_memory()
-    out_host = torch.empty(e2e_steps, args.batch, HQ, D, dtype=torch.bfloat16).pin_memory()
+    nb = len(wl["lengths"])
+    out_host = torch.empty(e2e_steps, nb, HQ, D, dtype=torch.bfloat16).pin_memory()
     qkv_dev = torch.empty_like(wl["qkv"][0])
-    lens_dev = torch.empty(2, args.batch, dtype=torch.int32, device=dev)
+    lens_dev = torch.empty(2, nb, dtype=torch.int32, device=dev)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
@@ -400,8 +411,8 @@ def run_b200(args):
                      "algorithmic_bytes": dbytes, "avg_launch_ms": decode_ms},
         "clocks": clocks.summary(),
         "e2e": {"value": tokens * e2e_steps / (e2e_ms / 1e3), "unit": "tokens/s",
-                "h2d_bytes_per_step": args.batch * (2048 * 2 + 2 * 4),
-                "d2h_bytes_per_step": args.batch * HQ * D * 2, "steps": e2e_steps},
+                "h2d_bytes_per_step": nb * (2048 * 2 + 2 * 4),
+                "d2h_bytes_per_step": nb * HQ * D * 2, "steps": e2e_steps},
         "gpu_launches": (1 if runner.fused else 3) * K,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -506,6 +517,86 @@ def run_c4(args):
     torch.distributed.destroy_process_group()
 
 
+def run_c2(args):
+    """Config C2: one sequence, the 6 attention layers of LFM2.5-230M, 64
+    consecutive decode steps from --context cached tokens (each step appends
+    one token per layer and attends over the grown cache).  One timed step =
+    one token through the 6 layers; the 64-step run is captured once as a
+    CUDA graph and replayed.  Replicas only across GPUs."""
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    attn = importlib.import_module(PKG + ".attention")
+    pc = importlib.import_module(PKG + ".paged_cache")
+    layers, steps = 6, 64
+    L0 = args.context
+    cap = L0 + steps + 1
+    cache = pc.PagedKVCache(pc.blocks_for(cap), cap, num_layers=layers, device=dev,
+                            shuffle_seed=args.seed * 1000 + 17)
+    cache.add_sequence(L0, capacity=cap)
+    gen = torch.Generator(device=dev).manual_seed(args.seed * 1000 + rank + 29)
+    cache.k.normal_(generator=gen)
+    cache.v.normal_(generator=gen)
+    gg = torch.Generator().manual_seed(args.seed + 31)
+    gammas = [((1.0 + 0.1 * torch.randn(D, generator=gg)).to(torch.bfloat16),
+               (1.0 + 0.1 * torch.randn(D, generator=gg)).to(torch.bfloat16)) for _ in range(layers)]
+    runners = [attn.PagedDecodeAttention(cache, gq, gk, 1, cap + 1, blocks_per_split=args.bps or None,
+                                         work_blocks=pc.blocks_for(cap)) for gq, gk in gammas]
+    qkv = (torch.randn(steps, layers, 1, 2048, generator=gen, device=dev) * 0.6).to(torch.bfloat16)
+    past = torch.arange(L0, L0 + steps, dtype=torch.int32, device=dev).reshape(steps, 1)
+    tables = cache.block_tables()
+    stream = torch.cuda.Stream(dev)
+
+    seq = past + 1
+    with torch.cuda.stream(stream):
+        for t in range(max(args.warmup, 1)):
+            for layer in range(layers):
+                runners[layer].step(layer, qkv[t % steps, layer], past[t % steps], seq[t % steps], tables)
+    stream.synchronize()
+    for r in runners:
+        r.check()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for t in range(steps):
+            for layer in range(layers):
+                runners[layer].step(layer, qkv[t, layer], past[t], seq[t], tables)
+    graph.replay()
+    torch.cuda.synchronize()
+    reps = max(1, args.steps // steps)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        with torch.cuda.stream(stream):
+            t0.record()
+            for _ in range(reps):
+                graph.replay()
+            t1.record()
+        torch.cuda.synchronize()
+    for r in runners:
+        r.check()
+    ms = t0.elapsed_time(t1)
+    K = reps * steps
+    step_bytes_all = sum(layers * (KV_BYTES_PER_TOKEN * (L0 + t + 4) + 4 * pc.blocks_for(L0 + t + 1))
+                         for t in range(steps)) / steps
+    peak, peak_kind = measured_hbm_peak()
+    gbs = step_bytes_all / (ms / K / 1e3) / 1e9
+    line = {
+        "metric": METRIC, "value": K / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": K,
+        "warmup": args.warmup, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "replicas",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"C2: one sequence, 6 attention layers x 64 consecutive decode steps from "
+                               f"{L0} cached tokens (CUDA graph of the 64 steps, replayed {reps}x)",
+                   "context": L0, "global_batch": 1, "blocks_per_split": runners[0].blocks_per_split,
+                   "parallelism": "replicas", "l2": "K/V of 6 layers; the step re-reads its cache once"},
+        "hbm_gbs_per_gpu": gbs, "hbm_pct_of_8tbs": 100 * gbs / 8000,
+        "roofline": {"bound": "hbm", "kernel": "decode_step_kernel x 6 layers", "achieved": gbs, "peak": peak,
+                     "peak_source": peak_kind, "unit": "GB/s", "frac": gbs / peak, "traffic": None},
+        "clocks": clocks.summary(), "gpu_launches": K * layers * 2,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     world, _, _ = dist_env()
@@ -516,6 +607,8 @@ def main():
         run_reference(args)
     elif args.config == "c4":
         run_c4(args)
+    elif args.config == "c2":
+        run_c2(args)
     else:
         run_b200(args)
 

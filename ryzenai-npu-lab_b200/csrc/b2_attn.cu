@@ -544,6 +544,7 @@ constexpr int kCombineGroups = 16;
 
 __global__ void __launch_bounds__(kCombineGroups * kDim) combine_kernel(const CombineArgs a) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   __shared__ float sm[kCombineGroups], sl[kCombineGroups], so[kCombineGroups][kDim];
   const int b = blockIdx.x;
   const int h = blockIdx.y;
@@ -1114,6 +1115,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 3)
     mbar_fence_init();
   }
   __syncthreads();
+  // Launched as a programmatic dependent of the previous kernel on the
+  // stream: the set-up above overlaps its tail; wait for its completion (and
+  // memory) before touching global memory.  A no-op for an ordinary launch.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   // Let the combine kernel be scheduled as soon as CTAs of this grid retire;
   // it waits for this grid's completion before reading the partial states.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -1357,7 +1362,24 @@ extern "C" int b2_decode_step(const uint16_t *qkv, int64_t row_stride, const uin
   if (max_ctas > 0 && max_ctas < ctas) ctas = max_ctas;
   if (ctas > total) ctas = total;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  decode_step_kernel<<<static_cast<unsigned>(ctas), kDecodeThreads, kStepSmem, st>>>(mk, mv, a);
+  cudaLaunchAttribute pdl[1];
+  pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  pdl[0].val.programmaticStreamSerializationAllowed = 1;
+  {
+    // programmatic dependent of the previous kernel on the stream (see the
+    // griddepcontrol.wait at the top of the kernel)
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(ctas));
+    cfg.blockDim = dim3(kDecodeThreads);
+    cfg.dynamicSmemBytes = kStepSmem;
+    cfg.stream = st;
+    cfg.attrs = pdl;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, decode_step_kernel, mk, mv, a) != cudaSuccess) {
+      const cudaError_t e = cudaGetLastError();
+      return fail(B2_ERR_CUDA, "decode_step_kernel launch failed: %s", cudaGetErrorString(e));
+    }
+  }
   rc = launch_status("decode_step_kernel");
   if (rc) return rc;
   // Merge the split sequences; launched as a programmatic dependent so that
@@ -1370,10 +1392,7 @@ extern "C" int b2_decode_step(const uint16_t *qkv, int64_t row_stride, const uin
   cfg.blockDim = dim3(c.groups * kDim);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
+  cfg.attrs = pdl;
   cfg.numAttrs = 1;
   if (cudaLaunchKernelEx(&cfg, combine_kernel, c) != cudaSuccess) {
     const cudaError_t e = cudaGetLastError();
