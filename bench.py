@@ -63,9 +63,10 @@ def parse():
     p.add_argument("--three-kernels", action="store_true",
                    help="run append, decode and combine as three launches instead of the fused kernel")
     p.add_argument("--max-ctas", type=int, default=0, help="cap on the fused kernel's persistent grid")
-    p.add_argument("--config", choices=["c3", "c4", "c2"], default="c3",
+    p.add_argument("--config", choices=["c3", "c4", "c2", "c5"], default="c3",
                    help="c3: batched paged decode (default); c4: one long sequence split over the GPUs; "
-                        "c2: 6 attention layers x 64 consecutive decode steps of one sequence")
+                        "c2: 6 attention layers x 64 consecutive decode steps of one sequence; "
+                        "c5: end-to-end greedy decode of the whole random-init model")
     p.add_argument("--context", type=int, default=131072, help="c4: cached tokens of the sequence")
     return p.parse_args()
 
@@ -597,6 +598,50 @@ def run_c2(args):
         print(json.dumps(line), flush=True)
 
 
+def run_c5(args):
+    """Config C5: end-to-end greedy decode of an LFM2.5-230M-shaped random-init
+    model (14 layers: 8 short-conv + 6 GQA attention, SwiGLU 2560, tied 65536
+    head): 256 prompts x 32 random ids, 256 new tokens each, paged KV, one
+    CUDA graph per token.  value = new tokens per second over the whole job
+    (prefill included); replicas across GPUs (each rank its own batch)."""
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    runner_mod = importlib.import_module(PKG + ".lfm2_runner")
+    from oracle import lfm2_attention as orc   # seeded weight generator (set-up only)
+    batch, prompt_len, new = 256, 32, 256
+    sd = orc.lfm2_model_weights(args.seed)
+    runner = runner_mod.LFM2DecodeRunner(sd, max_batch=batch, max_context=prompt_len + new + 1, device=dev)
+    del sd
+    g = torch.Generator().manual_seed(args.seed * 1000 + rank)
+    prompts = torch.randint(0, 65536, (batch, prompt_len), generator=g)
+    runner.generate(prompts[:, :4], 4)   # warm-up + graph capture
+    torch.cuda.synchronize()
+    runner.reset()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        t0.record()
+        out = runner.generate(prompts, new)
+        t1.record()
+        torch.cuda.synchronize()
+    runner.check()
+    ms = t0.elapsed_time(t1)
+    line = {
+        "metric": METRIC, "value": batch * new / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
+        "steps": prompt_len + new - 1, "warmup": 1, "ms_per_step": ms / (prompt_len + new - 1),
+        "higher_is_better": True, "scaling": "replicas", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": "C5 end-to-end greedy decode, LFM2.5-230M-shaped random-init model, "
+                               "256 prompts x 32 ids, 256 new tokens, paged KV, CUDA graph per token",
+                   "global_batch": batch * world, "prompt": prompt_len, "new_tokens": new,
+                   "parallelism": f"replicas x{world}"},
+        "generated_shape": list(out.shape), "clocks": clocks.summary(),
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     world, _, _ = dist_env()
@@ -609,6 +654,8 @@ def main():
         run_c4(args)
     elif args.config == "c2":
         run_c2(args)
+    elif args.config == "c5":
+        run_c5(args)
     else:
         run_b200(args)
 

@@ -59,6 +59,46 @@ def attention_weights(seed: int, hidden: int = 1024) -> dict[str, torch.Tensor]:
     return {k: v.to(BF16) for k, v in w.items()}
 
 
+LFM25_LAYER_TYPES = ("conv", "conv", "full_attention", "conv", "full_attention", "conv", "full_attention",
+                     "conv", "full_attention", "conv", "full_attention", "conv", "full_attention", "conv")
+
+
+def lfm2_model_weights(seed: int, hidden: int = 1024, ffn: int = 2560, vocab: int = 65536,
+                       layer_types=LFM25_LAYER_TYPES, conv_l: int = 3) -> dict[str, torch.Tensor]:
+    """Random-init LFM2.5-230M-shaped weights with Hugging Face parameter names
+    (the layer pattern of experiments/lfm25_x8.py:55-57, FFN width 2560 of
+    experiments/lfm25_x8.py:50): matrices N(0, 0.02) (the config's
+    initializer_range), RMSNorm gains 1, q/k layernorm gains 1 + N(0, 0.1);
+    lm_head tied to the embedding.  bf16."""
+    g = torch.Generator().manual_seed(seed)
+
+    def n(*shape, std=0.02):
+        return (torch.randn(*shape, generator=g) * std).to(BF16)
+
+    sd = {"model.embed_tokens.weight": n(vocab, hidden)}
+    for i, kind in enumerate(layer_types):
+        p = f"model.layers.{i}."
+        if kind == "full_attention":
+            sd[p + "self_attn.q_proj.weight"] = n(HQ * D, hidden)
+            sd[p + "self_attn.k_proj.weight"] = n(HKV * D, hidden)
+            sd[p + "self_attn.v_proj.weight"] = n(HKV * D, hidden)
+            sd[p + "self_attn.out_proj.weight"] = n(hidden, HQ * D)
+            sd[p + "self_attn.q_layernorm.weight"] = (1.0 + 0.1 * torch.randn(D, generator=g)).to(BF16)
+            sd[p + "self_attn.k_layernorm.weight"] = (1.0 + 0.1 * torch.randn(D, generator=g)).to(BF16)
+        else:
+            sd[p + "conv.conv.weight"] = n(hidden, 1, conv_l, std=0.3)
+            sd[p + "conv.in_proj.weight"] = n(3 * hidden, hidden)
+            sd[p + "conv.out_proj.weight"] = n(hidden, hidden)
+        sd[p + "feed_forward.w1.weight"] = n(ffn, hidden)
+        sd[p + "feed_forward.w3.weight"] = n(ffn, hidden)
+        sd[p + "feed_forward.w2.weight"] = n(hidden, ffn)
+        sd[p + "operator_norm.weight"] = torch.ones(hidden, dtype=BF16)
+        sd[p + "ffn_norm.weight"] = torch.ones(hidden, dtype=BF16)
+    sd["model.embedding_norm.weight"] = torch.ones(hidden, dtype=BF16)
+    sd["lm_head.weight"] = sd["model.embed_tokens.weight"]
+    return sd
+
+
 def past_cache(seed: int, length: int, batch: int = 1) -> tuple[torch.Tensor, torch.Tensor]:
     """K, V ~ N(0, 1) in bf16, shape [batch, 8, length, 64] (DynamicCache layout)."""
     g = torch.Generator().manual_seed(seed)

@@ -116,6 +116,42 @@ def run_case(length: int, impl: str, weights: dict) -> dict:
     }
 
 
+GREEDY_SEED = 5
+GREEDY_BATCH, GREEDY_PROMPT, GREEDY_NEW, GREEDY_TOPK = 2, 8, 16, 8
+
+
+def greedy_case() -> dict:
+    """The reference's CPU greedy loop (experiments/010_cpu_greedy.py:43-63):
+    Lfm2ForCausalLM in BF16, one token per forward with a DynamicCache, argmax.
+    Records, for every step, the input ids and the top-8 logits (values and
+    indices) so that a GPU runner can be checked teacher-forced."""
+    from transformers import Lfm2ForCausalLM
+    cfg = config("sdpa")
+    cfg.tie_word_embeddings = True
+    model = Lfm2ForCausalLM(cfg).to(BF16).eval()
+    sd = orc.lfm2_model_weights(GREEDY_SEED)
+    model.load_state_dict(sd, strict=True)
+    model.tie_weights()
+    g = torch.Generator().manual_seed(GREEDY_SEED + 1)
+    prompt = torch.randint(0, cfg.vocab_size, (GREEDY_BATCH, GREEDY_PROMPT), generator=g)
+    cache = DynamicCache(config=cfg)
+    inputs, topv, topi = [], [], []
+    nxt = None
+    with torch.no_grad():
+        for t in range(GREEDY_PROMPT + GREEDY_NEW - 1):
+            ids = prompt[:, t] if t < GREEDY_PROMPT else nxt
+            logits = model(ids[:, None], past_key_values=cache, use_cache=True).logits[:, -1]
+            v, i = logits.float().topk(GREEDY_TOPK, dim=-1)
+            inputs.append(ids.clone())
+            topv.append(v)
+            topi.append(i)
+            nxt = logits.argmax(-1)
+    return {"inputs": torch.stack(inputs, 1).numpy(), "top_values": torch.stack(topv, 1).numpy(),
+            "top_indices": torch.stack(topi, 1).numpy(), "prompt_len": np.int64(GREEDY_PROMPT),
+            "weight_seed": np.int64(GREEDY_SEED),
+            "model_weights_sha256": sha(*[sd[k] for k in sorted(sd) if k != "lm_head.weight"])}
+
+
 def main() -> None:
     torch.manual_seed(0)
     weights = orc.attention_weights(WEIGHT_SEED)
@@ -137,6 +173,7 @@ def main() -> None:
         cos, sin = rotary(torch.zeros(1, dtype=BF16), pos)
     np.savez_compressed(OUT / "lfm2_rope.npz", positions=np.array(ROPE_POSITIONS, dtype=np.int64),
                         cos=orc.bits(cos[0]), sin=orc.bits(sin[0]), **meta)
+    np.savez_compressed(OUT / "lfm2_greedy.npz", **greedy_case(), **meta)
     print("wrote", sorted(p.name for p in OUT.glob("*.npz")))
 
 
