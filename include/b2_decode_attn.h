@@ -166,8 +166,11 @@ int b2_combine(const float *part_ml, const float *part_o, int32_t num_parts,
  * A persistent grid (3 CTAs per SM, or max_ctas if smaller and > 0) takes
  * work items (sequence, split, kv head) from a counter; a sequence that fits
  * one split is written to out directly, the others leave partial states in
- * part_ml/part_o that a second, small kernel (launched by this call as a
- * programmatic dependent) merges into out.
+ * part_ml/part_o and the last split of a (sequence, kv head) to finish
+ * merges them (a dedicated warp per CTA counts the arrivals and merges, off
+ * the path of the warps that stream the cache).  With more than 16 splits
+ * per sequence the merge is left to the parallel combine kernel, which this
+ * call launches after the decode kernel as a programmatic dependent.
  *
  * seq_lens     NULL: attend over past_lens[b] + 1 tokens (the usual decode
  *              step).  Otherwise tokens attended per sequence; with
@@ -178,7 +181,7 @@ int b2_combine(const float *part_ml, const float *part_o, int32_t num_parts,
  *              (fp32 [batch][16][2] / [batch][16][64], as b2_combine) are
  *              given: the merged state of the attended tokens, for a
  *              further merge across GPUs.
- * counters     int32 [b2_decode_step_counters(batch)] (= 2); must be zero
+ * counters     int32 [b2_decode_step_counters(batch)] (= 2 + 8 * batch); must be zero
  *              before the first call; every call that completes leaves it
  *              zero again (after a device error, zero it again).
  * part_ml/o    as b2_decode_attn with num_splits = ceil(max_blocks / bps).

@@ -180,8 +180,8 @@ def decode_step(qkv: torch.Tensor, past_lens: torch.Tensor, *, k_pool: torch.Ten
     """Fused decode step in one persistent launch (b2_decode_step): norm + RoPE,
     append at past_lens[b], attention over past_lens[b] + 1 tokens (or
     seq_lens[b]), merge into `out` or into fp32 states (state_ml, state_o).
-    `counters` (int32[2]) must be zero on the first call; the kernel leaves
-    it zero.  Returns num_splits."""
+    `counters` (int32[2 + 8 * batch]) must be zero on the first call; the
+    kernel leaves it zero.  Returns num_splits."""
     dev = qkv.device
     if qkv.dim() != 2 or qkv.shape[1] < QKV_WIDTH:
         raise ValueError(f"qkv must be [batch, >= {QKV_WIDTH}], got {tuple(qkv.shape)}")
@@ -207,8 +207,8 @@ def decode_step(qkv: torch.Tensor, past_lens: torch.Tensor, *, k_pool: torch.Ten
     if q_out is not None:
         _need(q_out, "q_out", torch.bfloat16, dev, (b, HQ, D))
     _need(counters, "counters", torch.int32, dev)
-    if counters.numel() < 2:
-        raise ValueError("counters must hold 2 int32")
+    if counters.numel() < 2 + HKV * b:
+        raise ValueError("counters must hold 2 + 8 * batch int32")
     _need(dev_err, "dev_err", torch.int32, dev)
     rope_rows = 0
     if mode & _lib.B2_NORM_QK:
@@ -295,7 +295,7 @@ class PagedDecodeAttention:
         self.part_o = torch.empty(max_batch, self.num_splits, HQ, D, dtype=torch.float32, device=dev)
         self.out = torch.empty(max_batch, HQ, D, dtype=torch.bfloat16, device=dev)
         self.dev_err = torch.zeros(1, dtype=torch.int32, device=dev)
-        self.counters = torch.zeros(2, dtype=torch.int32, device=dev)
+        self.counters = torch.zeros(2 + HKV * max_batch, dtype=torch.int32, device=dev)
 
     def step(self, layer: int, qkv: torch.Tensor, past_lens: torch.Tensor, seq_lens: torch.Tensor,
              block_tables: torch.Tensor, out: torch.Tensor | None = None,

@@ -505,6 +505,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 3)
   }
 }
 
+
 // ------------------------------------------------------------------ combine
 
 struct CombineArgs {
@@ -624,10 +625,22 @@ struct __align__(16) StageMeta {
 // splits that lie past a sequence's end.
 constexpr int kMaxCompactBatch = 512;
 
+// Warps of the fused kernel: 4 consumers, 1 producer (TMA), 1 merger (the
+// cross-CTA arrival count and the merge of a sequence's splits, off the
+// consumers' path).
+constexpr int kProducerWarp = kConsumerWarps;
+constexpr int kMergerWarp = kConsumerWarps + 1;
+constexpr int kStepThreads = (kConsumerWarps + 2) * 32;
+constexpr int kPubSlots = 4;  // items published to the merger warp, in flight
+constexpr int kMergeInKernelSplits = 16;
+
 struct __align__(16) StepTail {
   uint64_t full[kStages];
   uint64_t empty[kStages];
   uint64_t ebar;  // consumer-warp barrier of the epilogue (bounded waits)
+  uint64_t pub[kPubSlots];    // consumers -> merger: a partial state is in memory
+  uint64_t pfree[kPubSlots];  // merger -> consumers: the slot may be reused
+  int4 pubinfo[kPubSlots];    // (b, kv head, split, nsplit); b < 0 ends the work
   StageMeta meta[kStages];
   float red[2][kConsumerWarps][2][2 + kDim];  // double-buffered by epilogue parity
   int prefix[kMaxCompactBatch + 1];  // prefix[b] = splits of sequences 0..b-1
@@ -649,11 +662,13 @@ struct StepArgs {
   int num_blocks;
   int batch, blocks_per_split, num_splits, total_items;
   int direct_out;  // whole-sequence items write the bf16 context themselves
+  int merge_here;  // the merger warp merges the splits (else a combine kernel follows)
   float scale_log2;
   int mode;
   uint16_t *out, *q_out;
+  float *state_ml, *state_o;  // merged fp32 state instead of out (direct_out == 0)
   float *part_ml, *part_o;
-  int32_t *counters;  // [0] work counter, [1] finished-CTA counter
+  int32_t *counters;  // [0] work counter, [1] finished CTAs, [2 + b * 8 + kv head] split arrivals
   int32_t *err;
 };
 
@@ -767,6 +782,28 @@ __device__ __forceinline__ void step_producer(const StepArgs &a, StepTail *tail,
     if (lane == 0) tail->prefix[0] = 0;
     __syncwarp();
     total = running * kHkv;
+  }
+  if (blockIdx.x == 0) {
+    // Sequences with nothing to attend (seq_lens[b] == 0) get no work item:
+    // write their empty result here (zero context, or the state (-inf, 0, 0)).
+    for (int b0 = 0; b0 < a.batch; b0 += 32) {
+      const int b = b0 + lane;
+      int past = 0, seq_len = 1;
+      const bool empty = b < a.batch && step_lengths(a, b, past, seq_len) && seq_len == 0;
+      unsigned mask = __ballot_sync(0xffffffffu, empty);
+      while (mask) {
+        const int e = b0 + __ffs(mask) - 1;
+        mask &= mask - 1;
+        for (int i = lane; i < kHq * kDim; i += 32) {
+          if (a.direct_out) a.out[(int64_t)e * kHq * kDim + i] = 0;
+          else a.state_o[(int64_t)e * kHq * kDim + i] = 0.f;
+        }
+        if (!a.direct_out && lane < kHq) {
+          a.state_ml[((int64_t)e * kHq + lane) * 2] = -1.0e30f;
+          a.state_ml[((int64_t)e * kHq + lane) * 2 + 1] = 0.f;
+        }
+      }
+    }
   }
   int issued = 0;
   bool ok = true;
@@ -966,6 +1003,80 @@ __device__ __forceinline__ void step_epilogue(const StepArgs &a, StepTail *tail,
   }
 }
 
+// Hand an item (or, with b < 0, the end of the work) to the merger warp.
+// Every consumer thread arrives (release) after its own stores of the
+// partial state, so the merger sees all of them when the phase completes.
+__device__ __forceinline__ void publish(const StepArgs &a, StepTail *tail, int lane, uint32_t &pubs, int b,
+                                        int kvh, int split, int nsplit) {
+  const int slot = pubs % kPubSlots;
+  if (pubs >= kPubSlots && !mbar_wait(smem_u32(&tail->pfree[slot]), ((pubs / kPubSlots) - 1) & 1)) {
+    if (lane == 0) atomicOr(a.err, B2_DEV_TIMEOUT);
+  }
+  if (threadIdx.x == 0) tail->pubinfo[slot] = make_int4(b, kvh, split, nsplit);
+  // all consumer threads must see the slot free before thread 0 overwrites it:
+  // the pfree wait above is done by every thread, and thread 0 writes after it
+  mbar_arrive(smem_u32(&tail->pub[slot]));
+  ++pubs;
+}
+
+// Merger warp: for every published item, count its arrival for (sequence,
+// kv head); the last split to arrive merges all splits of the sequence
+// (lane owns dims 2*lane, 2*lane+1 of both query heads) into the bf16
+// context, or into the fp32 state when the caller asked for states.
+__device__ __forceinline__ void step_merger(const StepArgs &a, StepTail *tail, int lane) {
+  for (uint32_t k = 0;; ++k) {
+    const int slot = k % kPubSlots;
+    if (!mbar_wait(smem_u32(&tail->pub[slot]), (k / kPubSlots) & 1)) {
+      if (lane == 0) atomicOr(a.err, B2_DEV_TIMEOUT);
+      return;
+    }
+    const int4 info = tail->pubinfo[slot];
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(&tail->pfree[slot]));
+    if (info.x < 0) return;
+    const int b = info.x, kvh = info.y, nsplit = info.w;
+    int32_t *cnt = a.counters + 2 + b * kHkv + kvh;
+    int last = 0;
+    if (lane == 0) {
+      __threadfence();  // release the consumers' partial-state stores at GPU scope
+      last = atomicAdd(cnt, 1) == nsplit - 1;
+      if (last) __threadfence();  // acquire the other CTAs' partial states
+    }
+    last = __shfl_sync(0xffffffffu, last, 0);
+    __syncwarp();
+    if (!last) continue;
+    const int64_t base = (int64_t)b * a.num_splits * kHq + 2 * kvh;  // (b, split 0, head 2kvh)
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const float *ml = a.part_ml + (base + hh) * 2;
+      const float *po = a.part_o + (base + hh) * kDim + 2 * lane;
+      float M = -1.0e30f, L = 0.f, O0 = 0.f, O1 = 0.f;
+      for (int sp = 0; sp < nsplit; ++sp) {
+        const float ms = __ldcg(ml + sp * kHq * 2), ls = __ldcg(ml + sp * kHq * 2 + 1);
+        const float2 o = __ldcg(reinterpret_cast<const float2 *>(po + (int64_t)sp * kHq * kDim));
+        const float nm = fmaxf(M, ms);
+        const float c1 = ex2(M - nm), c2 = ex2(ms - nm);
+        L = L * c1 + ls * c2;
+        O0 = O0 * c1 + o.x * c2;
+        O1 = O1 * c1 + o.y * c2;
+        M = nm;
+      }
+      const int64_t oi = ((int64_t)b * kHq + 2 * kvh + hh) * kDim + 2 * lane;
+      if (a.direct_out) {
+        *reinterpret_cast<uint32_t *>(a.out + oi) = bf16_bits(O0 / L) | (bf16_bits(O1 / L) << 16);
+      } else {
+        *reinterpret_cast<float2 *>(a.state_o + oi) = make_float2(O0, O1);
+        if (lane == 0) {
+          a.state_ml[((int64_t)b * kHq + 2 * kvh + hh) * 2] = M;
+          a.state_ml[((int64_t)b * kHq + 2 * kvh + hh) * 2 + 1] = L;
+        }
+      }
+    }
+    if (lane == 0) atomicExch(cnt, 0);
+  }
+}
+
+
 // Consumer warp w owns token rows [16w, 16w+16) of every 64-token tile.  Both
 // products run on the tensor cores with mma.sync m16n8k16 (bf16 in, fp32
 // accumulate), operands fetched from the 128-byte-swizzled tiles with
@@ -993,6 +1104,7 @@ __device__ __forceinline__ void step_consumer(const StepArgs &a, StepTail *tail,
   for (int ks = 0; ks < 4; ++ks) bq[ks][0] = bq[ks][1] = 0u;
   uint32_t ephase = 0;  // completed phases of the epilogue barrier
   int epilogues = 0;    // red[] buffer parity
+  uint32_t pubs = 0;    // items published to the merger warp
   // ldmatrix row addresses (without the stage base): rows of this lane's
   // sub-matrix, the 16-byte chunk index is added per k-step / m-tile.
   const int qk_row = 16 * warp + (lane & 7) + 8 * (j & 1);
@@ -1007,7 +1119,7 @@ __device__ __forceinline__ void step_consumer(const StepArgs &a, StepTail *tail,
     const StageMeta &meta = tail->meta[s];
     const int flags = meta.flags;
     if (flags & kFlagEnd) break;
-    const int b = meta.b, kvh = meta.kvh, split = meta.split;
+    const int b = meta.b, kvh = meta.kvh, split = meta.split, meta_nsplit = meta.nsplit;
     const int valid = meta.rows - 16 * warp;  // valid rows of this warp (may be <= 0 or >= 16)
     if (flags & kFlagFirst) {
       // B fragment of Q^T: (k = 2t, 2t+1 | 2t+8, 2t+9 of the k-step, n = g)
@@ -1090,13 +1202,17 @@ __device__ __forceinline__ void step_consumer(const StepArgs &a, StepTail *tail,
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(smem_u32(&tail->empty[s]));
-    if (flags & kFlagLast)
-      step_epilogue(a, tail, warp, lane, b, kvh, split, (flags & kFlagFinal) != 0, m0, m1, l0, l1, o, ephase,
+    if (flags & kFlagLast) {
+      const bool final_item = (flags & kFlagFinal) != 0;
+      step_epilogue(a, tail, warp, lane, b, kvh, split, final_item, m0, m1, l0, l1, o, ephase,
                     (epilogues++) & 1);
+      if (!final_item && a.merge_here) publish(a, tail, lane, pubs, b, kvh, split, meta_nsplit);
+    }
   }
+  publish(a, tail, lane, pubs, -1, 0, 0, 0);  // end of work for the merger warp
 }
 
-__global__ void __launch_bounds__(kDecodeThreads, 3)
+__global__ void __launch_bounds__(kStepThreads, 3)
     decode_step_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                        const StepArgs a) {
   extern __shared__ uint8_t smem_raw[];
@@ -1112,6 +1228,11 @@ __global__ void __launch_bounds__(kDecodeThreads, 3)
       mbar_init(smem_u32(&tail->empty[s]), kConsumerWarps);
     }
     mbar_init(smem_u32(&tail->ebar), kConsumerWarps);
+#pragma unroll
+    for (int s = 0; s < kPubSlots; ++s) {
+      mbar_init(smem_u32(&tail->pub[s]), kConsumerWarps * 32);
+      mbar_init(smem_u32(&tail->pfree[s]), 1);
+    }
     mbar_fence_init();
   }
   __syncthreads();
@@ -1119,12 +1240,14 @@ __global__ void __launch_bounds__(kDecodeThreads, 3)
   // stream: the set-up above overlaps its tail; wait for its completion (and
   // memory) before touching global memory.  A no-op for an ordinary launch.
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  // Let the combine kernel be scheduled as soon as CTAs of this grid retire;
-  // it waits for this grid's completion before reading the partial states.
+  // A dependent launched with programmatic serialization may start its own
+  // set-up now; it waits for this grid's completion before reading memory.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
-  if (warp == kConsumerWarps)
+  if (warp == kProducerWarp)
     step_producer(a, tail, tiles, &tm_k, &tm_v, lane);
+  else if (warp == kMergerWarp)
+    step_merger(a, tail, lane);
   else
     step_consumer(a, tail, tiles, warp, lane);
   __syncthreads();
@@ -1311,7 +1434,7 @@ extern "C" int b2_combine(const float *part_ml, const float *part_o, int32_t num
   return launch_status("combine_kernel");
 }
 
-extern "C" int b2_decode_step_counters(int32_t batch) { return batch < 0 ? 0 : 2; }
+extern "C" int b2_decode_step_counters(int32_t batch) { return batch < 0 ? 0 : 2 + batch * kHkv; }
 
 extern "C" int b2_decode_step(const uint16_t *qkv, int64_t row_stride, const uint16_t *gamma_q,
                               const uint16_t *gamma_k, float eps, const uint16_t *rope_cos,
@@ -1354,10 +1477,14 @@ extern "C" int b2_decode_step(const uint16_t *qkv, int64_t row_stride, const uin
   if (rc) return rc;
   if (!step_smem_ready()) return fail(B2_ERR_CUDA, "cannot set the decode-step kernel's shared memory size");
   const int direct_out = state_o == nullptr;
+  // One warp merges a (sequence, kv head)'s splits serially: right for a
+  // handful of splits; long single sequences with many splits are merged by
+  // the parallel combine kernel instead.
+  const int merge_here = splits <= kMergeInKernelSplits;
   StepArgs a{qkv, row_stride, gamma_q, gamma_k, eps, rope_cos, rope_sin, rope_rows, past_lens, seq_lens,
              block_tables, max_blocks_per_seq, k_pool, v_pool, num_blocks, batch, blocks_per_split,
-             static_cast<int>(splits), static_cast<int>(total), direct_out, scale * 1.4426950408889634f, mode, out,
-             q_out, part_ml, part_o, counters, dev_err};
+             static_cast<int>(splits), static_cast<int>(total), direct_out, merge_here,
+             scale * 1.4426950408889634f, mode, out, q_out, state_ml, state_o, part_ml, part_o, counters, dev_err};
   int64_t ctas = static_cast<int64_t>(sm_count()) * 3;
   if (max_ctas > 0 && max_ctas < ctas) ctas = max_ctas;
   if (ctas > total) ctas = total;
@@ -1370,7 +1497,7 @@ extern "C" int b2_decode_step(const uint16_t *qkv, int64_t row_stride, const uin
     // griddepcontrol.wait at the top of the kernel)
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(ctas));
-    cfg.blockDim = dim3(kDecodeThreads);
+    cfg.blockDim = dim3(kStepThreads);
     cfg.dynamicSmemBytes = kStepSmem;
     cfg.stream = st;
     cfg.attrs = pdl;
@@ -1381,9 +1508,9 @@ extern "C" int b2_decode_step(const uint16_t *qkv, int64_t row_stride, const uin
     }
   }
   rc = launch_status("decode_step_kernel");
-  if (rc) return rc;
-  // Merge the split sequences; launched as a programmatic dependent so that
-  // its launch overlaps the decode kernel's last CTAs.
+  if (rc || merge_here) return rc;
+  // Many splits: merge them with the parallel combine kernel, launched as a
+  // programmatic dependent so that its launch overlaps the decode tail.
   CombineArgs c{part_ml, part_o, static_cast<int>(splits), seq_lens ? seq_lens : past_lens, blocks_per_split, out,
                 state_ml, state_o, seq_lens ? 0 : 1, direct_out, static_cast<int>(splits) * blocks_per_split * kBlock,
                 0, 0, 0, 0, combine_groups(static_cast<int>(splits))};

@@ -117,7 +117,7 @@ class LongContextDecode:
         self.state_o = self.state[HQ * 2:].view(1, HQ, D)
         self.out = torch.empty(1, HQ, D, dtype=torch.bfloat16, device=self.device)
         self.dev_err = torch.zeros(1, dtype=torch.int32, device=self.device)
-        self.counters = torch.zeros(2, dtype=torch.int32, device=self.device)
+        self.counters = torch.zeros(2 + 8, dtype=torch.int32, device=self.device)
         self.past = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.seq = torch.zeros(1, dtype=torch.int32, device=self.device)
 

@@ -264,7 +264,7 @@ def test_fused_multi_step_decode_vs_oracle(cuda):
             assert torch.equal(vs[i], v_all)
 
 
-@pytest.mark.parametrize("total,cut", [(300, 128), (5000, 2048), (64, 64), (10, 64)])
+@pytest.mark.parametrize("total,cut", [(300, 128), (5000, 2048), (64, 64), (10, 64), (10, 0)])
 def test_split_sequence_states_merge(cuda, total, cut):
     """One sequence split along the token axis as two GPUs would hold it,
     emulated on one GPU: the head part attends over its tokens only (seq_lens,
@@ -299,7 +299,7 @@ def test_split_sequence_states_merge(cuda, total, cut):
         mode = _lib().B2_NORM_QK | _lib().B2_ROPE_QK | (_lib().B2_STORE_KV if tail else 0)
         attn.decode_step(raw.to(cuda), past, k_pool=kp, v_pool=vp, block_tables=cache.block_tables(),
                          blocks_per_split=2, out=None, part_ml=ml, part_o=po,
-                         counters=torch.zeros(2, dtype=torch.int32, device=cuda), dev_err=err,
+                         counters=torch.zeros(2 + 8, dtype=torch.int32, device=cuda), dev_err=err,
                          gamma_q=w["q_gamma"].to(cuda), gamma_k=w["k_gamma"].to(cuda), cos=cos[lo:], sin=sin[lo:],
                          seq_lens=None if tail else seq, state_ml=sml, state_o=so, mode=mode)
         torch.cuda.synchronize()
