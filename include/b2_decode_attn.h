@@ -216,6 +216,40 @@ int b2_merge_states(const float *states, int32_t num_parts, int32_t batch,
                     void *stream);
 
 /*
+ * Batched-prompt (prefill) attention: a chunk of `tokens` new tokens per
+ * sequence, rows qkv[b * tokens + t] (chunk_lens[b] <= tokens valid, NULL:
+ * all), token t at position past_lens[b] + t.
+ *
+ * b2_prefill_append: q/k RMSNorm + RoPE and the append of every chunk token's
+ * k/v (the decode append, one CTA per token); q_out [batch][tokens][16][64].
+ * b2_prefill_attn: each chunk token attends to the cached tokens and
+ * causally to the chunk (query t sees positions <= past_lens[b] + t), on the
+ * tcgen05 tensor cores: one CTA per (64-token query tile, kv head, sequence)
+ * computes S = Q.K^T and P.V as 128 x 64 x 64 MMAs with the accumulators in
+ * tensor memory.  out [batch][tokens][16][64] bf16.
+ *
+ * Replaces the reference's batched prompt attention: the x8p engine's
+ * attn_prep / attn_block4 (4 tokens x 2 heads per KV head, cached part then
+ * causal in-batch part, experiments/kernels/x8/x8p_core.cc:137-226) and the
+ * prefill pair operator (experiments/lfm25_prefill_pair_attention_context_kernel.py:21-85).
+ */
+int b2_prefill_append(const uint16_t *qkv, int64_t row_stride,
+                      const uint16_t *gamma_q, const uint16_t *gamma_k, float eps,
+                      const uint16_t *rope_cos, const uint16_t *rope_sin,
+                      int32_t rope_rows, const int32_t *past_lens,
+                      const int32_t *chunk_lens, int32_t tokens,
+                      const int32_t *block_tables, int32_t max_blocks_per_seq,
+                      uint16_t *k_pool, uint16_t *v_pool, int32_t num_blocks,
+                      uint16_t *q_out, int32_t batch, int32_t mode,
+                      int32_t *dev_err, void *stream);
+int b2_prefill_attn(const uint16_t *q, const uint16_t *k_pool,
+                    const uint16_t *v_pool, int32_t num_blocks,
+                    const int32_t *block_tables, int32_t max_blocks_per_seq,
+                    const int32_t *past_lens, const int32_t *chunk_lens,
+                    int32_t tokens, int32_t batch, float scale,
+                    uint16_t *out, int32_t *dev_err, void *stream);
+
+/*
  * Allocation-free decode: b2_decode_attn followed by b2_combine, with the
  * partial softmax states kept in a static device array inside this library
  * instead of caller-provided part_ml / part_o buffers.  It has no counterpart

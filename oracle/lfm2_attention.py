@@ -225,6 +225,29 @@ def decode_step(qkv_row: torch.Tensor, k_past: torch.Tensor, v_past: torch.Tenso
     return ctx.reshape(HQ, D), k_all[0], v_all[0], q[0]
 
 
+def prefill_step(qkv_rows: torch.Tensor, k_past: torch.Tensor, v_past: torch.Tensor, past: int,
+                 gamma_q, gamma_k, eps: float = EPS):
+    """A chunk of T new tokens of one sequence through Lfm2Attention.forward
+    from the projections on (modeling_lfm2.py:254-277 with T > 1): per-token
+    q/k norm + RoPE at positions past..past+T-1, the cache grown by the T
+    rows, and sdpa with the causal mask transformers builds for a cached
+    prefix (query t sees keys 0..past+t; with a mask, sdpa gets repeat_kv'd
+    K/V, integrations/sdpa_attention.py:57-60).  qkv_rows [T, 2048];
+    k_past/v_past [8, past, 64].  Returns (context [T, 16, 64], k_all, v_all)."""
+    t = qkv_rows.shape[0]
+    q_raw, k_raw, v = split_qkv(qkv_rows)
+    cos, sin = rope_cos_sin(list(range(past, past + t)))
+    q, k = norm_rope_qk(q_raw, k_raw, gamma_q, gamma_k, cos, sin, eps)    # [T, 16, 64], [T, 8, 64]
+    k_all = torch.cat([k_past, k.transpose(0, 1)], dim=1)                # [8, past+T, 64]
+    v_all = torch.cat([v_past, v.transpose(0, 1)], dim=1)
+    keys = torch.arange(past + t)
+    mask = keys[None, :] <= (past + torch.arange(t))[:, None]            # [T, past+T] bool
+    out = torch.nn.functional.scaled_dot_product_attention(
+        q.transpose(0, 1)[None], repeat_kv(k_all[None], HQ // HKV), repeat_kv(v_all[None], HQ // HKV),
+        attn_mask=mask[None, None], dropout_p=0.0, scale=SCALE)
+    return out[0].transpose(0, 1).contiguous(), k_all, v_all
+
+
 def attention_layer_step(x: torch.Tensor, w: dict, k_past: torch.Tensor, v_past: torch.Tensor,
                          position: int, impl: str = "sdpa"):
     """Whole Lfm2Attention.forward for one decode token (config C1): x [1, 1, H].

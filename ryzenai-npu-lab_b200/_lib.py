@@ -79,6 +79,22 @@ SIGNATURES = {
         _p, _i32, _i32,      # states, num_parts, batch
         _p, _p, _p, _p,      # out, state_ml, state_o, stream
     ]),
+    "b2_prefill_append": (ctypes.c_int, [
+        _p, _i64,            # qkv, row_stride
+        _p, _p, _f32,        # gamma_q, gamma_k, eps
+        _p, _p, _i32,        # rope_cos, rope_sin, rope_rows
+        _p, _p, _i32,        # past_lens, chunk_lens, tokens
+        _p, _i32,            # block_tables, max_blocks_per_seq
+        _p, _p, _i32,        # k_pool, v_pool, num_blocks
+        _p, _i32, _i32,      # q_out, batch, mode
+        _p, _p,              # dev_err, stream
+    ]),
+    "b2_prefill_attn": (ctypes.c_int, [
+        _p, _p, _p, _i32,    # q, k_pool, v_pool, num_blocks
+        _p, _i32,            # block_tables, max_blocks_per_seq
+        _p, _p, _i32, _i32,  # past_lens, chunk_lens, tokens, batch
+        _f32, _p, _p, _p,    # scale, out, dev_err, stream
+    ]),
     "b2_decode_attn_noalloc": (ctypes.c_int, [
         _p, _p, _p, _i32,    # q, k_pool, v_pool, num_blocks
         _p, _i32,            # block_tables, max_blocks_per_seq

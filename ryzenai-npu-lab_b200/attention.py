@@ -255,6 +255,56 @@ def merge_states(states: torch.Tensor, num_parts: int, batch: int, *, out: torch
     _lib.check(rc, "b2_merge_states")
 
 
+def prefill(qkv: torch.Tensor, past_lens: torch.Tensor, *, k_pool: torch.Tensor, v_pool: torch.Tensor,
+            block_tables: torch.Tensor, gamma_q: torch.Tensor, gamma_k: torch.Tensor, cos: torch.Tensor,
+            sin: torch.Tensor, dev_err: torch.Tensor, chunk_lens: torch.Tensor | None = None,
+            out: torch.Tensor | None = None, q_out: torch.Tensor | None = None, eps: float = EPS,
+            scale: float = SCALE, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """Batched-prompt attention (b2_prefill_append + b2_prefill_attn): qkv bf16
+    [B, T, >= 2048] raw projections of T new tokens per sequence at positions
+    past_lens[b] + t (chunk_lens[b] <= T valid).  Appends their k/v and returns
+    the context [B, T, 16, 64]."""
+    dev = qkv.device
+    if qkv.dim() != 3 or qkv.shape[2] < QKV_WIDTH:
+        raise ValueError(f"qkv must be [batch, tokens, >= {QKV_WIDTH}], got {tuple(qkv.shape)}")
+    _need(qkv, "qkv", torch.bfloat16, dev)
+    b, t = qkv.shape[0], qkv.shape[1]
+    _need(past_lens, "past_lens", torch.int32, dev, (b,))
+    if chunk_lens is not None:
+        _need(chunk_lens, "chunk_lens", torch.int32, dev, (b,))
+    _need(k_pool, "k_pool", torch.bfloat16, dev)
+    _need(v_pool, "v_pool", torch.bfloat16, dev, tuple(k_pool.shape))
+    if k_pool.dim() != 4 or tuple(k_pool.shape[1:]) != (HKV, BLOCK, D):
+        raise ValueError("pools must be [num_blocks, 8, 64, 64]")
+    _need(block_tables, "block_tables", torch.int32, dev)
+    if block_tables.dim() != 2 or block_tables.shape[0] != b:
+        raise ValueError("block_tables must be [batch, max_blocks_per_seq]")
+    _need(gamma_q, "gamma_q", torch.bfloat16, dev, (D,))
+    _need(gamma_k, "gamma_k", torch.bfloat16, dev, (D,))
+    _need(cos, "cos", torch.bfloat16, dev)
+    _need(sin, "sin", torch.bfloat16, dev, tuple(cos.shape))
+    _need(dev_err, "dev_err", torch.int32, dev)
+    if q_out is None:
+        q_out = torch.empty(b, t, HQ, D, dtype=torch.bfloat16, device=dev)
+    _need(q_out, "q_out", torch.bfloat16, dev, (b, t, HQ, D))
+    if out is None:
+        out = torch.empty(b, t, HQ, D, dtype=torch.bfloat16, device=dev)
+    _need(out, "out", torch.bfloat16, dev, (b, t, HQ, D))
+    lib = _lib.load()
+    st = _stream(dev, stream)
+    mode = _lib.B2_NORM_QK | _lib.B2_ROPE_QK | _lib.B2_STORE_KV
+    rc = lib.b2_prefill_append(_ptr(qkv), qkv.stride(1), _ptr(gamma_q), _ptr(gamma_k), ctypes.c_float(eps),
+                               _ptr(cos), _ptr(sin), cos.shape[0], _ptr(past_lens), _ptr(chunk_lens), t,
+                               _ptr(block_tables), block_tables.shape[1], _ptr(k_pool), _ptr(v_pool),
+                               k_pool.shape[0], _ptr(q_out), b, mode, _ptr(dev_err), st)
+    _lib.check(rc, "b2_prefill_append")
+    rc = lib.b2_prefill_attn(_ptr(q_out), _ptr(k_pool), _ptr(v_pool), k_pool.shape[0], _ptr(block_tables),
+                             block_tables.shape[1], _ptr(past_lens), _ptr(chunk_lens), t, b,
+                             ctypes.c_float(scale), _ptr(out), _ptr(dev_err), st)
+    _lib.check(rc, "b2_prefill_attn")
+    return out
+
+
 class PagedDecodeAttention:
     """Decode attention of one new token per sequence over a PagedKVCache.
 

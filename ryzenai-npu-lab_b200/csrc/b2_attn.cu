@@ -188,6 +188,8 @@ struct AppendArgs {
   uint16_t *q_out;
   int mode;
   int32_t *err;
+  int tokens;                 // tokens per sequence in qkv / q_out rows (1 for decode)
+  const int32_t *chunk_lens;  // valid tokens per sequence (NULL: all `tokens`)
 };
 
 // Per-head RMSNorm (optional) and rotate-half RoPE (optional) of one 64-wide
@@ -236,21 +238,25 @@ __device__ __forceinline__ void norm_rope8(float x[8], int j, bool norm, bool ro
   }
 }
 
-// One CTA (8 warps) per sequence.  The 32 head vectors of a qkv row
-// (16 q, 8 k, 8 v) are split 4 per warp; 8 lanes own one vector, 8
-// consecutive bf16 (16 bytes) each, so loads and stores are 16-byte
-// vectors and a vector's rotate-half partner chunk (d +- 32) sits on lane^4.
+// One CTA (8 warps) per token: grid (sequence, token of the chunk).  The 32
+// head vectors of a qkv row (16 q, 8 k, 8 v) are split 4 per warp; 8 lanes
+// own one vector, 8 consecutive bf16 (16 bytes) each, so loads and stores
+// are 16-byte vectors and a vector's rotate-half partner chunk (d +- 32)
+// sits on lane^4.  Token t of sequence b goes to position past_lens[b] + t.
 __global__ void __launch_bounds__(256) append_rope_kernel(const AppendArgs a) {
   const int b = blockIdx.x;
+  const int tok = blockIdx.y;
+  if (a.chunk_lens && tok >= a.chunk_lens[b]) return;
+  const int64_t row = (int64_t)b * a.tokens + tok;
   const int lane = threadIdx.x & 31;
   const int vec = (threadIdx.x >> 5) * 4 + (lane >> 3);  // 0..31
   const int j = lane & 7;                                // 16-byte chunk
   const bool is_q = vec < kHq;
   const bool is_v = vec >= kHq + kHkv;
-  const int pos = a.past_lens[b];
+  const int pos = a.past_lens[b] + tok;
 
   float x[8];
-  unpack8(*reinterpret_cast<const uint4 *>(a.qkv + b * a.row_stride + vec * kDim + j * 8), x);
+  unpack8(*reinterpret_cast<const uint4 *>(a.qkv + row * a.row_stride + vec * kDim + j * 8), x);
   const bool pos_ok = pos >= 0 && pos < a.max_blocks * kBlock;
   const bool rope_ok = pos >= 0 && pos < a.rope_rows;
   if ((a.mode & B2_ROPE_QK) && !rope_ok && j == 0 && vec == 0) atomicOr(a.err, B2_DEV_BAD_POSITION);
@@ -260,7 +266,7 @@ __global__ void __launch_bounds__(256) append_rope_kernel(const AppendArgs a) {
 
   if (is_q) {
     if (a.q_out)
-      *reinterpret_cast<uint4 *>(a.q_out + ((int64_t)b * kHq + vec) * kDim + j * 8) = pack8(x);
+      *reinterpret_cast<uint4 *>(a.q_out + (row * kHq + vec) * kDim + j * 8) = pack8(x);
     return;
   }
   if (!(a.mode & B2_STORE_KV)) return;
@@ -1262,6 +1268,303 @@ __global__ void __launch_bounds__(kStepThreads, 3)
   }
 }
 
+// ------------------------------------------------------------------ batched-prompt attention (tcgen05)
+
+// A chunk of T new tokens per sequence (a prompt, or the x8p engine's
+// 4-token batches, experiments/kernels/x8/x8p_core.cc:137-226) attends to
+// the cached tokens and causally to the chunk.  Per (64-token query tile, KV
+// head, sequence) one CTA holds a 128-row query tile (64 tokens x the GQA
+// pair) and streams the sequence's 64-token K/V blocks:
+//   S[128 x 64]  = Q[128 x 64] . K_blk^T          tcgen05.mma, M=128 N=64 K=64
+//   PV[128 x 64] = P[128 x 64] . V_blk            (P bf16 in shared memory)
+// with both results in tensor memory (128 columns).  One thread per query
+// row runs the online softmax in registers from tcgen05.ld; a producer warp
+// feeds the K/V tiles with TMA (128-byte swizzle, the layout the MMA reads:
+// K-major for K, MN-major for V).
+
+constexpr int kPfStages = 3;
+constexpr int kPfThreads = 5 * 32;  // 4 softmax warps (one query row per thread) + 1 TMA warp
+constexpr int kPfTmemCols = 128;    // S at column 0, PV at column 64
+constexpr uint32_t kPfIdescS = (1u << 4) | (1u << 7) | (1u << 10) | (8u << 17) | (8u << 24);  // f32 <- bf16, M128 N64, K-major
+constexpr uint32_t kPfIdescPV = kPfIdescS | (1u << 16);  // B (V) MN-major
+
+struct __align__(8) PrefillTail {
+  uint64_t full[kPfStages];
+  uint64_t empty[kPfStages];
+  uint64_t sbar, pvbar;
+  uint32_t tmem_base;
+  int abort;
+};
+constexpr int kPfSmem = 1024 + 2 * 16384 + kPfStages * kStageBytes + (int)sizeof(PrefillTail);
+
+struct PrefillArgs {
+  const uint16_t *q;  // [batch][tokens][16][64] normalised + rotated
+  const int32_t *block_tables;
+  int max_blocks;
+  const int32_t *past_lens;
+  const int32_t *chunk_lens;
+  int tokens;
+  int num_blocks;
+  float scale_log2;
+  uint16_t *out;  // [batch][tokens][16][64]
+  int32_t *err;
+};
+
+// Shared-memory matrix descriptor for tcgen05.mma: 128-byte swizzle, rows of
+// 128 bytes, 8-row groups 1024 bytes apart (SBO); LBO as given (unused for a
+// single swizzle atom along the contiguous dimension); version 1 (sm_100).
+__device__ __forceinline__ uint64_t umma_desc(uint32_t smem_addr, uint32_t lbo_bytes) {
+  return (uint64_t)((smem_addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16) |
+         ((uint64_t)(1024u >> 4) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void tmem_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tmem_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 16 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float v[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void pf_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// Barrier of the 4 softmax warps that also ORs a flag across them, so that a
+// decision taken after it is the same in every thread.
+__device__ __forceinline__ int pf_bar_or(int flag) {
+  int out;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.b32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, 1, 128, p;\n\tselp.b32 %0, 1, 0, q;\n\t}"
+      : "=r"(out)
+      : "r"(flag)
+      : "memory");
+  return out;
+}
+
+__global__ void __launch_bounds__(kPfThreads, 2)
+    prefill_attn_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                        const PrefillArgs a) {
+  const int tile = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int past = a.past_lens[b];
+  const int T = a.chunk_lens ? a.chunk_lens[b] : a.tokens;
+  const int t0 = tile * 64;
+  if (t0 >= T) return;
+  if (past < 0 || T > a.tokens || past + T > a.max_blocks * kBlock) {
+    if (threadIdx.x == 0 && tile == 0 && kvh == 0) atomicOr(a.err, B2_DEV_BAD_LENGTH);
+    return;
+  }
+  const int rows_t = min(64, T - t0);
+  const int last_key = past + t0 + rows_t - 1;  // the tile's highest query position
+  const int nblk = last_key / kBlock + 1;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *sQ = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t *sP = sQ + 16384;
+  uint8_t *ring = sP + 16384;
+  PrefillTail *tail = reinterpret_cast<PrefillTail *>(ring + kPfStages * kStageBytes);
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+
+  if (tid == 0) {
+#pragma unroll
+    for (int s = 0; s < kPfStages; ++s) {
+      mbar_init(smem_u32(&tail->full[s]), 1);
+      mbar_init(smem_u32(&tail->empty[s]), 1);
+    }
+    mbar_init(smem_u32(&tail->sbar), 1);
+    mbar_init(smem_u32(&tail->pvbar), 1);
+    tail->abort = 0;
+    mbar_fence_init();
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tail->tmem_base)),
+                 "n"(kPfTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  // query tile: row r = (head of the pair) * 64 + token, 128 bytes, swizzled
+  if (tid < 128) {
+    const int hl = tid >> 6, t = tid & 63;
+    const uint4 *src = reinterpret_cast<const uint4 *>(
+        a.q + (((int64_t)b * a.tokens + t0 + t) * kHq + 2 * kvh + hl) * kDim);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const uint4 v = t < rows_t ? src[c] : make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4 *>(sQ + tid * 128 + ((c ^ (tid & 7)) << 4)) = v;
+    }
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  tmem_fence_before();
+  __syncthreads();
+  tmem_fence_after();
+  const uint32_t tmem = tail->tmem_base;
+
+  if (warp == 4) {
+    // ---------------- TMA producer
+    if (lane == 0) {
+      const uint64_t policy = evict_first_policy();
+      const int32_t *tbl = a.block_tables + (int64_t)b * a.max_blocks;
+      int issued = 0;
+      for (int j = 0; j < nblk; ++j) {
+        const int s = j % kPfStages;
+        const uint32_t ph = (j / kPfStages) & 1;
+        if (j >= kPfStages && !mbar_wait(smem_u32(&tail->empty[s]), ph ^ 1)) {
+          atomicOr(a.err, B2_DEV_TIMEOUT);
+          tail->abort = 1;
+          break;
+        }
+        int blk = tbl[j];
+        if (blk < 0 || blk >= a.num_blocks) {
+          atomicOr(a.err, B2_DEV_BAD_BLOCK);
+          blk = 0;
+        }
+        const int row = (blk * kHkv + kvh) * kBlock;
+        uint8_t *dst = ring + s * kStageBytes;
+        const uint32_t full = smem_u32(&tail->full[s]);
+        mbar_expect_tx(full, kStageBytes);
+        tma_load_2d(smem_u32(dst), &tm_k, 0, row, full, policy);
+        tma_load_2d(smem_u32(dst + kTileBytes), &tm_v, 0, row, full, policy);
+        issued = j + 1;
+      }
+      // wait (bounded) until every issued copy has landed before leaving
+      for (int s = 0; s < kPfStages && s < issued; ++s) {
+        const int last = s + kPfStages * ((issued - 1 - s) / kPfStages);
+        if (!mbar_wait(smem_u32(&tail->full[s]), (last / kPfStages) & 1)) atomicOr(a.err, B2_DEV_TIMEOUT);
+      }
+    }
+  } else {
+    // ---------------- softmax / epilogue warps: thread = query row
+    const int hl = tid >> 6, t = tid & 63;
+    const bool row_ok = t < rows_t;
+    const int qpos = past + t0 + t;
+    const uint32_t trow = tmem + ((uint32_t)(32 * warp) << 16);
+    float O[64];
+#pragma unroll
+    for (int i = 0; i < 64; ++i) O[i] = 0.f;
+    float m = -1.0e30f, l = 0.f;
+    for (int j = 0; j < nblk; ++j) {
+      const int s = j % kPfStages;
+      const uint32_t ph = (j / kPfStages) & 1;
+      const uint32_t kt = smem_u32(ring + s * kStageBytes);
+      const uint32_t vt = kt + kTileBytes;
+      if (tid == 0) {
+        if (mbar_wait(smem_u32(&tail->full[s]), ph)) {
+          tmem_fence_after();
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks)
+            umma_f16(tmem, umma_desc(smem_u32(sQ) + 32 * ks, 16), umma_desc(kt + 32 * ks, 16), kPfIdescS, ks > 0);
+          umma_commit(smem_u32(&tail->sbar));
+        } else {
+          atomicOr(a.err, B2_DEV_TIMEOUT);
+          tail->abort = 1;
+          mbar_arrive(smem_u32(&tail->sbar));  // let the other rows through
+        }
+      }
+      mbar_wait(smem_u32(&tail->sbar), j & 1);
+      tmem_fence_after();
+      // scores of this row, masked: causal within the chunk, nothing past the tile
+      float sc[64];
+#pragma unroll
+      for (int c = 0; c < 64; c += 16) tmem_ld16(trow + c, sc + c);
+      const int key0 = j * kBlock;
+      float bm = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        sc[c] = (row_ok && key0 + c <= qpos) ? sc[c] * a.scale_log2 : -INFINITY;
+        bm = fmaxf(bm, sc[c]);
+      }
+      const float mn = fmaxf(m, bm);
+      const float alpha = ex2(m - mn);
+      m = mn;
+      float ps = 0.f;
+#pragma unroll
+      for (int c = 0; c < 64; c += 8) {
+        float p8[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          p8[e] = ex2(sc[c + e] - mn);
+          ps += p8[e];
+        }
+        *reinterpret_cast<uint4 *>(sP + tid * 128 + (((c >> 3) ^ (tid & 7)) << 4)) = pack8(p8);
+      }
+      l = fmaf(l, alpha, ps);
+      if (key0 + kBlock - 1 > last_key) {
+        // rows of the last block past every query of the tile may hold stale
+        // (even NaN) data: zero them so that P = 0 cannot meet them in P.V
+        // (after the stage's copy has landed, so the copy cannot overwrite)
+        mbar_wait(smem_u32(&tail->full[s]), ph);
+        const int first_bad = last_key - key0 + 1;
+        uint8_t *v_gen = ring + s * kStageBytes + kTileBytes;
+        for (int i = tid; i < (kBlock - first_bad) * 8; i += 128)
+          *reinterpret_cast<uint4 *>(v_gen + (first_bad + (i >> 3)) * 128 + ((i & 7) << 4)) = make_uint4(0, 0, 0, 0);
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      tmem_fence_before();
+      pf_bar();
+      if (tid == 0) {
+        tmem_fence_after();
+        if (!tail->abort) {
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks)
+            umma_f16(tmem + 64, umma_desc(smem_u32(sP) + 32 * ks, 16), umma_desc(vt + 2048 * ks, 0), kPfIdescPV,
+                     ks > 0);
+          umma_commit(smem_u32(&tail->pvbar));
+          umma_commit(smem_u32(&tail->empty[s]));
+        } else {
+          mbar_arrive(smem_u32(&tail->pvbar));
+        }
+      }
+      mbar_wait(smem_u32(&tail->pvbar), j & 1);
+      tmem_fence_after();
+#pragma unroll
+      for (int c = 0; c < 64; c += 16) {
+        float pv[16];
+        tmem_ld16(trow + 64 + c, pv);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) O[c + e] = fmaf(O[c + e], alpha, pv[e]);
+      }
+      tmem_fence_before();
+      if (pf_bar_or(tail->abort)) break;
+    }
+    if (row_ok && !tail->abort) {
+      const float inv = 1.0f / l;
+      uint4 *dst = reinterpret_cast<uint4 *>(a.out + (((int64_t)b * a.tokens + t0 + t) * kHq + 2 * kvh + hl) * kDim);
+#pragma unroll
+      for (int c = 0; c < 64; c += 8) {
+        float o8[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o8[e] = O[c + e] * inv;
+        dst[c >> 3] = pack8(o8);
+      }
+    }
+  }
+  tmem_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tmem_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(kPfTmemCols));
+  }
+}
+
 // ------------------------------------------------------------------ host helpers
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -1381,7 +1684,7 @@ extern "C" int b2_append_rope(const uint16_t *qkv, int64_t row_stride, const uin
   }
   AppendArgs a{qkv, row_stride, gamma_q, gamma_k, eps, rope_cos, rope_sin, rope_rows, past_lens,
                block_tables, max_blocks_per_seq > 0 ? max_blocks_per_seq : 1, k_pool, v_pool,
-               num_blocks, q_out, mode, dev_err};
+               num_blocks, q_out, mode, dev_err, 1, nullptr};
   append_rope_kernel<<<batch, 256, 0, static_cast<cudaStream_t>(stream)>>>(a);
   return launch_status("append_rope_kernel");
 }
@@ -1540,6 +1843,78 @@ extern "C" int b2_merge_states(const float *states, int32_t num_parts, int32_t b
                 state_o, 0, 0, 0, kHq * 2, part, kHq * kDim, part, combine_groups(num_parts)};
   combine_kernel<<<dim3(batch, kHq), a.groups * kDim, 0, static_cast<cudaStream_t>(stream)>>>(a);
   return launch_status("combine_kernel (merge states)");
+}
+
+bool prefill_smem_ready() {
+  static bool done[128] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return false;
+  if (!done[dev]) {
+    if (cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmem) !=
+        cudaSuccess)
+      return false;
+    done[dev] = true;
+  }
+  return true;
+}
+
+extern "C" int b2_prefill_append(const uint16_t *qkv, int64_t row_stride, const uint16_t *gamma_q,
+                                 const uint16_t *gamma_k, float eps, const uint16_t *rope_cos,
+                                 const uint16_t *rope_sin, int32_t rope_rows, const int32_t *past_lens,
+                                 const int32_t *chunk_lens, int32_t tokens, const int32_t *block_tables,
+                                 int32_t max_blocks_per_seq, uint16_t *k_pool, uint16_t *v_pool, int32_t num_blocks,
+                                 uint16_t *q_out, int32_t batch, int32_t mode, int32_t *dev_err, void *stream) {
+  if (batch < 0 || tokens < 0) return fail(B2_ERR_ARG, "batch and tokens must be >= 0");
+  if (batch == 0 || tokens == 0) return ok();
+  if (tokens > 65535) return fail(B2_ERR_ARG, "tokens must be <= 65535");
+  if (!qkv || !past_lens || !dev_err) return fail(B2_ERR_ARG, "qkv, past_lens and dev_err are required");
+  if (mode & ~(B2_NORM_QK | B2_ROPE_QK | B2_STORE_KV)) return fail(B2_ERR_ARG, "unknown mode bits 0x%x", mode);
+  if (row_stride < kQkvWidth || row_stride % 8 != 0)
+    return fail(B2_ERR_ARG, "row_stride must be >= %d and a multiple of 8", kQkvWidth);
+  if (!aligned16(qkv) || (q_out && !aligned16(q_out))) return fail(B2_ERR_ARG, "qkv and q_out must be 16-byte aligned");
+  if ((mode & B2_NORM_QK) && (!gamma_q || !gamma_k || !aligned16(gamma_q) || !aligned16(gamma_k)))
+    return fail(B2_ERR_ARG, "B2_NORM_QK needs 16-byte aligned gamma_q and gamma_k");
+  if ((mode & B2_ROPE_QK) &&
+      (!rope_cos || !rope_sin || rope_rows <= 0 || !aligned16(rope_cos) || !aligned16(rope_sin)))
+    return fail(B2_ERR_ARG, "B2_ROPE_QK needs 16-byte aligned cos/sin tables with rope_rows > 0");
+  if (mode & B2_STORE_KV) {
+    if (!block_tables || !k_pool || !v_pool || max_blocks_per_seq <= 0 || num_blocks <= 0)
+      return fail(B2_ERR_ARG, "B2_STORE_KV needs block_tables, k_pool, v_pool and positive sizes");
+    if (!aligned16(k_pool) || !aligned16(v_pool)) return fail(B2_ERR_ARG, "pools must be 16-byte aligned");
+  }
+  AppendArgs a{qkv, row_stride, gamma_q, gamma_k, eps, rope_cos, rope_sin, rope_rows, past_lens,
+               block_tables, max_blocks_per_seq > 0 ? max_blocks_per_seq : 1, k_pool, v_pool,
+               num_blocks, q_out, mode, dev_err, tokens, chunk_lens};
+  append_rope_kernel<<<dim3(batch, tokens), 256, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  return launch_status("append_rope_kernel (chunk)");
+}
+
+extern "C" int b2_prefill_attn(const uint16_t *q, const uint16_t *k_pool, const uint16_t *v_pool, int32_t num_blocks,
+                               const int32_t *block_tables, int32_t max_blocks_per_seq, const int32_t *past_lens,
+                               const int32_t *chunk_lens, int32_t tokens, int32_t batch, float scale, uint16_t *out,
+                               int32_t *dev_err, void *stream) {
+  if (batch < 0 || tokens < 0) return fail(B2_ERR_ARG, "batch and tokens must be >= 0");
+  if (batch == 0 || tokens == 0) return ok();
+  if (!q || !k_pool || !v_pool || !block_tables || !past_lens || !out || !dev_err)
+    return fail(B2_ERR_ARG, "null pointer argument");
+  if (num_blocks <= 0 || static_cast<int64_t>(num_blocks) * kHkv * kBlock >= (int64_t(1) << 31))
+    return fail(B2_ERR_ARG, "num_blocks must be in [1, 2^22) (got %d)", num_blocks);
+  if (max_blocks_per_seq <= 0) return fail(B2_ERR_ARG, "max_blocks_per_seq must be positive");
+  if (batch > 65535) return fail(B2_ERR_ARG, "batch must be <= 65535");
+  if (!aligned16(q) || !aligned16(out) || !aligned16(k_pool) || !aligned16(v_pool))
+    return fail(B2_ERR_ARG, "q, out and the pools must be 16-byte aligned");
+  if (!(scale > 0.f)) return fail(B2_ERR_ARG, "scale must be positive");
+  CUtensorMap mk, mv;
+  int rc = make_pool_map(&mk, k_pool, num_blocks);
+  if (rc) return rc;
+  rc = make_pool_map(&mv, v_pool, num_blocks);
+  if (rc) return rc;
+  if (!prefill_smem_ready()) return fail(B2_ERR_CUDA, "cannot set the prefill kernel's shared memory size");
+  PrefillArgs a{q, block_tables, max_blocks_per_seq, past_lens, chunk_lens, tokens, num_blocks,
+                scale * 1.4426950408889634f, out, dev_err};
+  const dim3 grid((tokens + 63) / 64, kHkv, batch);
+  prefill_attn_kernel<<<grid, kPfThreads, kPfSmem, static_cast<cudaStream_t>(stream)>>>(mk, mv, a);
+  return launch_status("prefill_attn_kernel");
 }
 
 // ------------------------------------------------------------------ allocation-free decode

@@ -116,6 +116,43 @@ def run_case(length: int, impl: str, weights: dict) -> dict:
     }
 
 
+PREFILL_CASES = [(21, 5), (0, 70), (100, 64)]   # (cached tokens, chunk tokens)
+
+
+def prefill_case(past: int, t: int, weights: dict) -> dict:
+    """Lfm2Attention.forward on a chunk of t tokens after `past` cached ones,
+    with the causal mask of a cached prefix (query i sees keys 0..past+i, the
+    mask transformers' create_causal_mask builds); sdpa."""
+    cfg = config("sdpa")
+    attn = hf.Lfm2Attention(cfg, layer_idx=2).to(BF16).eval()
+    with torch.no_grad():
+        for name in ("q_proj", "k_proj", "v_proj", "out_proj"):
+            getattr(attn, name).weight.copy_(weights[name])
+        attn.q_layernorm.weight.copy_(weights["q_gamma"])
+        attn.k_layernorm.weight.copy_(weights["k_gamma"])
+    rotary = hf.Lfm2RotaryEmbedding(cfg)
+    k_past, v_past = orc.past_cache(3000 + past, past)
+    g = torch.Generator().manual_seed(4000 + t)
+    x = torch.randn(1, t, 1024, generator=g).to(BF16)
+    cache = DynamicCache()
+    cache.update(k_past, v_past, 2)
+    seen = {}
+    hooks = [attn.out_proj.register_forward_hook(lambda m, i, o: seen.__setitem__("context", i[0])),
+             attn.q_proj.register_forward_hook(lambda m, i, o: seen.__setitem__("q_raw", o)),
+             attn.k_proj.register_forward_hook(lambda m, i, o: seen.__setitem__("k_raw", o)),
+             attn.v_proj.register_forward_hook(lambda m, i, o: seen.__setitem__("v_raw", o))]
+    keys = torch.arange(past + t)
+    mask = (keys[None, :] <= (past + torch.arange(t))[:, None])[None, None]
+    with torch.no_grad():
+        cos, sin = rotary(x, torch.arange(past, past + t)[None])
+        attn(x, (cos, sin), mask, past_key_values=cache)
+    for h in hooks:
+        h.remove()
+    qkv = torch.cat([seen["q_raw"], seen["k_raw"], seen["v_raw"]], dim=-1)[0]
+    return {"qkv": orc.bits(qkv), "context": orc.bits(seen["context"].reshape(t, 16, 64)),
+            "past": np.int64(past), "tokens": np.int64(t), "past_sha256": sha(k_past, v_past)}
+
+
 GREEDY_SEED = 5
 GREEDY_BATCH, GREEDY_PROMPT, GREEDY_NEW, GREEDY_TOPK = 2, 8, 16, 8
 
@@ -173,6 +210,9 @@ def main() -> None:
         cos, sin = rotary(torch.zeros(1, dtype=BF16), pos)
     np.savez_compressed(OUT / "lfm2_rope.npz", positions=np.array(ROPE_POSITIONS, dtype=np.int64),
                         cos=orc.bits(cos[0]), sin=orc.bits(sin[0]), **meta)
+    for past, t in PREFILL_CASES:
+        np.savez_compressed(OUT / f"lfm2_prefill_P{past}_T{t}.npz", **prefill_case(past, t, weights), **meta,
+                            weight_seed=np.int64(WEIGHT_SEED))
     np.savez_compressed(OUT / "lfm2_greedy.npz", **greedy_case(), **meta)
     print("wrote", sorted(p.name for p in OUT.glob("*.npz")))
 

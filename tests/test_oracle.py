@@ -111,3 +111,19 @@ def test_ref_layouts():
     assert np.array_equal(nxt[3, 0, 21], qkv[1024 + 192:1024 + 256])
     assert np.array_equal(nxt[3, 1, 21], qkv[1536 + 192:1536 + 256])
     assert orc.float_to_bf16_bits(np.float32(22.0)) == 0x41B0
+
+
+PREFILL = sorted(GOLDEN.glob("lfm2_prefill_*.npz"))
+
+
+@pytest.mark.parametrize("path", PREFILL, ids=lambda p: p.stem)
+def test_prefill_oracle_matches_hf(path):
+    f = _load(path)
+    past, t = int(f["past"]), int(f["tokens"])
+    w = orc.attention_weights(int(f["weight_seed"]))
+    k, v = orc.past_cache(3000 + past, past)
+    assert _sha(k, v) == str(f["past_sha256"])
+    ctx, k_all, v_all = orc.prefill_step(orc.from_bits(f["qkv"]).reshape(t, -1), k[0], v[0], past,
+                                         w["q_gamma"], w["k_gamma"])
+    assert np.array_equal(orc.bits(ctx), f["context"])
+    assert k_all.shape == (8, past + t, 64)
