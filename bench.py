@@ -15,8 +15,10 @@ so no L2 flush is needed between steps.
 
 The timed region replays a CUDA graph of exactly K steps with inputs already
 in HBM; `e2e` times the same steps through the public API
-(PagedDecodeAttention.step) with the per-step inputs copied from pinned host
-memory and the context copied back inside the timed region.
+(PagedDecodeAttention.step_host, one b2_decode_step_host2 call per step) with
+the per-step inputs copied from pinned host memory and the context copied
+back inside the timed region (uploads and downloads overlap the neighbouring
+steps' kernels).
 
 `--impl reference` times the reference's CPU path (the oracle's restatement
 of transformers' Lfm2Attention + DynamicCache in BF16) on this host's cores,
@@ -63,10 +65,12 @@ def parse():
     p.add_argument("--three-kernels", action="store_true",
                    help="run append, decode and combine as three launches instead of the fused kernel")
     p.add_argument("--max-ctas", type=int, default=0, help="cap on the fused kernel's persistent grid")
-    p.add_argument("--config", choices=["c3", "c4", "c2", "c5"], default="c3",
+    p.add_argument("--chunk", type=int, default=64, help="prefill: new tokens per sequence")
+    p.add_argument("--config", choices=["c3", "c4", "c2", "c5", "prefill"], default="c3",
                    help="c3: batched paged decode (default); c4: one long sequence split over the GPUs; "
                         "c2: 6 attention layers x 64 consecutive decode steps of one sequence; "
-                        "c5: end-to-end greedy decode of the whole random-init model")
+                        "c5: end-to-end greedy decode of the whole random-init model; "
+                        "prefill: a chunk of --chunk new tokens per C3 sequence on the tcgen05 kernel")
     p.add_argument("--context", type=int, default=131072, help="c4: cached tokens of the sequence")
     return p.parse_args()
 
@@ -305,9 +309,9 @@ def run_b200(args):
     stream.synchronize()
     runner.check()
 
-    # CUDA graph of exactly K steps; external events bracket the dominant
-    # kernel of every step (the fused kernel is the whole step; with three
-    # kernels, the decode launch)
+    # CUDA graph of exactly K steps.  The fused kernel is the whole step, so
+    # its launch time is the timed region / K (no event nodes between the
+    # launches); with three kernels, external events bracket the decode launch.
     attn = importlib.import_module(PKG + ".attention")
     ev0 = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(K)]
     ev1 = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(K)]
@@ -317,9 +321,7 @@ def run_b200(args):
     with torch.cuda.graph(graph, stream=stream):
         for j in range(K):
             if runner.fused:
-                ev0[j].record()
                 runner.step(0, wl["qkv"][j % ring], wl["past"], wl["seq"], wl["tables"])
-                ev1[j].record()
                 continue
             q = runner.q[:b]
             attn.append_rope(wl["qkv"][j % ring], wl["past"], q_out=q, dev_err=runner.dev_err,
@@ -350,34 +352,52 @@ def run_b200(args):
     if pg is not None:
         torch.distributed.barrier()
     ms = t_start.elapsed_time(t_end)
-    decode_ms = sum(a.elapsed_time(b) for a, b in zip(ev0, ev1)) / K
+    decode_ms = ms / K if runner.fused else sum(a.elapsed_time(b) for a, b in zip(ev0, ev1)) / K
     runner.check()
 
     # end-to-end through the public API: pinned host inputs in, context out, per step
     e2e_steps = min(args.e2e_steps, K)
     qkv_host = wl["qkv"].cpu().pin_memory()
-    lens_host = torch.stack([wl["past"].cpu(), wl["seq"].cpu()]).pin_memory()
+    past_host = wl["past"].cpu().pin_memory()
     nb = len(wl["lengths"])
     out_host = torch.empty(e2e_steps, nb, HQ, D, dtype=torch.bfloat16).pin_memory()
-    qkv_dev = torch.empty_like(wl["qkv"][0])
-    lens_dev = torch.empty(2, nb, dtype=torch.int32, device=dev)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        for j in range(3):
-            qkv_dev.copy_(qkv_host[j % ring], non_blocking=True)
-            runner.step(0, qkv_dev, wl["past"], wl["seq"], wl["tables"])
-    torch.cuda.synchronize()
-    if pg is not None:
-        torch.distributed.barrier()
-    with torch.cuda.stream(stream):
-        e0.record()
-        for j in range(e2e_steps):
-            qkv_dev.copy_(qkv_host[j % ring], non_blocking=True)
-            lens_dev.copy_(lens_host, non_blocking=True)
-            o = runner.step(0, qkv_dev, lens_dev[0], lens_dev[1], wl["tables"])
-            out_host[j].copy_(o, non_blocking=True)
-        e1.record()
+    if runner.fused:
+        # host-fed pipeline: per step H2D (copy stream), fused kernel, D2H
+        with torch.cuda.stream(stream):
+            runner.open_host_pipeline(0, wl["tables"])
+            for j in range(3):
+                runner.step_host(qkv_host[j % ring], past_host, out_host[j % e2e_steps])
+            runner.join_host()
+        torch.cuda.synchronize()
+        if pg is not None:
+            torch.distributed.barrier()
+        with torch.cuda.stream(stream):
+            e0.record()
+            for j in range(e2e_steps):
+                runner.step_host(qkv_host[j % ring], past_host, out_host[j])
+            runner.join_host()
+            e1.record()
+    else:
+        qkv_dev = torch.empty_like(wl["qkv"][0])
+        lens_dev = torch.empty(2, nb, dtype=torch.int32, device=dev)
+        lens_host = torch.stack([wl["past"].cpu(), wl["seq"].cpu()]).pin_memory()
+        with torch.cuda.stream(stream):
+            for j in range(3):
+                qkv_dev.copy_(qkv_host[j % ring], non_blocking=True)
+                runner.step(0, qkv_dev, wl["past"], wl["seq"], wl["tables"])
+        torch.cuda.synchronize()
+        if pg is not None:
+            torch.distributed.barrier()
+        with torch.cuda.stream(stream):
+            e0.record()
+            for j in range(e2e_steps):
+                qkv_dev.copy_(qkv_host[j % ring], non_blocking=True)
+                lens_dev.copy_(lens_host, non_blocking=True)
+                o = runner.step(0, qkv_dev, lens_dev[0], lens_dev[1], wl["tables"])
+                out_host[j].copy_(o, non_blocking=True)
+            e1.record()
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)
     runner.check()
@@ -412,7 +432,7 @@ def run_b200(args):
                      "algorithmic_bytes": dbytes, "avg_launch_ms": decode_ms},
         "clocks": clocks.summary(),
         "e2e": {"value": tokens * e2e_steps / (e2e_ms / 1e3), "unit": "tokens/s",
-                "h2d_bytes_per_step": nb * (2048 * 2 + 2 * 4),
+                "h2d_bytes_per_step": nb * (2048 * 2 + (4 if runner.fused else 8)),
                 "d2h_bytes_per_step": nb * HQ * D * 2, "steps": e2e_steps},
         "gpu_launches": (1 if runner.fused else 3) * K,
     }
@@ -642,6 +662,90 @@ def run_c5(args):
         print(json.dumps(line), flush=True)
 
 
+def run_prefill(args):
+    """Batched-prompt attention (the x8p engine's batched prompt tile, grown to
+    64-token chunks): the C3 batch of 64 sequences with cached prefixes
+    L ~ U[128, 8192], each receiving --chunk new tokens through one attention
+    layer (append of the chunk + tcgen05 attention).  tokens/s counts chunk
+    tokens.  Replicas across GPUs."""
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    attn = importlib.import_module(PKG + ".attention")
+    pc = importlib.import_module(PKG + ".paged_cache")
+    rope = importlib.import_module(PKG + ".rope")
+    lengths = seq_lengths(args, 0)
+    T = args.chunk
+    caps = [n + T for n in lengths]
+    cache = pc.PagedKVCache(sum(pc.blocks_for(c) for c in caps), max(caps), device=dev,
+                            shuffle_seed=args.seed * 1000 + 17)
+    for n, c in zip(lengths, caps):
+        cache.add_sequence(n, capacity=c)
+    gen = torch.Generator(device=dev).manual_seed(args.seed * 1000 + rank + 29)
+    cache.k.normal_(generator=gen)
+    cache.v.normal_(generator=gen)
+    gg = torch.Generator().manual_seed(args.seed + 31)
+    gq = (1.0 + 0.1 * torch.randn(D, generator=gg)).to(torch.bfloat16).to(dev)
+    gk = (1.0 + 0.1 * torch.randn(D, generator=gg)).to(torch.bfloat16).to(dev)
+    cos, sin = rope.rope_table(max(caps) + 1, device=dev)
+    b = len(lengths)
+    qkv = (torch.randn(b, T, 2048, generator=gen, device=dev) * 0.6).to(torch.bfloat16)
+    past = torch.tensor(lengths, dtype=torch.int32, device=dev)
+    tables = cache.block_tables()
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    q_out = torch.empty(b, T, HQ, D, dtype=torch.bfloat16, device=dev)
+    out = torch.empty(b, T, HQ, D, dtype=torch.bfloat16, device=dev)
+    kp, vp = cache.pool(0)
+    stream = torch.cuda.Stream(dev)
+
+    def step():
+        attn.prefill(qkv, past, k_pool=kp, v_pool=vp, block_tables=tables, gamma_q=gq, gamma_k=gk, cos=cos,
+                     sin=sin, dev_err=err, out=out, q_out=q_out)
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 1)):
+            step()
+    torch.cuda.synchronize()
+    assert err.item() == 0, "device error in prefill"
+    K = args.steps
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for _ in range(K):
+            step()
+    graph.replay()
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        with torch.cuda.stream(stream):
+            t0.record()
+            graph.replay()
+            t1.record()
+        torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / K
+    assert err.item() == 0, "device error in prefill"
+    nbytes = sum(KV_BYTES_PER_TOKEN * (n + T) + T * (2048 * 2 + HQ * D * 2 * 2) for n in lengths)
+    # useful flops: each chunk token's 16 heads over the keys it sees (causal)
+    flops = sum(4 * HQ * D * sum(n + t + 1 for t in range(T)) for n in lengths)
+    peak, peak_kind = measured_hbm_peak()
+    gbs = nbytes / (ms / 1e3) / 1e9
+    line = {
+        "metric": METRIC, "value": b * T / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": K,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "replicas",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"batched prompt: 64 sequences with cached L ~ U[128, 8192] each receiving "
+                               f"{T} new tokens through one attention layer (chunk append + tcgen05 "
+                               f"attention, causal within the chunk)", "chunk": T,
+                   "global_batch": b, "parallelism": "replicas"},
+        "hbm_gbs_per_gpu": gbs, "tflops": flops / (ms / 1e3) / 1e12,
+        "roofline": {"bound": "hbm", "kernel": "append_rope_kernel + prefill_attn_kernel", "achieved": gbs,
+                     "peak": peak, "peak_source": peak_kind, "unit": "GB/s", "frac": gbs / peak,
+                     "traffic": None, "algorithmic_bytes": nbytes},
+        "clocks": clocks.summary(), "gpu_launches": 2 * K,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     world, _, _ = dist_env()
@@ -656,6 +760,8 @@ def main():
         run_c2(args)
     elif args.config == "c5":
         run_c5(args)
+    elif args.config == "prefill":
+        run_prefill(args)
     else:
         run_b200(args)
 

@@ -204,6 +204,52 @@ int b2_decode_step(const uint16_t *qkv, int64_t row_stride,
                    int32_t max_ctas, int32_t *dev_err, void *stream);
 
 /*
+ * One decode step fed from host memory, in one call and stream order: copy
+ * the qkv rows (batch x 2048 bf16, packed) and past lengths from pinned host
+ * memory into the caller's device staging buffers, run b2_decode_step
+ * (norm + RoPE + append + attention, B2_NORM_QK | B2_ROPE_QK | B2_STORE_KV),
+ * copy the context (batch x 16 x 64 bf16) back into out_host.  For hosts that
+ * drive the decode loop from the CPU (the reference's X8Model.step submits one
+ * program per token, experiments/lfm25_x8_model.py:133-148).  Asynchronous:
+ * out_host is valid after the stream is synchronised.
+ */
+int b2_decode_step_host(const uint16_t *qkv_host, const int32_t *past_host,
+                        uint16_t *out_host, uint16_t *qkv_dev, int32_t *past_dev,
+                        uint16_t *out_dev, const uint16_t *gamma_q,
+                        const uint16_t *gamma_k, float eps,
+                        const uint16_t *rope_cos, const uint16_t *rope_sin,
+                        int32_t rope_rows, const int32_t *block_tables,
+                        int32_t max_blocks_per_seq, uint16_t *k_pool,
+                        uint16_t *v_pool, int32_t num_blocks, int32_t batch,
+                        int32_t blocks_per_split, float scale, float *part_ml,
+                        float *part_o, int32_t *counters, int32_t *dev_err,
+                        void *stream);
+
+/*
+ * Double-buffered form of b2_decode_step_host for a host loop that keeps the
+ * GPU busy: the caller alternates slot 0 and 1 and provides two staging slots
+ * (qkv_dev2 [2][batch][2048], past_dev2 [2][batch], out_dev2 [2][batch][16][64]).
+ * Uploads run on a library-owned stream, ahead of the kernel of the previous
+ * step; the kernel runs on `stream`; downloads on a second library-owned
+ * stream, overlapping the next kernel.  The streams and events are created on
+ * the first call on a device (no device memory is allocated).
+ * b2_decode_step_host_join(stream) makes `stream` wait for every download
+ * issued so far (then synchronising `stream` makes all out_host valid).
+ */
+int b2_decode_step_host2(const uint16_t *qkv_host, const int32_t *past_host,
+                         uint16_t *out_host, uint16_t *qkv_dev2, int32_t *past_dev2,
+                         uint16_t *out_dev2, int32_t slot,
+                         const uint16_t *gamma_q, const uint16_t *gamma_k, float eps,
+                         const uint16_t *rope_cos, const uint16_t *rope_sin,
+                         int32_t rope_rows, const int32_t *block_tables,
+                         int32_t max_blocks_per_seq, uint16_t *k_pool,
+                         uint16_t *v_pool, int32_t num_blocks, int32_t batch,
+                         int32_t blocks_per_split, float scale, float *part_ml,
+                         float *part_o, int32_t *counters, int32_t *dev_err,
+                         void *stream);
+int b2_decode_step_host_join(void *stream);
+
+/*
  * Merge states gathered from several GPUs (config C4: one sequence split
  * along the token axis).  `states` holds num_parts blocks of
  * batch * 16 * 66 fp32, each laid out [state_ml batch*16*2 | state_o

@@ -75,6 +75,29 @@ SIGNATURES = {
         _p, _p, _p,          # part_ml, part_o, counters
         _i32, _p, _p,        # max_ctas, dev_err, stream
     ]),
+    "b2_decode_step_host": (ctypes.c_int, [
+        _p, _p, _p,          # qkv_host, past_host, out_host
+        _p, _p, _p,          # qkv_dev, past_dev, out_dev
+        _p, _p, _f32,        # gamma_q, gamma_k, eps
+        _p, _p, _i32,        # rope_cos, rope_sin, rope_rows
+        _p, _i32,            # block_tables, max_blocks_per_seq
+        _p, _p, _i32,        # k_pool, v_pool, num_blocks
+        _i32, _i32, _f32,    # batch, blocks_per_split, scale
+        _p, _p, _p, _p,      # part_ml, part_o, counters, dev_err
+        _p,                  # stream
+    ]),
+    "b2_decode_step_host2": (ctypes.c_int, [
+        _p, _p, _p,          # qkv_host, past_host, out_host
+        _p, _p, _p, _i32,    # qkv_dev2, past_dev2, out_dev2, slot
+        _p, _p, _f32,        # gamma_q, gamma_k, eps
+        _p, _p, _i32,        # rope_cos, rope_sin, rope_rows
+        _p, _i32,            # block_tables, max_blocks_per_seq
+        _p, _p, _i32,        # k_pool, v_pool, num_blocks
+        _i32, _i32, _f32,    # batch, blocks_per_split, scale
+        _p, _p, _p, _p,      # part_ml, part_o, counters, dev_err
+        _p,                  # stream
+    ]),
+    "b2_decode_step_host_join": (ctypes.c_int, [_p]),
     "b2_merge_states": (ctypes.c_int, [
         _p, _i32, _i32,      # states, num_parts, batch
         _p, _p, _p, _p,      # out, state_ml, state_o, stream

@@ -373,6 +373,60 @@ class PagedDecodeAttention:
                 blocks_per_split=self.blocks_per_split, out=o, stream=stream)
         return o
 
+    # ---------------------------------------------------------------- host-fed steps
+
+    def open_host_pipeline(self, layer: int, block_tables: torch.Tensor, batch: int | None = None) -> None:
+        """Prepare step_host(): device staging buffers and the C-ABI arguments
+        of b2_decode_step_host, validated once here, not per step."""
+        if not self.fused:
+            raise ValueError("the host-fed step runs the fused kernel")
+        b = self.max_batch if batch is None else batch
+        dev = self.device
+        _need(block_tables, "block_tables", torch.int32, dev)
+        if block_tables.dim() != 2 or block_tables.shape[0] != b:
+            raise ValueError("block_tables must be [batch, max_blocks_per_seq]")
+        splits = num_splits_for(block_tables.shape[1], self.blocks_per_split)
+        if self.part_ml.numel() < b * splits * HQ * 2:
+            raise ValueError("partial-state buffers too small")
+        kp, vp = self.cache.pool(layer)
+        hp = {"b": b, "tables": block_tables, "slot": 0,
+              "qkv": torch.empty(2, b, QKV_WIDTH, dtype=torch.bfloat16, device=dev),
+              "past": torch.empty(2, b, dtype=torch.int32, device=dev),
+              "out": torch.empty(2, b, HQ, D, dtype=torch.bfloat16, device=dev)}
+        lib = _lib.load()
+        hp["call"] = lib.b2_decode_step_host2
+        hp["join"] = lib.b2_decode_step_host_join
+        hp["bufs"] = (_ptr(hp["qkv"]), _ptr(hp["past"]), _ptr(hp["out"]))
+        hp["args"] = (_ptr(self.gamma_q), _ptr(self.gamma_k),
+                      ctypes.c_float(self.eps), _ptr(self.cos), _ptr(self.sin), self.cos.shape[0],
+                      _ptr(block_tables), block_tables.shape[1], _ptr(kp), _ptr(vp), kp.shape[0], b,
+                      self.blocks_per_split, ctypes.c_float(SCALE), _ptr(self.part_ml), _ptr(self.part_o),
+                      _ptr(self.counters), _ptr(self.dev_err))
+        self._hp = hp
+
+    def step_host(self, qkv_host: torch.Tensor, past_host: torch.Tensor, out_host: torch.Tensor,
+                  stream: torch.cuda.Stream | None = None) -> None:
+        """One decode step fed from pinned host memory (b2_decode_step_host2, one
+        call): H2D of the qkv rows [B, 2048] and past lengths [B], the fused
+        kernel on the current stream, D2H of the context into out_host
+        [B, 16, 64].  Consecutive calls alternate two device slots, so uploads
+        and downloads overlap the neighbouring steps' kernels.  Asynchronous:
+        call join_host() and synchronise the stream before reading out_host."""
+        hp = self._hp
+        for t, n, dt in ((qkv_host, hp["b"] * QKV_WIDTH, torch.bfloat16), (past_host, hp["b"], torch.int32),
+                         (out_host, hp["b"] * HQ * D, torch.bfloat16)):
+            if t.dtype != dt or t.numel() != n or not t.is_contiguous() or not t.is_pinned():
+                raise ValueError("host buffers must be pinned, contiguous and of the pipeline's shape")
+        rc = hp["call"](ctypes.c_void_p(qkv_host.data_ptr()), ctypes.c_void_p(past_host.data_ptr()),
+                        ctypes.c_void_p(out_host.data_ptr()), *hp["bufs"], hp["slot"], *hp["args"],
+                        _stream(self.device, stream))
+        _lib.check(rc, "b2_decode_step_host2")
+        hp["slot"] ^= 1
+
+    def join_host(self, stream: torch.cuda.Stream | None = None) -> None:
+        """Make the stream wait for every context download issued by step_host."""
+        _lib.check(self._hp["join"](_stream(self.device, stream)), "b2_decode_step_host_join")
+
     def check(self) -> None:
         """Synchronise on the device error word; raise if any kernel flagged one."""
         word = int(self.dev_err.item())

@@ -1284,14 +1284,14 @@ __global__ void __launch_bounds__(kStepThreads, 3)
 
 constexpr int kPfStages = 3;
 constexpr int kPfThreads = 5 * 32;  // 4 softmax warps (one query row per thread) + 1 TMA warp
-constexpr int kPfTmemCols = 128;    // S at column 0, PV at column 64
+constexpr int kPfTmemCols = 256;    // S double buffer at columns 0 and 64, PV at column 128
 constexpr uint32_t kPfIdescS = (1u << 4) | (1u << 7) | (1u << 10) | (8u << 17) | (8u << 24);  // f32 <- bf16, M128 N64, K-major
 constexpr uint32_t kPfIdescPV = kPfIdescS | (1u << 16);  // B (V) MN-major
 
 struct __align__(8) PrefillTail {
   uint64_t full[kPfStages];
   uint64_t empty[kPfStages];
-  uint64_t sbar, pvbar;
+  uint64_t sbar[2], pvbar;
   uint32_t tmem_base;
   int abort;
 };
@@ -1331,6 +1331,28 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
 
 __device__ __forceinline__ void tmem_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tmem_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 16 consecutive fp32 columns of this thread's TMEM lane, without waiting
+// (several loads in flight; tmem_wait_ld() before using any of them).
+__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t r[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// 64 consecutive fp32 columns of this thread's TMEM lane (4 loads, one wait).
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float v[64]) {
+  uint32_t r[64];
+#pragma unroll
+  for (int c = 0; c < 64; c += 16) tmem_ld16_nowait(taddr + c, r + c);
+  tmem_wait_ld();
+#pragma unroll
+  for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+}
 
 // 16 consecutive fp32 columns of this thread's TMEM lane.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float v[16]) {
@@ -1391,7 +1413,8 @@ __global__ void __launch_bounds__(kPfThreads, 2)
       mbar_init(smem_u32(&tail->full[s]), 1);
       mbar_init(smem_u32(&tail->empty[s]), 1);
     }
-    mbar_init(smem_u32(&tail->sbar), 1);
+    mbar_init(smem_u32(&tail->sbar[0]), 1);
+    mbar_init(smem_u32(&tail->sbar[1]), 1);
     mbar_init(smem_u32(&tail->pvbar), 1);
     tail->abort = 0;
     mbar_fence_init();
@@ -1453,6 +1476,11 @@ __global__ void __launch_bounds__(kPfThreads, 2)
     }
   } else {
     // ---------------- softmax / epilogue warps: thread = query row
+    // Software-pipelined over the K/V blocks: S_{j+1} = Q.K_{j+1}^T runs on
+    // the tensor cores (second S buffer) while the softmax of block j runs,
+    // and P_j.V_j runs while the next iteration loads S_{j+1}; the output
+    // O = sum_j alpha-rescaled P_j.V_j is accumulated in registers one
+    // iteration behind.
     const int hl = tid >> 6, t = tid & 63;
     const bool row_ok = t < rows_t;
     const int qpos = past + t0 + t;
@@ -1460,58 +1488,78 @@ __global__ void __launch_bounds__(kPfThreads, 2)
     float O[64];
 #pragma unroll
     for (int i = 0; i < 64; ++i) O[i] = 0.f;
-    float m = -1.0e30f, l = 0.f;
+    float m = -1.0e30f, l = 0.f, alpha_prev = 1.f;
+
+    auto issue_s = [&](int j) {  // thread 0 only: S_j into buffer j % 2
+      const int s = j % kPfStages;
+      if (!tail->abort && mbar_wait(smem_u32(&tail->full[s]), (j / kPfStages) & 1)) {
+        tmem_fence_after();
+        const uint32_t kt = smem_u32(ring + s * kStageBytes);
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          umma_f16(tmem + 64 * (j & 1), umma_desc(smem_u32(sQ) + 32 * ks, 16), umma_desc(kt + 32 * ks, 16),
+                   kPfIdescS, ks > 0);
+        umma_commit(smem_u32(&tail->sbar[j & 1]));
+      } else {
+        if (!tail->abort) atomicOr(a.err, B2_DEV_TIMEOUT);
+        tail->abort = 1;
+        mbar_arrive(smem_u32(&tail->sbar[j & 1]));  // let the other rows through
+      }
+    };
+    auto accumulate_pv = [&](int j) {  // all rows: O = O * alpha_prev + P_j.V_j
+      mbar_wait(smem_u32(&tail->pvbar), j & 1);
+      tmem_fence_after();
+      float pv[64];
+      tmem_ld64(trow + 128, pv);
+#pragma unroll
+      for (int e = 0; e < 64; ++e) O[e] = fmaf(O[e], alpha_prev, pv[e]);
+    };
+
+    if (tid == 0) issue_s(0);
     for (int j = 0; j < nblk; ++j) {
       const int s = j % kPfStages;
-      const uint32_t ph = (j / kPfStages) & 1;
-      const uint32_t kt = smem_u32(ring + s * kStageBytes);
-      const uint32_t vt = kt + kTileBytes;
-      if (tid == 0) {
-        if (mbar_wait(smem_u32(&tail->full[s]), ph)) {
-          tmem_fence_after();
-#pragma unroll
-          for (int ks = 0; ks < 4; ++ks)
-            umma_f16(tmem, umma_desc(smem_u32(sQ) + 32 * ks, 16), umma_desc(kt + 32 * ks, 16), kPfIdescS, ks > 0);
-          umma_commit(smem_u32(&tail->sbar));
-        } else {
-          atomicOr(a.err, B2_DEV_TIMEOUT);
-          tail->abort = 1;
-          mbar_arrive(smem_u32(&tail->sbar));  // let the other rows through
-        }
-      }
-      mbar_wait(smem_u32(&tail->sbar), j & 1);
+      mbar_wait(smem_u32(&tail->sbar[j & 1]), (j >> 1) & 1);
       tmem_fence_after();
-      // scores of this row, masked: causal within the chunk, nothing past the tile
       float sc[64];
-#pragma unroll
-      for (int c = 0; c < 64; c += 16) tmem_ld16(trow + c, sc + c);
+      tmem_ld64(trow + 64 * (j & 1), sc);
+      if (tid == 0 && j + 1 < nblk) issue_s(j + 1);
+      // scores of this row, masked: causal within the chunk, nothing past the
+      // tile; max and sum in 8 independent chains (shorter dependency chains)
       const int key0 = j * kBlock;
-      float bm = -INFINITY;
+      const int lim = row_ok ? qpos - key0 : -1;  // columns c <= lim are visible
+      float bm8[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) bm8[e] = -INFINITY;
 #pragma unroll
       for (int c = 0; c < 64; ++c) {
-        sc[c] = (row_ok && key0 + c <= qpos) ? sc[c] * a.scale_log2 : -INFINITY;
-        bm = fmaxf(bm, sc[c]);
+        sc[c] = c <= lim ? sc[c] * a.scale_log2 : -INFINITY;
+        bm8[c & 7] = fmaxf(bm8[c & 7], sc[c]);
       }
+      const float bm = fmaxf(fmaxf(fmaxf(bm8[0], bm8[1]), fmaxf(bm8[2], bm8[3])),
+                             fmaxf(fmaxf(bm8[4], bm8[5]), fmaxf(bm8[6], bm8[7])));
       const float mn = fmaxf(m, bm);
       const float alpha = ex2(m - mn);
       m = mn;
-      float ps = 0.f;
+      float ps8[8];
 #pragma unroll
-      for (int c = 0; c < 64; c += 8) {
-        float p8[8];
+      for (int e = 0; e < 8; ++e) ps8[e] = 0.f;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          p8[e] = ex2(sc[c + e] - mn);
-          ps += p8[e];
-        }
-        *reinterpret_cast<uint4 *>(sP + tid * 128 + (((c >> 3) ^ (tid & 7)) << 4)) = pack8(p8);
+      for (int c = 0; c < 64; ++c) {
+        sc[c] = ex2(sc[c] - mn);
+        ps8[c & 7] += sc[c];
       }
+      const float ps = ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
       l = fmaf(l, alpha, ps);
+      if (j > 0) accumulate_pv(j - 1);  // P_{j-1} is no longer needed after this
+      alpha_prev = alpha;
+#pragma unroll
+      for (int c = 0; c < 64; c += 8)
+        *reinterpret_cast<uint4 *>(sP + tid * 128 + (((c >> 3) ^ (tid & 7)) << 4)) = pack8(sc + c);
       if (key0 + kBlock - 1 > last_key) {
         // rows of the last block past every query of the tile may hold stale
         // (even NaN) data: zero them so that P = 0 cannot meet them in P.V
         // (after the stage's copy has landed, so the copy cannot overwrite)
-        mbar_wait(smem_u32(&tail->full[s]), ph);
+        mbar_wait(smem_u32(&tail->full[s]), (j / kPfStages) & 1);
         const int first_bad = last_key - key0 + 1;
         uint8_t *v_gen = ring + s * kStageBytes + kTileBytes;
         for (int i = tid; i < (kBlock - first_bad) * 8; i += 128)
@@ -1519,13 +1567,14 @@ __global__ void __launch_bounds__(kPfThreads, 2)
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       tmem_fence_before();
-      pf_bar();
+      const int stop = pf_bar_or(tail->abort);
       if (tid == 0) {
         tmem_fence_after();
-        if (!tail->abort) {
+        if (!stop) {
+          const uint32_t vt = smem_u32(ring + s * kStageBytes) + kTileBytes;
 #pragma unroll
           for (int ks = 0; ks < 4; ++ks)
-            umma_f16(tmem + 64, umma_desc(smem_u32(sP) + 32 * ks, 16), umma_desc(vt + 2048 * ks, 0), kPfIdescPV,
+            umma_f16(tmem + 128, umma_desc(smem_u32(sP) + 32 * ks, 16), umma_desc(vt + 2048 * ks, 0), kPfIdescPV,
                      ks > 0);
           umma_commit(smem_u32(&tail->pvbar));
           umma_commit(smem_u32(&tail->empty[s]));
@@ -1533,18 +1582,14 @@ __global__ void __launch_bounds__(kPfThreads, 2)
           mbar_arrive(smem_u32(&tail->pvbar));
         }
       }
-      mbar_wait(smem_u32(&tail->pvbar), j & 1);
-      tmem_fence_after();
-#pragma unroll
-      for (int c = 0; c < 64; c += 16) {
-        float pv[16];
-        tmem_ld16(trow + 64 + c, pv);
-#pragma unroll
-        for (int e = 0; e < 16; ++e) O[c + e] = fmaf(O[c + e], alpha, pv[e]);
+      if (stop) {
+        // an S MMA issued for block j + 1 must finish before the CTA leaves
+        if (j + 1 < nblk) mbar_wait(smem_u32(&tail->sbar[(j + 1) & 1]), ((j + 1) >> 1) & 1);
+        mbar_wait(smem_u32(&tail->pvbar), j & 1);
+        break;
       }
-      tmem_fence_before();
-      if (pf_bar_or(tail->abort)) break;
     }
+    if (!tail->abort) accumulate_pv(nblk - 1);
     if (row_ok && !tail->abort) {
       const float inv = 1.0f / l;
       uint4 *dst = reinterpret_cast<uint4 *>(a.out + (((int64_t)b * a.tokens + t0 + t) * kHq + 2 * kvh + hl) * kDim);
@@ -1915,6 +1960,126 @@ extern "C" int b2_prefill_attn(const uint16_t *q, const uint16_t *k_pool, const 
   const dim3 grid((tokens + 63) / 64, kHkv, batch);
   prefill_attn_kernel<<<grid, kPfThreads, kPfSmem, static_cast<cudaStream_t>(stream)>>>(mk, mv, a);
   return launch_status("prefill_attn_kernel");
+}
+
+extern "C" int b2_decode_step_host(const uint16_t *qkv_host, const int32_t *past_host, uint16_t *out_host,
+                                   uint16_t *qkv_dev, int32_t *past_dev, uint16_t *out_dev, const uint16_t *gamma_q,
+                                   const uint16_t *gamma_k, float eps, const uint16_t *rope_cos,
+                                   const uint16_t *rope_sin, int32_t rope_rows, const int32_t *block_tables,
+                                   int32_t max_blocks_per_seq, uint16_t *k_pool, uint16_t *v_pool, int32_t num_blocks,
+                                   int32_t batch, int32_t blocks_per_split, float scale, float *part_ml, float *part_o,
+                                   int32_t *counters, int32_t *dev_err, void *stream) {
+  if (batch <= 0) return batch == 0 ? ok() : fail(B2_ERR_ARG, "batch must be >= 0");
+  if (!qkv_host || !past_host || !out_host || !qkv_dev || !past_dev || !out_dev)
+    return fail(B2_ERR_ARG, "null host or staging pointer");
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t qkv_bytes = static_cast<size_t>(batch) * kQkvWidth * 2;
+  const size_t out_bytes = static_cast<size_t>(batch) * kHq * kDim * 2;
+  if (cudaMemcpyAsync(qkv_dev, qkv_host, qkv_bytes, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+      cudaMemcpyAsync(past_dev, past_host, static_cast<size_t>(batch) * 4, cudaMemcpyHostToDevice, st) != cudaSuccess)
+    return fail(B2_ERR_CUDA, "host-to-device copy failed: %s", cudaGetErrorString(cudaGetLastError()));
+  const int rc = b2_decode_step(qkv_dev, kQkvWidth, gamma_q, gamma_k, eps, rope_cos, rope_sin, rope_rows, past_dev,
+                                nullptr, block_tables, max_blocks_per_seq, k_pool, v_pool, num_blocks, batch,
+                                blocks_per_split, scale, B2_NORM_QK | B2_ROPE_QK | B2_STORE_KV, out_dev, nullptr,
+                                nullptr, nullptr, part_ml, part_o, counters, 0, dev_err, stream);
+  if (rc) return rc;
+  if (cudaMemcpyAsync(out_host, out_dev, out_bytes, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+    return fail(B2_ERR_CUDA, "device-to-host copy failed: %s", cudaGetErrorString(cudaGetLastError()));
+  return ok();
+}
+
+namespace {
+
+// Streams and events of the double-buffered host-fed step, one set per device
+// (created on first use; no device memory is allocated).
+struct HostPipe {
+  bool ready = false;
+  cudaStream_t h2d = nullptr, d2h = nullptr;
+  cudaEvent_t in_ready[2] = {}, out_ready[2] = {}, slot_free[2] = {}, d2h_done = nullptr;
+};
+std::mutex g_pipe_mu;
+HostPipe g_pipe[128];
+
+HostPipe *host_pipe(int *rc) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) {
+    *rc = fail(B2_ERR_CUDA, "no current CUDA device");
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_pipe_mu);
+  HostPipe &p = g_pipe[dev];
+  if (!p.ready) {
+    bool okk = cudaStreamCreateWithFlags(&p.h2d, cudaStreamNonBlocking) == cudaSuccess &&
+               cudaStreamCreateWithFlags(&p.d2h, cudaStreamNonBlocking) == cudaSuccess &&
+               cudaEventCreateWithFlags(&p.d2h_done, cudaEventDisableTiming) == cudaSuccess;
+    for (int i = 0; i < 2 && okk; ++i)
+      okk = cudaEventCreateWithFlags(&p.in_ready[i], cudaEventDisableTiming) == cudaSuccess &&
+            cudaEventCreateWithFlags(&p.out_ready[i], cudaEventDisableTiming) == cudaSuccess &&
+            cudaEventCreateWithFlags(&p.slot_free[i], cudaEventDisableTiming) == cudaSuccess &&
+            cudaEventRecord(p.slot_free[i], p.d2h) == cudaSuccess;
+    if (!okk) {
+      *rc = fail(B2_ERR_CUDA, "cannot create the host pipeline's streams/events: %s",
+                 cudaGetErrorString(cudaGetLastError()));
+      return nullptr;
+    }
+    p.ready = true;
+  }
+  *rc = B2_OK;
+  return &p;
+}
+
+}  // namespace
+
+extern "C" int b2_decode_step_host2(const uint16_t *qkv_host, const int32_t *past_host, uint16_t *out_host,
+                                    uint16_t *qkv_dev2, int32_t *past_dev2, uint16_t *out_dev2, int32_t slot,
+                                    const uint16_t *gamma_q, const uint16_t *gamma_k, float eps,
+                                    const uint16_t *rope_cos, const uint16_t *rope_sin, int32_t rope_rows,
+                                    const int32_t *block_tables, int32_t max_blocks_per_seq, uint16_t *k_pool,
+                                    uint16_t *v_pool, int32_t num_blocks, int32_t batch, int32_t blocks_per_split,
+                                    float scale, float *part_ml, float *part_o, int32_t *counters,
+                                    int32_t *dev_err, void *stream) {
+  if (batch <= 0) return batch == 0 ? ok() : fail(B2_ERR_ARG, "batch must be >= 0");
+  if (slot != 0 && slot != 1) return fail(B2_ERR_ARG, "slot must be 0 or 1");
+  if (!qkv_host || !past_host || !out_host || !qkv_dev2 || !past_dev2 || !out_dev2)
+    return fail(B2_ERR_ARG, "null host or staging pointer");
+  int rc = B2_OK;
+  HostPipe *p = host_pipe(&rc);
+  if (!p) return rc;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t qkv_n = static_cast<size_t>(batch) * kQkvWidth, out_n = static_cast<size_t>(batch) * kHq * kDim;
+  uint16_t *qkv_dev = qkv_dev2 + slot * qkv_n;
+  int32_t *past_dev = past_dev2 + slot * batch;
+  uint16_t *out_dev = out_dev2 + slot * out_n;
+  // inputs: H2D on the pipeline's upload stream once the slot's previous use has finished
+  if (cudaStreamWaitEvent(p->h2d, p->slot_free[slot], 0) != cudaSuccess ||
+      cudaMemcpyAsync(qkv_dev, qkv_host, qkv_n * 2, cudaMemcpyHostToDevice, p->h2d) != cudaSuccess ||
+      cudaMemcpyAsync(past_dev, past_host, static_cast<size_t>(batch) * 4, cudaMemcpyHostToDevice, p->h2d) !=
+          cudaSuccess ||
+      cudaEventRecord(p->in_ready[slot], p->h2d) != cudaSuccess || cudaStreamWaitEvent(st, p->in_ready[slot], 0) !=
+                                                                        cudaSuccess)
+    return fail(B2_ERR_CUDA, "host-to-device stage failed: %s", cudaGetErrorString(cudaGetLastError()));
+  rc = b2_decode_step(qkv_dev, kQkvWidth, gamma_q, gamma_k, eps, rope_cos, rope_sin, rope_rows, past_dev, nullptr,
+                      block_tables, max_blocks_per_seq, k_pool, v_pool, num_blocks, batch, blocks_per_split, scale,
+                      B2_NORM_QK | B2_ROPE_QK | B2_STORE_KV, out_dev, nullptr, nullptr, nullptr, part_ml, part_o,
+                      counters, 0, dev_err, stream);
+  if (rc) return rc;
+  // output: D2H on the download stream after the kernel; then the slot is free
+  if (cudaEventRecord(p->out_ready[slot], st) != cudaSuccess ||
+      cudaStreamWaitEvent(p->d2h, p->out_ready[slot], 0) != cudaSuccess ||
+      cudaMemcpyAsync(out_host, out_dev, out_n * 2, cudaMemcpyDeviceToHost, p->d2h) != cudaSuccess ||
+      cudaEventRecord(p->slot_free[slot], p->d2h) != cudaSuccess)
+    return fail(B2_ERR_CUDA, "device-to-host stage failed: %s", cudaGetErrorString(cudaGetLastError()));
+  return ok();
+}
+
+extern "C" int b2_decode_step_host_join(void *stream) {
+  int rc = B2_OK;
+  HostPipe *p = host_pipe(&rc);
+  if (!p) return rc;
+  if (cudaEventRecord(p->d2h_done, p->d2h) != cudaSuccess ||
+      cudaStreamWaitEvent(static_cast<cudaStream_t>(stream), p->d2h_done, 0) != cudaSuccess)
+    return fail(B2_ERR_CUDA, "cannot join the host pipeline: %s", cudaGetErrorString(cudaGetLastError()));
+  return ok();
 }
 
 // ------------------------------------------------------------------ allocation-free decode
