@@ -12,6 +12,8 @@ Modules:
   attention    torch-facing wrappers and the PagedDecodeAttention runner
   operators    drop-in shims with the reference's NPU operator signatures
   distributed  sequence sharding and long-context split-KV across GPUs
+  lfm2_runner  whole-token LFM2.5 decode runner (one CUDA graph per token)
+  hf_paged     transformers adapter: "b200_paged" attention + B200PagedCache
 """
 from . import _lib  # noqa: F401
 

@@ -256,14 +256,18 @@ def merge_states(states: torch.Tensor, num_parts: int, batch: int, *, out: torch
 
 
 def prefill(qkv: torch.Tensor, past_lens: torch.Tensor, *, k_pool: torch.Tensor, v_pool: torch.Tensor,
-            block_tables: torch.Tensor, gamma_q: torch.Tensor, gamma_k: torch.Tensor, cos: torch.Tensor,
-            sin: torch.Tensor, dev_err: torch.Tensor, chunk_lens: torch.Tensor | None = None,
-            out: torch.Tensor | None = None, q_out: torch.Tensor | None = None, eps: float = EPS,
-            scale: float = SCALE, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+            block_tables: torch.Tensor, gamma_q: torch.Tensor | None, gamma_k: torch.Tensor | None,
+            cos: torch.Tensor | None, sin: torch.Tensor | None, dev_err: torch.Tensor,
+            chunk_lens: torch.Tensor | None = None, out: torch.Tensor | None = None,
+            q_out: torch.Tensor | None = None, eps: float = EPS, scale: float = SCALE,
+            mode: int = _lib.B2_NORM_QK | _lib.B2_ROPE_QK | _lib.B2_STORE_KV,
+            stream: torch.cuda.Stream | None = None) -> torch.Tensor:
     """Batched-prompt attention (b2_prefill_append + b2_prefill_attn): qkv bf16
     [B, T, >= 2048] raw projections of T new tokens per sequence at positions
     past_lens[b] + t (chunk_lens[b] <= T valid).  Appends their k/v and returns
-    the context [B, T, 16, 64]."""
+    the context [B, T, 16, 64].  `mode` selects the q/k norm and RoPE steps
+    (B2_STORE_KV alone for projections that are already normalised and rotated;
+    gamma/cos/sin are then unused)."""
     dev = qkv.device
     if qkv.dim() != 3 or qkv.shape[2] < QKV_WIDTH:
         raise ValueError(f"qkv must be [batch, tokens, >= {QKV_WIDTH}], got {tuple(qkv.shape)}")
@@ -279,10 +283,14 @@ def prefill(qkv: torch.Tensor, past_lens: torch.Tensor, *, k_pool: torch.Tensor,
     _need(block_tables, "block_tables", torch.int32, dev)
     if block_tables.dim() != 2 or block_tables.shape[0] != b:
         raise ValueError("block_tables must be [batch, max_blocks_per_seq]")
-    _need(gamma_q, "gamma_q", torch.bfloat16, dev, (D,))
-    _need(gamma_k, "gamma_k", torch.bfloat16, dev, (D,))
-    _need(cos, "cos", torch.bfloat16, dev)
-    _need(sin, "sin", torch.bfloat16, dev, tuple(cos.shape))
+    rope_rows = 0
+    if mode & _lib.B2_NORM_QK:
+        _need(gamma_q, "gamma_q", torch.bfloat16, dev, (D,))
+        _need(gamma_k, "gamma_k", torch.bfloat16, dev, (D,))
+    if mode & _lib.B2_ROPE_QK:
+        _need(cos, "cos", torch.bfloat16, dev)
+        _need(sin, "sin", torch.bfloat16, dev, tuple(cos.shape))
+        rope_rows = cos.shape[0]
     _need(dev_err, "dev_err", torch.int32, dev)
     if q_out is None:
         q_out = torch.empty(b, t, HQ, D, dtype=torch.bfloat16, device=dev)
@@ -292,9 +300,8 @@ def prefill(qkv: torch.Tensor, past_lens: torch.Tensor, *, k_pool: torch.Tensor,
     _need(out, "out", torch.bfloat16, dev, (b, t, HQ, D))
     lib = _lib.load()
     st = _stream(dev, stream)
-    mode = _lib.B2_NORM_QK | _lib.B2_ROPE_QK | _lib.B2_STORE_KV
     rc = lib.b2_prefill_append(_ptr(qkv), qkv.stride(1), _ptr(gamma_q), _ptr(gamma_k), ctypes.c_float(eps),
-                               _ptr(cos), _ptr(sin), cos.shape[0], _ptr(past_lens), _ptr(chunk_lens), t,
+                               _ptr(cos), _ptr(sin), rope_rows, _ptr(past_lens), _ptr(chunk_lens), t,
                                _ptr(block_tables), block_tables.shape[1], _ptr(k_pool), _ptr(v_pool),
                                k_pool.shape[0], _ptr(q_out), b, mode, _ptr(dev_err), st)
     _lib.check(rc, "b2_prefill_append")
@@ -375,9 +382,13 @@ class PagedDecodeAttention:
 
     # ---------------------------------------------------------------- host-fed steps
 
-    def open_host_pipeline(self, layer: int, block_tables: torch.Tensor, batch: int | None = None) -> None:
-        """Prepare step_host(): device staging buffers and the C-ABI arguments
-        of b2_decode_step_host, validated once here, not per step."""
+    def open_host_pipeline(self, layer: int, block_tables: torch.Tensor, batch: int | None = None,
+                           double_buffered: bool = True) -> None:
+        """Prepare step_host(): device staging buffers and the C-ABI arguments,
+        validated once here, not per step.  double_buffered selects
+        b2_decode_step_host2 (two staging slots; copies on library-owned
+        streams overlap the neighbouring kernels) over b2_decode_step_host
+        (one slot; copies and kernel in the caller's stream order)."""
         if not self.fused:
             raise ValueError("the host-fed step runs the fused kernel")
         b = self.max_batch if batch is None else batch
@@ -389,12 +400,13 @@ class PagedDecodeAttention:
         if self.part_ml.numel() < b * splits * HQ * 2:
             raise ValueError("partial-state buffers too small")
         kp, vp = self.cache.pool(layer)
-        hp = {"b": b, "tables": block_tables, "slot": 0,
-              "qkv": torch.empty(2, b, QKV_WIDTH, dtype=torch.bfloat16, device=dev),
-              "past": torch.empty(2, b, dtype=torch.int32, device=dev),
-              "out": torch.empty(2, b, HQ, D, dtype=torch.bfloat16, device=dev)}
+        slots = 2 if double_buffered else 1
+        hp = {"b": b, "tables": block_tables, "slot": 0, "double": double_buffered,
+              "qkv": torch.empty(slots, b, QKV_WIDTH, dtype=torch.bfloat16, device=dev),
+              "past": torch.empty(slots, b, dtype=torch.int32, device=dev),
+              "out": torch.empty(slots, b, HQ, D, dtype=torch.bfloat16, device=dev)}
         lib = _lib.load()
-        hp["call"] = lib.b2_decode_step_host2
+        hp["call"] = lib.b2_decode_step_host2 if double_buffered else lib.b2_decode_step_host
         hp["join"] = lib.b2_decode_step_host_join
         hp["bufs"] = (_ptr(hp["qkv"]), _ptr(hp["past"]), _ptr(hp["out"]))
         hp["args"] = (_ptr(self.gamma_q), _ptr(self.gamma_k),
@@ -406,26 +418,32 @@ class PagedDecodeAttention:
 
     def step_host(self, qkv_host: torch.Tensor, past_host: torch.Tensor, out_host: torch.Tensor,
                   stream: torch.cuda.Stream | None = None) -> None:
-        """One decode step fed from pinned host memory (b2_decode_step_host2, one
-        call): H2D of the qkv rows [B, 2048] and past lengths [B], the fused
-        kernel on the current stream, D2H of the context into out_host
-        [B, 16, 64].  Consecutive calls alternate two device slots, so uploads
-        and downloads overlap the neighbouring steps' kernels.  Asynchronous:
-        call join_host() and synchronise the stream before reading out_host."""
+        """One decode step fed from pinned host memory (one C-ABI call): H2D of
+        the qkv rows [B, 2048] and past lengths [B], the fused kernel on the
+        current stream, D2H of the context into out_host [B, 16, 64].  When
+        double-buffered, consecutive calls alternate two device slots, so
+        uploads and downloads overlap the neighbouring steps' kernels.
+        Asynchronous: the host buffers must stay alive and unchanged until
+        join_host() and a synchronise of the stream; then out_host is valid."""
         hp = self._hp
         for t, n, dt in ((qkv_host, hp["b"] * QKV_WIDTH, torch.bfloat16), (past_host, hp["b"], torch.int32),
                          (out_host, hp["b"] * HQ * D, torch.bfloat16)):
             if t.dtype != dt or t.numel() != n or not t.is_contiguous() or not t.is_pinned():
                 raise ValueError("host buffers must be pinned, contiguous and of the pipeline's shape")
-        rc = hp["call"](ctypes.c_void_p(qkv_host.data_ptr()), ctypes.c_void_p(past_host.data_ptr()),
-                        ctypes.c_void_p(out_host.data_ptr()), *hp["bufs"], hp["slot"], *hp["args"],
-                        _stream(self.device, stream))
-        _lib.check(rc, "b2_decode_step_host2")
-        hp["slot"] ^= 1
+        host = (ctypes.c_void_p(qkv_host.data_ptr()), ctypes.c_void_p(past_host.data_ptr()),
+                ctypes.c_void_p(out_host.data_ptr()))
+        if hp["double"]:
+            rc = hp["call"](*host, *hp["bufs"], hp["slot"], *hp["args"], _stream(self.device, stream))
+            hp["slot"] ^= 1
+        else:
+            rc = hp["call"](*host, *hp["bufs"], *hp["args"], _stream(self.device, stream))
+        _lib.check(rc, "b2_decode_step_host2" if hp["double"] else "b2_decode_step_host")
 
     def join_host(self, stream: torch.cuda.Stream | None = None) -> None:
-        """Make the stream wait for every context download issued by step_host."""
-        _lib.check(self._hp["join"](_stream(self.device, stream)), "b2_decode_step_host_join")
+        """Make the stream wait for every context download issued by step_host
+        (a no-op for the single-buffered pipeline, whose copies are in stream order)."""
+        if self._hp["double"]:
+            _lib.check(self._hp["join"](_stream(self.device, stream)), "b2_decode_step_host_join")
 
     def check(self) -> None:
         """Synchronise on the device error word; raise if any kernel flagged one."""

@@ -318,26 +318,29 @@ def test_split_sequence_states_merge(cuda, total, cut):
     assert torch.equal(out, out2)
 
 
-def test_step_host_pipeline_matches_step(cuda):
-    """The host-fed pipeline (pinned H2D, fused kernel, D2H, two device slots)
-    returns what step() returns for the same inputs, over several steps."""
+@pytest.mark.parametrize("double_buffered", [True, False])
+def test_step_host_pipeline_matches_step(cuda, double_buffered):
+    """The host-fed pipeline (pinned H2D, fused kernel, D2H; two device slots
+    or one) returns what step() returns for the same inputs, over several steps."""
     lengths = [5, 300, 64, 1000]
     b = len(lengths)
     w = orc.attention_weights(0)
     outs = []
+    keep = []   # pinned inputs stay alive until the stream is synchronised
     for host in (False, True):
         cache, _ = build_batch(lengths, cuda, seed=31, capacity=1100)
         runner = _attn().PagedDecodeAttention(cache, w["q_gamma"], w["k_gamma"], b, 2048, blocks_per_split=4)
         tables = cache.block_tables()
         res = []
         if host:
-            runner.open_host_pipeline(0, tables)
+            runner.open_host_pipeline(0, tables, double_buffered=double_buffered)
             out_host = torch.empty(5, b, 16, 64, dtype=torch.bfloat16).pin_memory()
         for step in range(5):
             raw = rand_qkv(b, 60 + step)
             past = torch.tensor([n + step for n in lengths], dtype=torch.int32)
             if host:
-                runner.step_host(raw.pin_memory(), past.pin_memory(), out_host[step])
+                keep.append((raw.pin_memory(), past.pin_memory()))
+                runner.step_host(*keep[-1], out_host[step])
             else:
                 res.append(runner.step(0, raw.to(cuda), past.to(cuda), (past + 1).to(cuda), tables).cpu())
         if host:
