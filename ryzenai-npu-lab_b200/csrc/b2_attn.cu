@@ -3,6 +3,9 @@
 //   append_rope_kernel   q/k RMSNorm + rotate-half RoPE + paged KV append
 //   paged_decode_kernel  split-KV flash-decode, TMA + mbarrier pipeline
 //   combine_kernel       log-sum-exp merge of partial softmax states
+//   decode_step_kernel   the whole decode step in one persistent launch
+//                        (norm + RoPE + append + split-KV attention + merge)
+//   prefill_attn_kernel  batched-prompt attention on tcgen05 (TMEM accumulators)
 //
 // Model constants: 16 query heads, 8 KV heads, head_dim 64, 64-token blocks.
 // The numerics follow the reference's PyTorch BF16 path (Hugging Face
