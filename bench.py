@@ -72,6 +72,8 @@ def parse():
                         "c5: end-to-end greedy decode of the whole random-init model; "
                         "prefill: a chunk of --chunk new tokens per C3 sequence on the tcgen05 kernel")
     p.add_argument("--context", type=int, default=131072, help="c4: cached tokens of the sequence")
+    p.add_argument("--exchange", choices=["auto", "p2p", "collective"], default="auto",
+                   help="c4: how the ranks' partial states are merged")
     return p.parse_args()
 
 
@@ -452,7 +454,8 @@ def run_b200(args):
 def run_c4(args):
     """Config C4: one sequence of --context cached tokens split along the token
     axis over the ranks; per step each rank appends (last rank) and attends over
-    its tokens, the partial states are all-gathered (NCCL) and merged."""
+    its tokens, the partial states are exchanged (NVLink P2P kernel, or an NCCL
+    all-gather with --exchange collective) and merged."""
     import datetime
     world, rank, local = dist_env()
     if "RANK" not in os.environ:   # single process without torchrun: a world of one
@@ -471,7 +474,8 @@ def run_c4(args):
     gamma_q = (1.0 + 0.1 * torch.randn(D, generator=gg)).to(torch.bfloat16)
     gamma_k = (1.0 + 0.1 * torch.randn(D, generator=gg)).to(torch.bfloat16)
     lc = dmod.LongContextDecode(args.context + 1, gamma_q, gamma_k, device=dev,
-                                blocks_per_split=args.bps or None, growth=64)
+                                blocks_per_split=args.bps or None, growth=64, exchange=args.exchange,
+                                max_ctas=args.max_ctas)
     gen = torch.Generator(device=dev).manual_seed(args.seed * 1000 + rank + 29)
     lc.fill_random(args.context, gen)
     lc.set_lengths(args.context)
@@ -482,17 +486,28 @@ def run_c4(args):
             lc.step(qkv[j % 8])
     stream.synchronize()
     lc.check()
-    ev0 = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(K)]
-    ev1 = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(K)]
+    # the timed graph: K whole steps, no event nodes between the launches
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
         for j in range(K):
-            ev0[j].record()
-            lc.partial(qkv[j % 8])
-            ev1[j].record()
-            lc.merge()
+            lc.step(qkv[j % 8])
+    # a second graph brackets the local partial of every step with events
+    # (the roofline's kernel time); with one GPU the partial is the step
+    ev0 = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(K)]
+    ev1 = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(K)]
+    graph_ev = None
+    if world > 1:
+        graph_ev = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph_ev, stream=stream):
+            for j in range(K):
+                ev0[j].record()
+                lc.partial(qkv[j % 8])
+                ev1[j].record()
+                lc.merge()
+        graph_ev.replay()
     graph.replay()
     torch.cuda.synchronize()
+    lc.check()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     torch.distributed.barrier()
@@ -506,7 +521,14 @@ def run_c4(args):
     torch.distributed.barrier()
     lc.check()
     ms = t0.elapsed_time(t1)
-    part_ms = sum(a.elapsed_time(b) for a, b in zip(ev0, ev1)) / K
+    if graph_ev is not None:
+        with torch.cuda.stream(stream):
+            graph_ev.replay()
+        torch.cuda.synchronize()
+        lc.check()
+        part_ms = sum(a.elapsed_time(b) for a, b in zip(ev0, ev1)) / K
+    else:
+        part_ms = ms / K
     local_tokens = lc.local_len + (1 if lc.is_tail else 0)
     local_bytes = KV_BYTES_PER_TOKEN * local_tokens + 2048 * 2 + 2 * 1024
     times = torch.tensor([ms, part_ms], dtype=torch.float64, device=dev)
@@ -519,21 +541,26 @@ def run_c4(args):
         "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": f"C4 long-context decode: one sequence of {args.context} cached tokens "
-                               f"split along the token axis over {world} GPU(s), partial states "
-                               f"all-gathered over NCCL and merged", "context": args.context,
+                               f"split along the token axis over {world} GPU(s), partial softmax states "
+                               + {"p2p": "exchanged over NVLink peer memory and merged in one kernel "
+                                         "(b2_exchange_merge)",
+                                  "collective": "all-gathered over NCCL and merged",
+                                  "direct": "(one GPU: merged in the step)"}[lc.exchange],
+                   "context": args.context, "exchange": lc.exchange,
                    "global_batch": 1, "blocks_per_split": lc.bps, "parallelism": f"split-kv x{world}",
                    "l2": "inputs larger than L2 (268 MB of K/V), no flush"},
         "hbm_gbs_aggregate": total_bytes / (ms / K / 1e3) / 1e9,
-        "roofline": {"bound": "hbm", "kernel": "paged_decode_kernel (+append, local merge)",
+        "roofline": {"bound": "hbm", "kernel": "decode_step_kernel (+ combine of its splits)",
                      "achieved": local_bytes / (part_ms / 1e3) / 1e9, "peak": peak, "peak_source": peak_kind,
                      "unit": "GB/s", "frac": local_bytes / (part_ms / 1e3) / 1e9 / peak, "traffic": None,
                      "algorithmic_bytes": local_bytes, "avg_launch_ms": part_ms},
         "clocks": clocks.summary(),
-        "gpu_launches": K * 3,
+        "gpu_launches": K * (1 + (lc.splits > 16) + {"p2p": 1, "collective": 2, "direct": 0}[lc.exchange]),
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
-    del graph
+    del graph, graph_ev
+    lc.close()
     torch.distributed.barrier()
     torch.distributed.destroy_process_group()
 

@@ -185,7 +185,7 @@ int b2_combine(const float *part_ml, const float *part_o, int32_t num_parts,
  *              before the first call; every call that completes leaves it
  *              zero again (after a device error, zero it again).
  * part_ml/o    as b2_decode_attn with num_splits = ceil(max_blocks / bps).
- * blocks_per_split  1 .. 32.
+ * blocks_per_split  1 .. 64.
  * q_out        optional bf16 [batch][16][64] normalised + rotated q.
  * Calls sharing `counters` must not overlap on the GPU.
  */
@@ -260,6 +260,39 @@ int b2_decode_step_host_join(void *stream);
 int b2_merge_states(const float *states, int32_t num_parts, int32_t batch,
                     uint16_t *out, float *state_ml, float *state_o,
                     void *stream);
+
+/*
+ * Multi-GPU merge without a collective library (config C4 over NVLink).
+ * Replaces the all-gather + b2_merge_states pair that the split-KV long
+ * context needs (the reference itself has no multi-device code: its long
+ * contexts stream 64-token blocks through one NPU core,
+ * experiments/lfm25_attention_chunked_cache_kernel.py:21-89, and merge with
+ * the chunked kernel's online-softmax state, kernels/lfm25_attention_chunked_head.cc:73-88).
+ *
+ * Every rank owns an exchange area of b2_exchange_bytes(world, batch) bytes
+ * in its own device memory, zeroed before first use, and maps the other
+ * ranks' areas with b2_ipc_handle (export: a 64-byte handle and the offset of
+ * `ptr` in its allocation) / b2_ipc_open (import on another process) /
+ * b2_ipc_close.  b2_exchange_merge(state_ml [batch][16][2], state_o
+ * [batch][16][64], areas[world] = every rank's area as mapped on this GPU,
+ * areas[rank] = this rank's own) writes this rank's state into every area
+ * (each value with a step tag in one 8-byte store), waits until the other
+ * ranks' values of this step are in its own area and merges the world's
+ * states into out (bf16 [batch][16][64]).  All ranks must
+ * call it the same number of times, each on its own GPU (it waits for the
+ * others; two ranks on one GPU are not supported).  A wait gives up after
+ * 5 s and sets B2_DEV_TIMEOUT in dev_err, leaving out unwritten; the areas
+ * must then be zeroed again on every rank before the next call.
+ * Launched as a programmatic dependent of the previous kernel in the stream.
+ */
+#define B2_XCHG_MAX_WORLD 8
+int64_t b2_exchange_bytes(int32_t world, int32_t batch);
+int b2_ipc_handle(const void *ptr, void *handle64, int64_t *offset);
+int b2_ipc_open(const void *handle64, int64_t offset, void **peer_ptr);
+int b2_ipc_close(void *peer_ptr, int64_t offset);
+int b2_exchange_merge(const float *state_ml, const float *state_o, int32_t batch,
+                      void *const *areas, int32_t world, int32_t rank,
+                      uint16_t *out, int32_t *dev_err, void *stream);
 
 /*
  * Batched-prompt (prefill) attention: a chunk of `tokens` new tokens per

@@ -26,6 +26,7 @@ B2_ROPE_QK = 2
 B2_STORE_KV = 4
 
 B2_NOALLOC_MAX_PARTS = 1024   # batch * num_splits limit of b2_decode_attn_noalloc
+B2_XCHG_MAX_WORLD = 8         # ranks of b2_exchange_merge
 
 DEV_ERR_NAMES = {
     B2_DEV_BAD_BLOCK: "block table entry outside the pool",
@@ -98,6 +99,15 @@ SIGNATURES = {
         _p,                  # stream
     ]),
     "b2_decode_step_host_join": (ctypes.c_int, [_p]),
+    "b2_exchange_bytes": (ctypes.c_int64, [_i32, _i32]),
+    "b2_ipc_handle": (ctypes.c_int, [_p, _p, ctypes.POINTER(ctypes.c_int64)]),
+    "b2_ipc_open": (ctypes.c_int, [_p, ctypes.c_int64, ctypes.POINTER(ctypes.c_void_p)]),
+    "b2_ipc_close": (ctypes.c_int, [_p, ctypes.c_int64]),
+    "b2_exchange_merge": (ctypes.c_int, [
+        _p, _p, _i32,        # state_ml, state_o, batch
+        _p, _i32, _i32,      # areas (host array of world pointers), world, rank
+        _p, _p, _p,          # out, dev_err, stream
+    ]),
     "b2_merge_states": (ctypes.c_int, [
         _p, _i32, _i32,      # states, num_parts, batch
         _p, _p, _p, _p,      # out, state_ml, state_o, stream

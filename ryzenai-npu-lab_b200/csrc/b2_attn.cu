@@ -642,6 +642,7 @@ constexpr int kMergerWarp = kConsumerWarps + 1;
 constexpr int kStepThreads = (kConsumerWarps + 2) * 32;
 constexpr int kPubSlots = 4;  // items published to the merger warp, in flight
 constexpr int kMergeInKernelSplits = 16;
+constexpr int kStepMaxBlocksPerSplit = 64;  // two block-table entries per producer lane
 
 struct __align__(16) StepTail {
   uint64_t full[kStages];
@@ -707,6 +708,7 @@ __device__ __forceinline__ bool step_lengths(const StepArgs &a, int b, int &past
 struct ProducerItem {
   int valid, b, kvh, split, past, seq_len, nsplit, blk0, n;
   int my_blk;   // block table entry blk0 + lane (lane < n)
+  int my_blk2;  // block table entry blk0 + 32 + lane (32 + lane < n)
   uint4 raw;    // this lane's 16 bytes of the item's q/k/v vectors
 };
 
@@ -745,6 +747,7 @@ __device__ __forceinline__ ProducerItem producer_load(const StepArgs &a, const S
   it.blk0 = it.split * a.blocks_per_split;
   it.n = min(a.blocks_per_split, nblk - it.blk0);
   it.my_blk = lane < it.n ? __ldg(a.block_tables + (int64_t)it.b * a.max_blocks + it.blk0 + lane) : 0;
+  it.my_blk2 = lane + 32 < it.n ? __ldg(a.block_tables + (int64_t)it.b * a.max_blocks + it.blk0 + 32 + lane) : 0;
   const int grp = lane >> 3;
   const int vec = grp < 2 ? 2 * it.kvh + grp : (grp == 2 ? kHq + it.kvh : kHq + kHkv + it.kvh);
   it.raw = __ldg(reinterpret_cast<const uint4 *>(a.qkv + it.b * a.row_stride + vec * kDim + (lane & 7) * 8));
@@ -848,7 +851,8 @@ __device__ __forceinline__ void step_producer(const StepArgs &a, StepTail *tail,
     if (cur.split == cur.nsplit - 1 && (a.mode & B2_STORE_KV)) {
       // The new token's row lies in this item's last block: write it, then
       // fence so the TMA (async proxy) read of that tile sees the store.
-      const int blk = __shfl_sync(0xffffffffu, cur.my_blk, cur.past / kBlock - cur.blk0);
+      const int idx = cur.past / kBlock - cur.blk0;  // < n <= 64, the same in every lane
+      const int blk = __shfl_sync(0xffffffffu, idx < 32 ? cur.my_blk : cur.my_blk2, idx & 31);
       if (blk < 0 || blk >= a.num_blocks) {
         if (lane == 0) atomicOr(a.err, B2_DEV_BAD_BLOCK);
       } else if (grp >= 2) {
@@ -870,7 +874,7 @@ __device__ __forceinline__ void step_producer(const StepArgs &a, StepTail *tail,
         ok = false;
         break;
       }
-      int blk = __shfl_sync(0xffffffffu, cur.my_blk, jj);
+      int blk = __shfl_sync(0xffffffffu, jj < 32 ? cur.my_blk : cur.my_blk2, jj & 31);
       StageMeta &m = tail->meta[s];
       if (jj == 0 && grp < 2) *reinterpret_cast<uint4 *>(m.q + grp * kDim + j * 8) = packed;
       if (lane == 0) {
@@ -1358,20 +1362,6 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float v[64]) {
 }
 
 // 16 consecutive fp32 columns of this thread's TMEM lane.
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float v[16]) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-__device__ __forceinline__ void pf_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
-
 // Barrier of the 4 softmax warps that also ORs a flag across them, so that a
 // decision taken after it is the same in every thread.
 __device__ __forceinline__ int pf_bar_or(int flag) {
@@ -1815,8 +1805,8 @@ extern "C" int b2_decode_step(const uint16_t *qkv, int64_t row_stride, const uin
   if (num_blocks <= 0 || static_cast<int64_t>(num_blocks) * kHkv * kBlock >= (int64_t(1) << 31))
     return fail(B2_ERR_ARG, "num_blocks must be in [1, 2^22) (got %d)", num_blocks);
   if (max_blocks_per_seq <= 0) return fail(B2_ERR_ARG, "max_blocks_per_seq must be positive");
-  if (blocks_per_split < 1 || blocks_per_split > 32)
-    return fail(B2_ERR_ARG, "blocks_per_split must be in [1, 32] (got %d)", blocks_per_split);
+  if (blocks_per_split < 1 || blocks_per_split > kStepMaxBlocksPerSplit)
+    return fail(B2_ERR_ARG, "blocks_per_split must be in [1, %d] (got %d)", kStepMaxBlocksPerSplit, blocks_per_split);
   if (!(scale > 0.f)) return fail(B2_ERR_ARG, "scale must be positive");
   const int64_t splits = (static_cast<int64_t>(max_blocks_per_seq) + blocks_per_split - 1) / blocks_per_split;
   const int64_t total = splits * batch * kHkv;
@@ -1839,6 +1829,11 @@ extern "C" int b2_decode_step(const uint16_t *qkv, int64_t row_stride, const uin
   int64_t ctas = static_cast<int64_t>(sm_count()) * 3;
   if (max_ctas > 0 && max_ctas < ctas) ctas = max_ctas;
   if (ctas > total) ctas = total;
+  // Equal waves: items are handed out dynamically, so with `waves` rounds the
+  // last round should be as full as the others (e.g. 520 items run as 2 x 260
+  // rather than 444 + 76; every CTA then streams the same number of blocks).
+  const int64_t waves = (total + ctas - 1) / ctas;
+  ctas = (total + waves - 1) / waves;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaLaunchAttribute pdl[1];
   pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -2083,6 +2078,193 @@ extern "C" int b2_decode_step_host_join(void *stream) {
       cudaStreamWaitEvent(static_cast<cudaStream_t>(stream), p->d2h_done, 0) != cudaSuccess)
     return fail(B2_ERR_CUDA, "cannot join the host pipeline: %s", cudaGetErrorString(cudaGetLastError()));
   return ok();
+}
+
+namespace {
+
+// ------------------------------------------------------------------ multi-GPU state exchange (NVLink P2P)
+
+// One sequence's KV cache split along the token axis over `world` GPUs: every
+// rank holds a partial softmax state (max, sum, unnormalised output) per
+// (sequence, query head).  Instead of an all-gather collective followed by a
+// merge launch, one kernel writes this rank's state straight into every
+// rank's exchange area over NVLink (peer pointers from CUDA IPC) and merges
+// the world's states once they have arrived in its own area.
+//
+// Every value travels as one 8-byte word {float bits, tag}, written with a
+// single 8-byte store, where tag = step number + 1 (the low-latency protocol
+// of collective libraries): a reader polls the words themselves until their
+// tags show the current step, so no fence or separate flag is needed.
+// Exchange area (every rank, same layout; zeroed before first use):
+//   uint2 word[2 slots][world][batch][16][kXState]   (m, l, 2 unused, o[64])
+//   int   step[batch][16]                            (local step counter)
+// Steps alternate slots.  A rank can be at most one step ahead of another
+// (its next merge needs the other's words of that step, written after the
+// other's previous merge finished reading), so a slot is never overwritten
+// while it is read.
+
+constexpr int kXState = 4 + kDim;
+constexpr int kXMaxWorld = B2_XCHG_MAX_WORLD;
+constexpr uint64_t kXWaitNs = 5000000000ull;  // 5 s, then B2_DEV_TIMEOUT
+
+struct XchgArgs {
+  const float *state_ml;  // [batch][16][2]
+  const float *state_o;   // [batch][16][64]
+  int batch, world, rank;
+  uint16_t *out;  // [batch][16][64]
+  int32_t *err;
+  char *area[kXMaxWorld];  // rank r's exchange area as mapped on this GPU
+};
+
+__host__ __device__ constexpr int64_t x_words(int world, int batch) {
+  return 2ll * world * batch * kHq * kXState;
+}
+
+__device__ __forceinline__ void st_word(uint2 *p, float v, uint32_t tag) {
+  asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(__float_as_uint(v)), "r"(tag)
+               : "memory");
+}
+
+__device__ __forceinline__ uint2 ld_word(const uint2 *p) {
+  uint2 w;
+  asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(w.x), "=r"(w.y) : "l"(p) : "memory");
+  return w;
+}
+
+// grid (batch, 16 heads), block 64 threads (one per output dim).
+__global__ void __launch_bounds__(kDim) exchange_merge_kernel(const XchgArgs a) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const int b = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+  const int bh = b * kHq + h;
+  const uint2 *own = reinterpret_cast<const uint2 *>(a.area[a.rank]);
+  int32_t *steps = reinterpret_cast<int32_t *>(reinterpret_cast<uint2 *>(a.area[a.rank]) + x_words(a.world, a.batch));
+  const int32_t step = steps[bh];
+  const int slot = step & 1;
+  const uint32_t tag = static_cast<uint32_t>(step) + 1u;
+  const float m = a.state_ml[bh * 2], l = a.state_ml[bh * 2 + 1], o = a.state_o[(int64_t)bh * kDim + d];
+  const int64_t mine = (((static_cast<int64_t>(slot) * a.world + a.rank) * a.batch + b) * kHq + h) * kXState;
+  for (int r = 0; r < a.world; ++r) {
+    uint2 *dst = reinterpret_cast<uint2 *>(a.area[r]) + mine;
+    st_word(dst + 4 + d, o, tag);
+    if (d == 0) {
+      st_word(dst, m, tag);
+      st_word(dst + 1, l, tag);
+    }
+  }
+  float M = -1.0e30f, L = 0.f, O = 0.f;
+  bool ok = true;
+  const uint64_t t0 = global_ns();
+  for (int r = 0; r < a.world && ok; ++r) {
+    const uint2 *src = own + (((static_cast<int64_t>(slot) * a.world + r) * a.batch + b) * kHq + h) * kXState;
+    uint2 wm, wl, wo;
+    for (;;) {
+      wm = ld_word(src);
+      wl = ld_word(src + 1);
+      wo = ld_word(src + 4 + d);
+      if (wm.y == tag && wl.y == tag && wo.y == tag) break;
+      if (global_ns() - t0 > kXWaitNs) {
+        atomicOr(a.err, B2_DEV_TIMEOUT);
+        ok = false;
+        break;
+      }
+    }
+    if (!ok) break;
+    const float ms = __uint_as_float(wm.x), ls = __uint_as_float(wl.x), os = __uint_as_float(wo.x);
+    const float nm = fmaxf(M, ms);
+    const float c1 = ex2(M - nm), c2 = ex2(ms - nm);
+    L = L * c1 + ls * c2;
+    O = O * c1 + os * c2;
+    M = nm;
+  }
+  if (ok) a.out[(int64_t)bh * kDim + d] = static_cast<uint16_t>(bf16_bits(L > 0.f ? O / L : 0.f));
+  __syncthreads();
+  if (d == 0) steps[bh] = step + 1;
+}
+
+using PFN_memGetAddressRange = CUresult (*)(CUdeviceptr *, size_t *, CUdeviceptr);
+
+PFN_memGetAddressRange address_range_fn() {
+  static PFN_memGetAddressRange fn = nullptr;
+  if (!fn) {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_memGetAddressRange>(p);
+  }
+  return fn;
+}
+
+}  // namespace
+
+extern "C" int64_t b2_exchange_bytes(int32_t world, int32_t batch) {
+  if (world < 1 || world > kXMaxWorld || batch < 1) return 0;
+  return x_words(world, batch) * 8 + static_cast<int64_t>(batch) * kHq * 4;
+}
+
+extern "C" int b2_ipc_handle(const void *ptr, void *handle, int64_t *offset) {
+  if (!ptr || !handle || !offset) return fail(B2_ERR_ARG, "null pointer argument");
+  auto fn = address_range_fn();
+  if (!fn) return fail(B2_ERR_NOSYM, "cuMemGetAddressRange is not available from the driver");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (fn(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)
+    return fail(B2_ERR_ARG, "pointer is not device memory of this context");
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void *>(base));
+  if (e != cudaSuccess) return fail(B2_ERR_CUDA, "cudaIpcGetMemHandle failed: %s", cudaGetErrorString(e));
+  memcpy(handle, &h, sizeof(h));
+  *offset = static_cast<int64_t>(reinterpret_cast<CUdeviceptr>(ptr) - base);
+  return ok();
+}
+
+extern "C" int b2_ipc_open(const void *handle, int64_t offset, void **peer_ptr) {
+  if (!handle || !peer_ptr || offset < 0) return fail(B2_ERR_ARG, "bad argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void *base = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return fail(B2_ERR_CUDA, "cudaIpcOpenMemHandle failed: %s", cudaGetErrorString(e));
+  *peer_ptr = static_cast<char *>(base) + offset;
+  return ok();
+}
+
+extern "C" int b2_ipc_close(void *peer_ptr, int64_t offset) {
+  if (!peer_ptr || offset < 0) return fail(B2_ERR_ARG, "bad argument");
+  const cudaError_t e = cudaIpcCloseMemHandle(static_cast<char *>(peer_ptr) - offset);
+  if (e != cudaSuccess) return fail(B2_ERR_CUDA, "cudaIpcCloseMemHandle failed: %s", cudaGetErrorString(e));
+  return ok();
+}
+
+extern "C" int b2_exchange_merge(const float *state_ml, const float *state_o, int32_t batch, void *const *areas,
+                                 int32_t world, int32_t rank, uint16_t *out, int32_t *dev_err, void *stream) {
+  if (batch < 0) return fail(B2_ERR_ARG, "batch must be >= 0");
+  if (batch == 0) return ok();
+  if (batch > 65535) return fail(B2_ERR_ARG, "batch must be <= 65535");
+  if (world < 1 || world > kXMaxWorld) return fail(B2_ERR_ARG, "world must be in [1, %d]", kXMaxWorld);
+  if (rank < 0 || rank >= world) return fail(B2_ERR_ARG, "rank must be in [0, world)");
+  if (!state_ml || !state_o || !areas || !out || !dev_err) return fail(B2_ERR_ARG, "null pointer argument");
+  XchgArgs a{state_ml, state_o, batch, world, rank, out, dev_err, {}};
+  for (int r = 0; r < world; ++r) {
+    if (!areas[r] || (reinterpret_cast<uintptr_t>(areas[r]) & 15))
+      return fail(B2_ERR_ARG, "exchange area %d is null or not 16-byte aligned", r);
+    a.area[r] = static_cast<char *>(areas[r]);
+  }
+  cudaLaunchAttribute pdl[1];
+  pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  pdl[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(batch), kHq);
+  cfg.blockDim = dim3(kDim);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cfg.attrs = pdl;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, exchange_merge_kernel, a) != cudaSuccess) {
+    const cudaError_t e = cudaGetLastError();
+    return fail(B2_ERR_CUDA, "exchange_merge_kernel launch failed: %s", cudaGetErrorString(e));
+  }
+  return launch_status("exchange_merge_kernel");
 }
 
 // ------------------------------------------------------------------ allocation-free decode

@@ -12,11 +12,17 @@ Two modes:
     path, each rank decodes its own sequences.
   * long context (config C4): the tokens of one sequence are split along the
     token axis (`token_ranges`); every rank computes a partial softmax state
-    (max, sum, output) of the new query over its tokens, the states are
-    all-gathered (16 x 66 fp32 = 4224 bytes per rank) and merged with the same
-    log-sum-exp kernel that merges the splits inside one GPU.
+    (max, sum, output) of the new query over its tokens and the states are
+    merged.  Two exchanges: "p2p" (default on one host, one GPU per rank) —
+    one kernel, b2_exchange_merge, writes the state into every rank's
+    exchange area over NVLink, waits for the others' and merges, no
+    collective library; "collective" — an all-gather (16 x 66 fp32 = 4224
+    bytes per rank; NCCL, or gloo on CPU) and the log-sum-exp merge kernel.
 """
 from __future__ import annotations
+
+import ctypes
+import socket
 
 import torch
 import torch.distributed as dist
@@ -72,15 +78,85 @@ def gather_states(state: torch.Tensor, group=None) -> torch.Tensor:
     return out
 
 
+def p2p_possible(hosts: list[str], devices: list[str]) -> bool:
+    """The P2P exchange needs every rank on one host and on its own GPU (its
+    kernel waits for the other ranks; two ranks on one GPU could deadlock)."""
+    return len(set(hosts)) == 1 and len(set(devices)) == len(devices) and 1 < len(devices) <= _lib.B2_XCHG_MAX_WORLD
+
+
+class PeerExchange:
+    """Exchange areas for b2_exchange_merge: one in this rank's memory, the
+    other ranks' mapped through CUDA IPC (peer access over NVLink).  All ranks
+    of `group` construct it together; close() together."""
+
+    def __init__(self, batch: int, group=None, device: torch.device | str = "cuda"):
+        lib = _lib.load()
+        self.lib, self.group = lib, group
+        self.device = torch.device(device)
+        self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        self.batch = batch
+        nbytes = lib.b2_exchange_bytes(self.world, batch)
+        if nbytes <= 0:
+            raise ValueError(f"exchange of world {self.world}, batch {batch} is not supported")
+        self.area = torch.zeros(nbytes // 4, dtype=torch.int32, device=self.device)
+        handle = ctypes.create_string_buffer(64)
+        offset = ctypes.c_int64(0)
+        _lib.check(lib.b2_ipc_handle(ctypes.c_void_p(self.area.data_ptr()), handle, ctypes.byref(offset)),
+                   "b2_ipc_handle")
+        uuid = str(torch.cuda.get_device_properties(self.device).uuid)
+        info = [None] * self.world
+        dist.all_gather_object(info, (handle.raw, offset.value, socket.gethostname(), uuid), group=group)
+        if not p2p_possible([i[2] for i in info], [i[3] for i in info]):
+            raise ValueError("the P2P exchange needs all ranks on one host, each on its own GPU")
+        self.opened = []
+        ptrs = []
+        for r, (h, off, _, _) in enumerate(info):
+            if r == self.rank:
+                ptrs.append(self.area.data_ptr())
+                continue
+            peer = ctypes.c_void_p()
+            _lib.check(lib.b2_ipc_open(h, off, ctypes.byref(peer)), "b2_ipc_open")
+            self.opened.append((peer.value, off))
+            ptrs.append(peer.value)
+        self.areas = (ctypes.c_void_p * self.world)(*ptrs)
+        dist.barrier(group=group)
+
+    def merge(self, state_ml: torch.Tensor, state_o: torch.Tensor, out: torch.Tensor, dev_err: torch.Tensor,
+              stream: torch.cuda.Stream | None = None) -> None:
+        """This rank's state in, the world-merged bf16 context out (one launch)."""
+        from .attention import _ptr, _stream
+        rc = self.lib.b2_exchange_merge(_ptr(state_ml), _ptr(state_o), self.batch, self.areas, self.world,
+                                        self.rank, _ptr(out), _ptr(dev_err), _stream(self.device, stream))
+        _lib.check(rc, "b2_exchange_merge")
+
+    def reset(self) -> None:
+        """Zero the area (after a device error; every rank, then a barrier)."""
+        self.area.zero_()
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+
+    def close(self) -> None:
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for ptr, off in self.opened:
+            _lib.check(self.lib.b2_ipc_close(ctypes.c_void_p(ptr), off), "b2_ipc_close")
+        self.opened = []
+
+
 class LongContextDecode:
     """One sequence whose KV cache is split along the token axis over the ranks
     of `group`.  Rank r holds tokens token_ranges(capacity)[r] in its own
     paged pool; new tokens are appended on the last rank.  step() returns the
-    bf16 context [16, 64] on every rank."""
+    bf16 context [16, 64] on every rank.
+
+    exchange: "p2p" (b2_exchange_merge over NVLink peer memory), "collective"
+    (all-gather + merge kernel) or "auto" (p2p when the ranks are on distinct
+    GPUs of one host with NCCL as the backend, else collective).  A world of
+    one writes the context directly."""
 
     def __init__(self, capacity: int, gamma_q: torch.Tensor, gamma_k: torch.Tensor, *, group=None,
                  device: torch.device | str = "cuda", blocks_per_split: int | None = None, eps: float = EPS,
-                 growth: int = 4096):
+                 growth: int = 4096, exchange: str = "auto", max_ctas: int = 0):
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
@@ -120,6 +196,21 @@ class LongContextDecode:
         self.counters = torch.zeros(2 + 8, dtype=torch.int32, device=self.device)
         self.past = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.seq = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.max_ctas = max_ctas
+        if exchange not in ("auto", "p2p", "collective"):
+            raise ValueError("exchange must be auto, p2p or collective")
+        self.peer = None
+        if self.world > 1 and exchange != "collective" and self.device.type == "cuda":
+            if exchange == "p2p":
+                self.peer = PeerExchange(1, group, self.device)
+            elif dist.get_backend(group) == "nccl":
+                try:
+                    self.peer = PeerExchange(1, group, self.device)
+                except ValueError:
+                    self.peer = None
+        elif exchange == "p2p":
+            raise ValueError("the P2P exchange needs CUDA devices and a world of more than one")
+        self.exchange = "p2p" if self.peer is not None else ("direct" if self.world == 1 else "collective")
 
     def load_history(self, k: torch.Tensor, v: torch.Tensor) -> None:
         """k, v: [8, L, 64] of the whole sequence (only this rank's range is kept)."""
@@ -168,22 +259,40 @@ class LongContextDecode:
         kp, vp = self.cache.pool(0)
         # RoPE rows are read at past_lens; offsetting the table by this rank's
         # first global token turns the local slot into the global position.
+        direct = self.exchange == "direct"
         decode_step(qkv, self.past, k_pool=kp, v_pool=vp, block_tables=self.tables, blocks_per_split=self.bps,
-                    out=None, part_ml=self.part_ml, part_o=self.part_o, counters=self.counters,
-                    dev_err=self.dev_err, gamma_q=self.gamma_q, gamma_k=self.gamma_k,
+                    out=self.out if direct else None, part_ml=self.part_ml, part_o=self.part_o,
+                    counters=self.counters, dev_err=self.dev_err, gamma_q=self.gamma_q, gamma_k=self.gamma_k,
                     cos=self.cos_all[self.start:], sin=self.sin_all[self.start:], q_out=self.q,
-                    seq_lens=None if self.is_tail else self.seq, state_ml=self.state_ml, state_o=self.state_o,
-                    mode=mode, eps=self.eps, stream=stream)
+                    seq_lens=None if self.is_tail else self.seq,
+                    state_ml=None if direct else self.state_ml, state_o=None if direct else self.state_o,
+                    mode=mode, eps=self.eps, max_ctas=self.max_ctas, stream=stream)
 
     def merge(self, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
-        """Exchange the local states (one all-gather) and merge them into the context."""
-        allst = gather_states(self.state, self.group)            # [world, 16 * 66]
-        merge_states(allst, self.world, 1, out=self.out, stream=stream)
+        """Exchange the local states and merge them into the context: one P2P
+        kernel, or an all-gather and the merge kernel (nothing for a world of one)."""
+        if self.exchange == "p2p":
+            self.peer.merge(self.state_ml, self.state_o, self.out, self.dev_err, stream)
+        elif self.exchange == "collective":
+            allst = gather_states(self.state, self.group)            # [world, 16 * 66]
+            merge_states(allst, self.world, 1, out=self.out, stream=stream)
         return self.out[0]
+
+    def close(self) -> None:
+        """Release the peer mappings (every rank together)."""
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
 
     def check(self) -> None:
         word = int(self.dev_err.item())
         if word:
             self.dev_err.zero_()
             self.counters.zero_()
-            raise RuntimeError("long-context decode device error: " + "; ".join(_lib.decode_dev_err(word)))
+            raise RuntimeError("long-context decode device error: " + "; ".join(_lib.decode_dev_err(word)) +
+                               ("; call reset_exchange() on every rank" if self.peer is not None else ""))
+
+    def reset_exchange(self) -> None:
+        """After a device error in the P2P exchange: zero the areas (every rank)."""
+        if self.peer is not None:
+            self.peer.reset()

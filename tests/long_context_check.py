@@ -1,11 +1,13 @@
 """Long-context split-KV decode across the ranks of a torchrun job, checked
 against the CPU oracle on every rank.  Run by tests/test_long_context_gpu.py:
 
-    python -m torch.distributed.run --standalone --nproc-per-node N tests/long_context_check.py TOTAL
+    python -m torch.distributed.run --standalone --nproc-per-node N tests/long_context_check.py TOTAL EXCHANGE
 
 Each rank holds a block-aligned token range of one sequence; every rank
-computes a partial softmax state, the states are all-gathered over NCCL and
-merged.  Three decode steps are run (the new token lives on the last rank).
+computes a partial softmax state; the states are exchanged (EXCHANGE "p2p":
+b2_exchange_merge over NVLink peer memory; "collective": NCCL all-gather +
+merge kernel) and merged.  Five decode steps are run (the new token lives on
+the last rank), so the exchange's two slots are each reused.
 Exit status 0 when every step's context is within the attention tolerance.
 """
 import datetime
@@ -26,6 +28,7 @@ dmod = importlib.import_module("ryzenai-npu-lab_b200.distributed")
 
 def main():
     total = int(sys.argv[1]) if len(sys.argv) > 1 else 5000
+    exchange = sys.argv[2] if len(sys.argv) > 2 else "collective"
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -34,9 +37,11 @@ def main():
     w = orc.attention_weights(0)
     k, v = orc.past_cache(77, total)
     k, v = k[0], v[0]
-    steps = 3
+    steps = 5
     lc = dmod.LongContextDecode(total + steps, w["q_gamma"], w["k_gamma"], device=dev, blocks_per_split=4,
-                                growth=steps + 64)
+                                growth=steps + 64, exchange=exchange)
+    want = "direct" if dist.get_world_size() == 1 else exchange
+    assert lc.exchange == want, (lc.exchange, want)
     lc.load_history(k, v)
     ok = True
     for step in range(steps):
@@ -52,8 +57,9 @@ def main():
         got = out.float().cpu()
         err = (got - ctx.float()).abs().max().item()
         rel = ((got - ctx.float()).norm() / ctx.float().norm()).item()
-        print(f"rank {rank} step {step}: max-abs {err:.3e} rel {rel:.3e}", flush=True)
+        print(f"rank {rank} step {step} ({lc.exchange}): max-abs {err:.3e} rel {rel:.3e}", flush=True)
         ok &= err <= 2e-2 and rel <= 1e-2 and bool(torch.isfinite(got).all())
+    lc.close()
     flag = torch.tensor([0 if ok else 1], device=dev)
     dist.all_reduce(flag)
     dist.destroy_process_group()

@@ -41,6 +41,23 @@ def test_token_ranges_cover_and_align(total, world):
     assert max(sizes) - min(sizes) <= 64 * 2
 
 
+def test_p2p_exchange_needs_one_host_and_distinct_gpus():
+    dist_mod = load_pkg("distributed")
+    assert dist_mod.p2p_possible(["h", "h"], ["GPU-a", "GPU-b"])
+    assert not dist_mod.p2p_possible(["h", "h"], ["GPU-a", "GPU-a"])     # two ranks on one GPU
+    assert not dist_mod.p2p_possible(["h", "g"], ["GPU-a", "GPU-b"])     # two hosts
+    assert not dist_mod.p2p_possible(["h"], ["GPU-a"])                   # a world of one merges directly
+    assert not dist_mod.p2p_possible(["h"] * 9, [f"GPU-{i}" for i in range(9)])
+
+
+def test_exchange_area_size():
+    lib = load_pkg("_lib").load()
+    # [2 slots][world][batch][16][68] tagged 8-byte words + [batch][16] step counters
+    assert lib.b2_exchange_bytes(2, 1) == 2 * 2 * 16 * 68 * 8 + 16 * 4
+    assert lib.b2_exchange_bytes(8, 3) == 2 * 8 * 3 * 16 * 68 * 8 + 3 * 16 * 4
+    assert lib.b2_exchange_bytes(9, 1) == 0 and lib.b2_exchange_bytes(0, 1) == 0 and lib.b2_exchange_bytes(2, 0) == 0
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))

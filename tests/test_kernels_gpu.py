@@ -133,7 +133,7 @@ def test_append_with_norm_matches_oracle(cuda):
 
 
 @pytest.mark.parametrize("fused", [True, False], ids=["fused", "three_kernels"])
-@pytest.mark.parametrize("bps", [1, 2, 3, 16])
+@pytest.mark.parametrize("bps", [1, 2, 3, 16, 40, 64])
 def test_decode_ragged_vs_oracle(cuda, bps, fused):
     lengths = [1, 2, 63, 64, 65, 127, 128, 129, 1000, 4097]
     cache, hist = build_batch([n - 1 for n in lengths], cuda, seed=3)
