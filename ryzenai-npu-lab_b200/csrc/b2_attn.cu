@@ -203,9 +203,8 @@ struct AppendArgs {
 //    IEEE-rounded sqrt and divide, as torch's CPU rsqrt computes 1/sqrt.
 //  * RoPE: bf16(bf16(x*cos) + bf16(rotate_half(x)*sin)), rotate_half(x) =
 //    [-x[32:], x[:32]]; the partner chunk j^4 sits on lane^4.
-__device__ __forceinline__ void norm_rope8(float x[8], int j, bool norm, bool rope,
-                                           const uint16_t *gamma, float eps,
-                                           const uint16_t *cos_row, const uint16_t *sin_row) {
+__device__ __forceinline__ void norm_rope8_v(float x[8], int j, bool norm, bool rope, const uint4 gam,
+                                             float eps, const uint4 cos8, const uint4 sin8) {
   float ss = 0.f;
 #pragma unroll
   for (int e = 0; e < 8; ++e) ss = fmaf(x[e], x[e], ss);
@@ -215,7 +214,7 @@ __device__ __forceinline__ void norm_rope8(float x[8], int j, bool norm, bool ro
   if (norm) {
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ss * (1.0f / kDim), eps)));
     float g[8];
-    unpack8(*reinterpret_cast<const uint4 *>(gamma + j * 8), g);
+    unpack8(gam, g);
 #pragma unroll
     for (int e = 0; e < 8; ++e) x[e] = bf16_round(__fmul_rn(g[e], bf16_round(__fmul_rn(x[e], inv))));
   }
@@ -229,8 +228,8 @@ __device__ __forceinline__ void norm_rope8(float x[8], int j, bool norm, bool ro
   }
   if (rope) {
     float c[8], s[8];
-    unpack8(*reinterpret_cast<const uint4 *>(cos_row + j * 8), c);
-    unpack8(*reinterpret_cast<const uint4 *>(sin_row + j * 8), s);
+    unpack8(cos8, c);
+    unpack8(sin8, s);
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       const float rot = j < 4 ? -p[e] : p[e];
@@ -239,6 +238,16 @@ __device__ __forceinline__ void norm_rope8(float x[8], int j, bool norm, bool ro
       x[e] = bf16_round(__fadd_rn(part1, part2));
     }
   }
+}
+
+// The same with gamma (the 8 values at j * 8) and the RoPE rows read here.
+__device__ __forceinline__ void norm_rope8(float x[8], int j, bool norm, bool rope,
+                                           const uint16_t *gamma, float eps,
+                                           const uint16_t *cos_row, const uint16_t *sin_row) {
+  const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+  norm_rope8_v(x, j, norm, rope, norm ? *reinterpret_cast<const uint4 *>(gamma + j * 8) : zero, eps,
+               rope ? *reinterpret_cast<const uint4 *>(cos_row + j * 8) : zero,
+               rope ? *reinterpret_cast<const uint4 *>(sin_row + j * 8) : zero);
 }
 
 // One CTA (8 warps) per token: grid (sequence, token of the chunk).  The 32
@@ -537,9 +546,11 @@ struct CombineArgs {
 
 // Part groups for a merge of up to num_parts parts: enough threads to merge
 // hundreds of parts quickly, few for the usual handful (small CTAs launch fast).
+// At most 8 groups (512 threads): a CTA of that size still fits beside the
+// decode-step CTAs, so it can launch early as a programmatic dependent.
 int combine_groups(int num_parts) {
   int g = 1;
-  while (g < 16 && g * 8 < num_parts) g *= 2;
+  while (g < 8 && g * 4 < num_parts) g *= 2;
   return g;
 }
 
@@ -575,14 +586,25 @@ __global__ void __launch_bounds__(kCombineGroups * kDim) combine_kernel(const Co
   const float *ml = a.part_ml + b * ml_b + h * 2;
   const float *po = a.part_o + b * o_b + h * kDim + d;
   float M = -1.0e30f, L = 0.f, O = 0.f;
-#pragma unroll 4
-  for (int s = grp; s < parts; s += a.groups) {
-    const float ms = ml[s * ml_s], ls = ml[s * ml_s + 1], os = po[s * o_s];
-    const float nm = fmaxf(M, ms);
-    const float c1 = ex2(M - nm), c2 = ex2(ms - nm);
-    L = L * c1 + ls * c2;
-    O = O * c1 + os * c2;
-    M = nm;
+  // four parts per group and round: their loads are issued together
+  for (int s0 = grp; s0 < parts; s0 += 4 * a.groups) {
+    float mv[4], lv[4], ov[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int s = s0 + k * a.groups;
+      const bool in = s < parts;
+      mv[k] = in ? ml[s * ml_s] : -1.0e30f;
+      lv[k] = in ? ml[s * ml_s + 1] : 0.f;
+      ov[k] = in ? po[s * o_s] : 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float nm = fmaxf(M, mv[k]);
+      const float c1 = ex2(M - nm), c2 = ex2(mv[k] - nm);
+      L = L * c1 + lv[k] * c2;
+      O = O * c1 + ov[k] * c2;
+      M = nm;
+    }
   }
   if (d == 0) {
     sm[grp] = M;
@@ -707,8 +729,7 @@ __device__ __forceinline__ bool step_lengths(const StepArgs &a, int b, int &past
 // One work item as the producer sees it, with its loads already issued.
 struct ProducerItem {
   int valid, b, kvh, split, past, seq_len, nsplit, blk0, n;
-  int my_blk;   // block table entry blk0 + lane (lane < n)
-  int my_blk2;  // block table entry blk0 + 32 + lane (32 + lane < n)
+  int my_blk;   // block table entry blk0 + lane (lane < n); entries from 32 on are read when needed
   uint4 raw;    // this lane's 16 bytes of the item's q/k/v vectors
 };
 
@@ -747,7 +768,6 @@ __device__ __forceinline__ ProducerItem producer_load(const StepArgs &a, const S
   it.blk0 = it.split * a.blocks_per_split;
   it.n = min(a.blocks_per_split, nblk - it.blk0);
   it.my_blk = lane < it.n ? __ldg(a.block_tables + (int64_t)it.b * a.max_blocks + it.blk0 + lane) : 0;
-  it.my_blk2 = lane + 32 < it.n ? __ldg(a.block_tables + (int64_t)it.b * a.max_blocks + it.blk0 + 32 + lane) : 0;
   const int grp = lane >> 3;
   const int vec = grp < 2 ? 2 * it.kvh + grp : (grp == 2 ? kHq + it.kvh : kHq + kHkv + it.kvh);
   it.raw = __ldg(reinterpret_cast<const uint4 *>(a.qkv + it.b * a.row_stride + vec * kDim + (lane & 7) * 8));
@@ -819,12 +839,21 @@ __device__ __forceinline__ void step_producer(const StepArgs &a, StepTail *tail,
   }
   int issued = 0;
   bool ok = true;
+  const bool norm = grp < 3 && (a.mode & B2_NORM_QK);
+  // Item w = blockIdx.x is this CTA's first (no counter round trip before the
+  // first copies); the counter hands out gridDim.x, gridDim.x + 1, ... after it.
+  bool first_claim = true;
   auto next_item = [&]() {
     ProducerItem it;
     do {
       int w = 0;
-      if (lane == 0) w = atomicAdd(work_ctr, 1);
-      w = __shfl_sync(0xffffffffu, w, 0);
+      if (first_claim) {
+        w = blockIdx.x;
+        first_claim = false;
+      } else {
+        if (lane == 0) w = atomicAdd(work_ctr, 1) + static_cast<int>(gridDim.x);
+        w = __shfl_sync(0xffffffffu, w, 0);
+      }
       it = producer_load(a, tail, compact, total, w, lane);
     } while (it.valid == 0);
     return it;
@@ -834,7 +863,9 @@ __device__ __forceinline__ void step_producer(const StepArgs &a, StepTail *tail,
     const ProducerItem cur = nxt;
     // start the next item's counter update before this item's work
     int w_next = 0;
-    if (lane == 0) w_next = atomicAdd(work_ctr, 1);
+    if (lane == 0) w_next = atomicAdd(work_ctr, 1) + static_cast<int>(gridDim.x);
+    const bool stores = cur.split == cur.nsplit - 1 && (a.mode & B2_STORE_KV);
+    const int new_idx = stores ? cur.past / kBlock - cur.blk0 : -1;  // block receiving the new token
 
     float x[8];
     unpack8(cur.raw, x);
@@ -842,17 +873,18 @@ __device__ __forceinline__ void step_producer(const StepArgs &a, StepTail *tail,
     if ((a.mode & B2_ROPE_QK) && !rope_ok && lane == 0 && cur.split == 0 && cur.kvh == 0)
       atomicOr(a.err, B2_DEV_BAD_POSITION);
     const bool rope = grp < 3 && (a.mode & B2_ROPE_QK) && rope_ok;
-    norm_rope8(x, j, grp < 3 && (a.mode & B2_NORM_QK), rope, grp < 2 ? a.gamma_q : a.gamma_k, a.eps,
+    norm_rope8(x, j, norm, rope, grp < 2 ? a.gamma_q : a.gamma_k, a.eps,
                rope ? a.cos + (int64_t)cur.past * kDim : nullptr,
                rope ? a.sin + (int64_t)cur.past * kDim : nullptr);
     const uint4 packed = pack8(x);
     if (cur.split == 0 && grp < 2 && a.q_out)
       *reinterpret_cast<uint4 *>(a.q_out + ((int64_t)cur.b * kHq + 2 * cur.kvh + grp) * kDim + j * 8) = packed;
-    if (cur.split == cur.nsplit - 1 && (a.mode & B2_STORE_KV)) {
+    if (stores) {
       // The new token's row lies in this item's last block: write it, then
       // fence so the TMA (async proxy) read of that tile sees the store.
-      const int idx = cur.past / kBlock - cur.blk0;  // < n <= 64, the same in every lane
-      const int blk = __shfl_sync(0xffffffffu, idx < 32 ? cur.my_blk : cur.my_blk2, idx & 31);
+      const int idx = new_idx;  // < n <= 64, the same in every lane
+      const int blk = idx < 32 ? __shfl_sync(0xffffffffu, cur.my_blk, idx)
+                               : __ldg(a.block_tables + (int64_t)cur.b * a.max_blocks + cur.blk0 + idx);
       if (blk < 0 || blk >= a.num_blocks) {
         if (lane == 0) atomicOr(a.err, B2_DEV_BAD_BLOCK);
       } else if (grp >= 2) {
@@ -863,6 +895,7 @@ __device__ __forceinline__ void step_producer(const StepArgs &a, StepTail *tail,
       }
     }
     __syncwarp();
+    int blk_hi = 0;  // block table entry blk0 + 32 + lane, read at jj == 32
     for (int jj = 0; jj < cur.n; ++jj, ++issued) {
       const int s = issued % kStages;
       const uint32_t ph = (issued / kStages) & 1;
@@ -874,7 +907,9 @@ __device__ __forceinline__ void step_producer(const StepArgs &a, StepTail *tail,
         ok = false;
         break;
       }
-      int blk = __shfl_sync(0xffffffffu, jj < 32 ? cur.my_blk : cur.my_blk2, jj & 31);
+      if (jj == 32)
+        blk_hi = lane + 32 < cur.n ? __ldg(a.block_tables + (int64_t)cur.b * a.max_blocks + cur.blk0 + 32 + lane) : 0;
+      int blk = __shfl_sync(0xffffffffu, jj < 32 ? cur.my_blk : blk_hi, jj & 31);
       StageMeta &m = tail->meta[s];
       if (jj == 0 && grp < 2) *reinterpret_cast<uint4 *>(m.q + grp * kDim + j * 8) = packed;
       if (lane == 0) {
