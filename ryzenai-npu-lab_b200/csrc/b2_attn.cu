@@ -1317,27 +1317,39 @@ __global__ void __launch_bounds__(kStepThreads, 3)
 // the cached tokens and causally to the chunk.  Per (64-token query tile, KV
 // head, sequence) one CTA holds a 128-row query tile (64 tokens x the GQA
 // pair) and streams the sequence's 64-token K/V blocks:
-//   S[128 x 64]  = Q[128 x 64] . K_blk^T          tcgen05.mma, M=128 N=64 K=64
-//   PV[128 x 64] = P[128 x 64] . V_blk            (P bf16 in shared memory)
-// with both results in tensor memory (128 columns).  One thread per query
-// row runs the online softmax in registers from tcgen05.ld; a producer warp
-// feeds the K/V tiles with TMA (128-byte swizzle, the layout the MMA reads:
-// K-major for K, MN-major for V).
+//   S_j[128 x 64]  = Q[128 x 64] . K_j^T     tcgen05.mma, M=128 N=64 K=64, into TMEM
+//   O[128 x 64]   += P_j[128 x 64] . V_j     tcgen05.mma accumulating in TMEM
+// Warp roles: warp 4 lane 0 feeds K tiles and warp 6 lane 0 V tiles with TMA
+// (two 3-stage rings: a K stage is free again once its S product is done, so
+// K copies run two to three blocks ahead), warp 5 lane 0 issues the MMAs,
+// warps 0-3 run the online softmax (thread = query row = TMEM lane).  S is double-buffered in TMEM and P in shared memory, so
+// the tensor cores compute S_{j+1} and P_j.V_j while the softmax of the next
+// block runs.  The running maximum is re-based lazily: a row's O is rescaled
+// (TMEM load, scale, store) only when its block maximum exceeds the one in
+// use by more than kPfRebase (log2 units); between re-bases P <= 2^kPfRebase,
+// well inside bf16 and fp32 range.
 
 constexpr int kPfStages = 3;
-constexpr int kPfThreads = 5 * 32;  // 4 softmax warps (one query row per thread) + 1 TMA warp
-constexpr int kPfTmemCols = 256;    // S double buffer at columns 0 and 64, PV at column 128
+constexpr int kPfThreads = 7 * 32;  // 4 softmax warps + K TMA warp + MMA warp + V TMA warp
+constexpr int kPfTmemCols = 256;    // S buffers at columns 0 and 64, O at 128
+constexpr float kPfRebase = 8.0f;
 constexpr uint32_t kPfIdescS = (1u << 4) | (1u << 7) | (1u << 10) | (8u << 17) | (8u << 24);  // f32 <- bf16, M128 N64, K-major
 constexpr uint32_t kPfIdescPV = kPfIdescS | (1u << 16);  // B (V) MN-major
 
 struct __align__(8) PrefillTail {
-  uint64_t full[kPfStages];
-  uint64_t empty[kPfStages];
-  uint64_t sbar[2], pvbar;
+  uint64_t kfull[kPfStages];   // K tile landed (TMA)
+  uint64_t kempty[kPfStages];  // K stage read by its S product (commit)
+  uint64_t vfull[kPfStages];   // V tile landed (TMA)
+  uint64_t vempty[kPfStages];  // V stage read by its P.V product (commit)
+  uint64_t sbar[2];           // S_j computed (commit)
+  uint64_t sfree[2];          // S_j read by all 128 softmax threads
+  uint64_t pready[2];         // P_j written (and O re-based) by all 128 softmax threads
+  uint64_t pfree[2];          // P buffer read by its P.V MMA (commit)
+  uint64_t pvbar;             // P_j.V_j accumulated (commit, once per block)
   uint32_t tmem_base;
   int abort;
 };
-constexpr int kPfSmem = 1024 + 2 * 16384 + kPfStages * kStageBytes + (int)sizeof(PrefillTail);
+constexpr int kPfSmem = 1024 + 3 * 16384 + kPfStages * kStageBytes + (int)sizeof(PrefillTail);
 
 struct PrefillArgs {
   const uint16_t *q;  // [batch][tokens][16][64] normalised + rotated
@@ -1386,6 +1398,21 @@ __device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t r[16])
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// 16 consecutive fp32 columns into this thread's TMEM lane.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float v[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+      "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])),
+      "r"(__float_as_uint(v[11])), "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])),
+      "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15]))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 // 64 consecutive fp32 columns of this thread's TMEM lane (4 loads, one wait).
 __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float v[64]) {
   uint32_t r[64];
@@ -1394,20 +1421,6 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float v[64]) {
   tmem_wait_ld();
 #pragma unroll
   for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-// 16 consecutive fp32 columns of this thread's TMEM lane.
-// Barrier of the 4 softmax warps that also ORs a flag across them, so that a
-// decision taken after it is the same in every thread.
-__device__ __forceinline__ int pf_bar_or(int flag) {
-  int out;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\tsetp.ne.b32 p, %1, 0;\n\t"
-      "bar.red.or.pred q, 1, 128, p;\n\tselp.b32 %0, 1, 0, q;\n\t}"
-      : "=r"(out)
-      : "r"(flag)
-      : "memory");
-  return out;
 }
 
 __global__ void __launch_bounds__(kPfThreads, 2)
@@ -1429,20 +1442,28 @@ __global__ void __launch_bounds__(kPfThreads, 2)
   extern __shared__ uint8_t smem_raw[];
   uint8_t *sQ = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint8_t *sP = sQ + 16384;
-  uint8_t *ring = sP + 16384;
-  PrefillTail *tail = reinterpret_cast<PrefillTail *>(ring + kPfStages * kStageBytes);
+  uint8_t *sP = sQ + 16384;  // two P buffers of 16 KiB
+  uint8_t *kring = sP + 2 * 16384;             // kPfStages K tiles of 8 KiB
+  uint8_t *vring = kring + kPfStages * kTileBytes;  // kPfStages V tiles of 8 KiB
+  PrefillTail *tail = reinterpret_cast<PrefillTail *>(vring + kPfStages * kTileBytes);
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
 
   if (tid == 0) {
 #pragma unroll
     for (int s = 0; s < kPfStages; ++s) {
-      mbar_init(smem_u32(&tail->full[s]), 1);
-      mbar_init(smem_u32(&tail->empty[s]), 1);
+      mbar_init(smem_u32(&tail->kfull[s]), 1);
+      mbar_init(smem_u32(&tail->kempty[s]), 1);
+      mbar_init(smem_u32(&tail->vfull[s]), 1);
+      mbar_init(smem_u32(&tail->vempty[s]), 1);
     }
-    mbar_init(smem_u32(&tail->sbar[0]), 1);
-    mbar_init(smem_u32(&tail->sbar[1]), 1);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_u32(&tail->sbar[i]), 1);
+      mbar_init(smem_u32(&tail->sfree[i]), 128);
+      mbar_init(smem_u32(&tail->pready[i]), 128);
+      mbar_init(smem_u32(&tail->pfree[i]), 1);
+    }
     mbar_init(smem_u32(&tail->pvbar), 1);
     tail->abort = 0;
     mbar_fence_init();
@@ -1469,90 +1490,116 @@ __global__ void __launch_bounds__(kPfThreads, 2)
   tmem_fence_after();
   const uint32_t tmem = tail->tmem_base;
 
-  if (warp == 4) {
-    // ---------------- TMA producer
+  if (warp == 4 || warp == 6) {
+    // ---------------- TMA producers: warp 4 the K tiles, warp 6 the V tiles
     if (lane == 0) {
+      const bool is_k = warp == 4;
+      const CUtensorMap *map = is_k ? &tm_k : &tm_v;
+      uint64_t *fullb = is_k ? tail->kfull : tail->vfull;
+      uint64_t *emptyb = is_k ? tail->kempty : tail->vempty;
+      uint8_t *ringb = is_k ? kring : vring;
       const uint64_t policy = evict_first_policy();
       const int32_t *tbl = a.block_tables + (int64_t)b * a.max_blocks;
       int issued = 0;
       for (int j = 0; j < nblk; ++j) {
         const int s = j % kPfStages;
         const uint32_t ph = (j / kPfStages) & 1;
-        if (j >= kPfStages && !mbar_wait(smem_u32(&tail->empty[s]), ph ^ 1)) {
+        if (j >= kPfStages && !mbar_wait(smem_u32(&emptyb[s]), ph ^ 1)) {
           atomicOr(a.err, B2_DEV_TIMEOUT);
           tail->abort = 1;
           break;
         }
+        if (tail->abort) break;
         int blk = tbl[j];
         if (blk < 0 || blk >= a.num_blocks) {
-          atomicOr(a.err, B2_DEV_BAD_BLOCK);
+          if (is_k) atomicOr(a.err, B2_DEV_BAD_BLOCK);
           blk = 0;
         }
         const int row = (blk * kHkv + kvh) * kBlock;
-        uint8_t *dst = ring + s * kStageBytes;
-        const uint32_t full = smem_u32(&tail->full[s]);
-        mbar_expect_tx(full, kStageBytes);
-        tma_load_2d(smem_u32(dst), &tm_k, 0, row, full, policy);
-        tma_load_2d(smem_u32(dst + kTileBytes), &tm_v, 0, row, full, policy);
+        const uint32_t full = smem_u32(&fullb[s]);
+        mbar_expect_tx(full, kTileBytes);
+        tma_load_2d(smem_u32(ringb + s * kTileBytes), map, 0, row, full, policy);
         issued = j + 1;
       }
       // wait (bounded) until every issued copy has landed before leaving
       for (int s = 0; s < kPfStages && s < issued; ++s) {
         const int last = s + kPfStages * ((issued - 1 - s) / kPfStages);
-        if (!mbar_wait(smem_u32(&tail->full[s]), (last / kPfStages) & 1)) atomicOr(a.err, B2_DEV_TIMEOUT);
+        if (!mbar_wait(smem_u32(&fullb[s]), (last / kPfStages) & 1)) atomicOr(a.err, B2_DEV_TIMEOUT);
       }
     }
-  } else {
-    // ---------------- softmax / epilogue warps: thread = query row
-    // Software-pipelined over the K/V blocks: S_{j+1} = Q.K_{j+1}^T runs on
-    // the tensor cores (second S buffer) while the softmax of block j runs,
-    // and P_j.V_j runs while the next iteration loads S_{j+1}; the output
-    // O = sum_j alpha-rescaled P_j.V_j is accumulated in registers one
-    // iteration behind.
-    const int hl = tid >> 6, t = tid & 63;
-    const bool row_ok = t < rows_t;
-    const int qpos = past + t0 + t;
-    const uint32_t trow = tmem + ((uint32_t)(32 * warp) << 16);
-    float O[64];
-#pragma unroll
-    for (int i = 0; i < 64; ++i) O[i] = 0.f;
-    float m = -1.0e30f, l = 0.f, alpha_prev = 1.f;
-
-    auto issue_s = [&](int j) {  // thread 0 only: S_j into buffer j % 2
-      const int s = j % kPfStages;
-      if (!tail->abort && mbar_wait(smem_u32(&tail->full[s]), (j / kPfStages) & 1)) {
+  } else if (warp == 5) {
+    // ---------------- MMA issuer: S_0, S_1, then per block P_j.V_j and S_{j+2}
+    if (lane == 0) {
+      auto issue_s = [&](int j) -> bool {
+        const int s = j % kPfStages;
+        if (!mbar_wait(smem_u32(&tail->kfull[s]), (j / kPfStages) & 1)) return false;
+        if (j >= 2 && !mbar_wait(smem_u32(&tail->sfree[j & 1]), ((j >> 1) - 1) & 1)) return false;
         tmem_fence_after();
-        const uint32_t kt = smem_u32(ring + s * kStageBytes);
+        const uint32_t kt = smem_u32(kring + s * kTileBytes);
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks)
           umma_f16(tmem + 64 * (j & 1), umma_desc(smem_u32(sQ) + 32 * ks, 16), umma_desc(kt + 32 * ks, 16),
                    kPfIdescS, ks > 0);
         umma_commit(smem_u32(&tail->sbar[j & 1]));
-      } else {
+        umma_commit(smem_u32(&tail->kempty[s]));
+        return true;
+      };
+      bool ok = issue_s(0) && (nblk < 2 || issue_s(1));
+      int done = 0;  // P.V products issued
+      for (int j = 0; ok && j < nblk; ++j) {
+        const int s = j % kPfStages;
+        if (!mbar_wait(smem_u32(&tail->pready[j & 1]), (j >> 1) & 1) || tail->abort ||
+            !mbar_wait(smem_u32(&tail->vfull[s]), (j / kPfStages) & 1)) {
+          ok = false;
+          break;
+        }
+        tmem_fence_after();
+        const uint32_t vt = smem_u32(vring + s * kTileBytes);
+        const uint32_t pb = smem_u32(sP + (j & 1) * 16384);
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          umma_f16(tmem + 128, umma_desc(pb + 32 * ks, 16), umma_desc(vt + 2048 * ks, 0), kPfIdescPV,
+                   (j > 0 || ks > 0) ? 1u : 0u);
+        umma_commit(smem_u32(&tail->pvbar));
+        umma_commit(smem_u32(&tail->pfree[j & 1]));
+        umma_commit(smem_u32(&tail->vempty[s]));
+        done = j + 1;
+        if (j + 2 < nblk) ok = issue_s(j + 2);
+      }
+      if (!ok) {
         if (!tail->abort) atomicOr(a.err, B2_DEV_TIMEOUT);
         tail->abort = 1;
-        mbar_arrive(smem_u32(&tail->sbar[j & 1]));  // let the other rows through
       }
+      // the MMAs issued must finish before the CTA leaves (bounded)
+      if (done > 0) mbar_wait(smem_u32(&tail->pvbar), (done - 1) & 1);
+    }
+  } else {
+    // ---------------- softmax warps: thread = query row = TMEM lane
+    const int hl = tid >> 6, t = tid & 63;
+    const bool row_ok = t < rows_t;
+    const int qpos = past + t0 + t;
+    const uint32_t trow = tmem + ((uint32_t)(32 * warp) << 16);
+    float m = -1.0e30f, l = 0.f;  // max in use (log2 units) and running sum
+    bool ok = true;
+    // Waits decided for the whole warp (the TMEM loads and stores below are
+    // warp-collective): false if any lane timed out or the CTA is aborting.
+    auto warp_wait = [&](uint32_t bar, uint32_t parity) -> bool {
+      const bool got = mbar_wait(bar, parity);
+      return !__any_sync(0xffffffffu, !got || tail->abort);
     };
-    auto accumulate_pv = [&](int j) {  // all rows: O = O * alpha_prev + P_j.V_j
-      mbar_wait(smem_u32(&tail->pvbar), j & 1);
-      tmem_fence_after();
-      float pv[64];
-      tmem_ld64(trow + 128, pv);
-#pragma unroll
-      for (int e = 0; e < 64; ++e) O[e] = fmaf(O[e], alpha_prev, pv[e]);
-    };
-
-    if (tid == 0) issue_s(0);
     for (int j = 0; j < nblk; ++j) {
       const int s = j % kPfStages;
-      mbar_wait(smem_u32(&tail->sbar[j & 1]), (j >> 1) & 1);
+      if (!warp_wait(smem_u32(&tail->sbar[j & 1]), (j >> 1) & 1)) {
+        ok = false;
+        break;
+      }
       tmem_fence_after();
       float sc[64];
       tmem_ld64(trow + 64 * (j & 1), sc);
-      if (tid == 0 && j + 1 < nblk) issue_s(j + 1);
+      tmem_fence_before();
+      mbar_arrive(smem_u32(&tail->sfree[j & 1]));  // S_j is in registers: its buffer may be reused
       // scores of this row, masked: causal within the chunk, nothing past the
-      // tile; max and sum in 8 independent chains (shorter dependency chains)
+      // tile; max in 8 independent chains
       const int key0 = j * kBlock;
       const int lim = row_ok ? qpos - key0 : -1;  // columns c <= lim are visible
       float bm8[8];
@@ -1565,8 +1612,30 @@ __global__ void __launch_bounds__(kPfThreads, 2)
       }
       const float bm = fmaxf(fmaxf(fmaxf(bm8[0], bm8[1]), fmaxf(bm8[2], bm8[3])),
                              fmaxf(fmaxf(bm8[4], bm8[5]), fmaxf(bm8[6], bm8[7])));
-      const float mn = fmaxf(m, bm);
-      const float alpha = ex2(m - mn);
+      // re-base when this block's maximum is well above the one in use
+      const bool rebase = bm > m + kPfRebase;
+      const float mn = rebase ? bm : m;
+      const float alpha = ex2(m - mn);  // 1 when not re-based
+      if (__any_sync(0xffffffffu, rebase && j > 0)) {
+        // O holds P_0..P_{j-1} . V: wait for the last product, then scale
+        // this warp's rows in TMEM (alpha = 1 for rows not re-based)
+        if (!warp_wait(smem_u32(&tail->pvbar), (j - 1) & 1)) {
+          ok = false;
+          break;
+        }
+        tmem_fence_after();
+#pragma unroll
+        for (int c = 0; c < 64; c += 16) {
+          uint32_t r[16];
+          tmem_ld16_nowait(trow + 128 + c, r);
+          tmem_wait_ld();
+          float o16[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) o16[e] = __uint_as_float(r[e]) * alpha;
+          tmem_st16(trow + 128 + c, o16);
+        }
+        tmem_wait_st();
+      }
       m = mn;
       float ps8[8];
 #pragma unroll
@@ -1578,56 +1647,55 @@ __global__ void __launch_bounds__(kPfThreads, 2)
       }
       const float ps = ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
       l = fmaf(l, alpha, ps);
-      if (j > 0) accumulate_pv(j - 1);  // P_{j-1} is no longer needed after this
-      alpha_prev = alpha;
+      // P_j into buffer j % 2 once the product that read it (P_{j-2}) is done
+      if (j >= 2 && !warp_wait(smem_u32(&tail->pfree[j & 1]), ((j >> 1) - 1) & 1)) {
+        ok = false;
+        break;
+      }
+      uint8_t *pbuf = sP + (j & 1) * 16384;
 #pragma unroll
       for (int c = 0; c < 64; c += 8)
-        *reinterpret_cast<uint4 *>(sP + tid * 128 + (((c >> 3) ^ (tid & 7)) << 4)) = pack8(sc + c);
+        *reinterpret_cast<uint4 *>(pbuf + tid * 128 + (((c >> 3) ^ (tid & 7)) << 4)) = pack8(sc + c);
       if (key0 + kBlock - 1 > last_key) {
         // rows of the last block past every query of the tile may hold stale
         // (even NaN) data: zero them so that P = 0 cannot meet them in P.V
         // (after the stage's copy has landed, so the copy cannot overwrite)
-        mbar_wait(smem_u32(&tail->full[s]), (j / kPfStages) & 1);
+        if (!warp_wait(smem_u32(&tail->vfull[s]), (j / kPfStages) & 1)) {
+          ok = false;
+          break;
+        }
         const int first_bad = last_key - key0 + 1;
-        uint8_t *v_gen = ring + s * kStageBytes + kTileBytes;
+        uint8_t *v_gen = vring + s * kTileBytes;
         for (int i = tid; i < (kBlock - first_bad) * 8; i += 128)
           *reinterpret_cast<uint4 *>(v_gen + (first_bad + (i >> 3)) * 128 + ((i & 7) << 4)) = make_uint4(0, 0, 0, 0);
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       tmem_fence_before();
-      const int stop = pf_bar_or(tail->abort);
-      if (tid == 0) {
-        tmem_fence_after();
-        if (!stop) {
-          const uint32_t vt = smem_u32(ring + s * kStageBytes) + kTileBytes;
+      mbar_arrive(smem_u32(&tail->pready[j & 1]));
+    }
+    if (!ok) {
+      if (!tail->abort) atomicOr(a.err, B2_DEV_TIMEOUT);
+      tail->abort = 1;
+    } else if (warp_wait(smem_u32(&tail->pvbar), (nblk - 1) & 1)) {
+      // O = sum_j P_j . V_j, every product done
+      tmem_fence_after();
+      float o[64];
+      tmem_ld64(trow + 128, o);
+      if (row_ok && !tail->abort) {
+        const float inv = 1.0f / l;
+        uint4 *dst =
+            reinterpret_cast<uint4 *>(a.out + (((int64_t)b * a.tokens + t0 + t) * kHq + 2 * kvh + hl) * kDim);
 #pragma unroll
-          for (int ks = 0; ks < 4; ++ks)
-            umma_f16(tmem + 128, umma_desc(smem_u32(sP) + 32 * ks, 16), umma_desc(vt + 2048 * ks, 0), kPfIdescPV,
-                     ks > 0);
-          umma_commit(smem_u32(&tail->pvbar));
-          umma_commit(smem_u32(&tail->empty[s]));
-        } else {
-          mbar_arrive(smem_u32(&tail->pvbar));
+        for (int c = 0; c < 64; c += 8) {
+          float o8[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) o8[e] = o[c + e] * inv;
+          dst[c >> 3] = pack8(o8);
         }
       }
-      if (stop) {
-        // an S MMA issued for block j + 1 must finish before the CTA leaves
-        if (j + 1 < nblk) mbar_wait(smem_u32(&tail->sbar[(j + 1) & 1]), ((j + 1) >> 1) & 1);
-        mbar_wait(smem_u32(&tail->pvbar), j & 1);
-        break;
-      }
-    }
-    if (!tail->abort) accumulate_pv(nblk - 1);
-    if (row_ok && !tail->abort) {
-      const float inv = 1.0f / l;
-      uint4 *dst = reinterpret_cast<uint4 *>(a.out + (((int64_t)b * a.tokens + t0 + t) * kHq + 2 * kvh + hl) * kDim);
-#pragma unroll
-      for (int c = 0; c < 64; c += 8) {
-        float o8[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) o8[e] = O[c + e] * inv;
-        dst[c >> 3] = pack8(o8);
-      }
+    } else {
+      atomicOr(a.err, B2_DEV_TIMEOUT);
+      tail->abort = 1;
     }
   }
   tmem_fence_before();
