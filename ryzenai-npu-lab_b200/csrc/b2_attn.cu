@@ -86,12 +86,19 @@ __device__ __forceinline__ float bf16_round(float x) {
   return __uint_as_float(bf16_bits(x) << 16);
 }
 
+// two fp32 -> one bf16x2 word (lo in the low half), round-to-nearest-even,
+// in one paired conversion instruction
+__device__ __forceinline__ uint32_t pack_bf16x2_rn(float lo, float hi) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t *>(&h);
+}
+
 __device__ __forceinline__ uint4 pack8(const float f[8]) {
   uint4 w;
-  w.x = bf16_bits(f[0]) | (bf16_bits(f[1]) << 16);
-  w.y = bf16_bits(f[2]) | (bf16_bits(f[3]) << 16);
-  w.z = bf16_bits(f[4]) | (bf16_bits(f[5]) << 16);
-  w.w = bf16_bits(f[6]) | (bf16_bits(f[7]) << 16);
+  w.x = pack_bf16x2_rn(f[0], f[1]);
+  w.y = pack_bf16x2_rn(f[2], f[3]);
+  w.z = pack_bf16x2_rn(f[4], f[5]);
+  w.w = pack_bf16x2_rn(f[6], f[7]);
   return w;
 }
 
@@ -985,7 +992,7 @@ __device__ __forceinline__ void mma_bf16(float c[4], uint32_t a0, uint32_t a1, u
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) { return bf16_bits(lo) | (bf16_bits(hi) << 16); }
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) { return pack_bf16x2_rn(lo, hi); }
 
 // Zero the bf16 halves of a fragment register whose token index is >= valid.
 __device__ __forceinline__ uint32_t mask_pair(uint32_t v, int tok, int valid) {
@@ -1383,6 +1390,27 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
 
+// Packed fp32 pairs (sm_100 f32x2 arithmetic): one instruction for two lanes'
+// worth of FMA / add, halving the softmax's FMA-pipe instructions.
+__device__ __forceinline__ void ffma2(float &d0, float &d1, float a0, float a1, float b0, float b1, float c0,
+                                      float c1) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+
+__device__ __forceinline__ void fadd2(float &d0, float &d1, float a0, float a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
 __device__ __forceinline__ void tmem_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tmem_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -1605,13 +1633,17 @@ __global__ void __launch_bounds__(kPfThreads, 2)
       float bm8[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) bm8[e] = -INFINITY;
+      // raw scores (the scale is folded into the exponent); the mask only
+      // where a row of this warp needs it (the tile's diagonal block, rows
+      // past the chunk)
+      if (__any_sync(0xffffffffu, lim < kBlock - 1)) {
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        sc[c] = c <= lim ? sc[c] * a.scale_log2 : -INFINITY;
-        bm8[c & 7] = fmaxf(bm8[c & 7], sc[c]);
+        for (int c = 0; c < 64; ++c) sc[c] = c <= lim ? sc[c] : -INFINITY;
       }
+#pragma unroll
+      for (int c = 0; c < 64; ++c) bm8[c & 7] = fmaxf(bm8[c & 7], sc[c]);
       const float bm = fmaxf(fmaxf(fmaxf(bm8[0], bm8[1]), fmaxf(bm8[2], bm8[3])),
-                             fmaxf(fmaxf(bm8[4], bm8[5]), fmaxf(bm8[6], bm8[7])));
+                             fmaxf(fmaxf(bm8[4], bm8[5]), fmaxf(bm8[6], bm8[7]))) * a.scale_log2;
       // re-base when this block's maximum is well above the one in use
       const bool rebase = bm > m + kPfRebase;
       const float mn = rebase ? bm : m;
@@ -1641,9 +1673,13 @@ __global__ void __launch_bounds__(kPfThreads, 2)
 #pragma unroll
       for (int e = 0; e < 8; ++e) ps8[e] = 0.f;
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        sc[c] = ex2(sc[c] - mn);
-        ps8[c & 7] += sc[c];
+      for (int c = 0; c < 64; c += 2) {
+        float x0, x1;
+        ffma2(x0, x1, sc[c], sc[c + 1], a.scale_log2, a.scale_log2, -mn, -mn);
+        sc[c] = ex2(x0);
+        sc[c + 1] = ex2(x1);
+        const int e = c & 7;
+        fadd2(ps8[e], ps8[e + 1], ps8[e], ps8[e + 1], sc[c], sc[c + 1]);
       }
       const float ps = ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
       l = fmaf(l, alpha, ps);

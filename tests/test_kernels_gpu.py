@@ -128,7 +128,9 @@ def test_append_with_norm_matches_oracle(cuda):
     assert torch.equal(v_got.cpu(), v)
     for got, ref, name in [(q_out, q_ref, "q"), (k_got, k_ref, "k")]:
         d = ulp_diff(got, ref)
-        assert d.max() <= 1, f"{name}: {d.max()} ulps"
+        # one ulp, or (where RoPE cancels to ~0) one ulp of the RoPE terms
+        diff = (got.float().cpu() - ref.float()).abs().numpy()
+        assert ((d <= 1) | (diff <= 2.0 ** -7)).all(), f"{name}: {d.max()} ulps, {diff.max()} abs"
         assert (d == 0).mean() >= 0.99, f"{name}: exact fraction {(d == 0).mean():.4f}"
 
 

@@ -32,6 +32,18 @@ def _run_prefill(cuda, cache, qkv, past, chunk, gq, gk):
     return out
 
 
+def assert_k_close(kd: torch.Tensor, k_ref: torch.Tensor) -> None:
+    """Appended k (RMSNorm + RoPE) against the oracle: within one bf16 ulp,
+    except where RoPE cancels (x.cos + rot(x).sin ~ 0, where the result can be
+    exactly 0 on one side and a few 1e-3 on the other after a one-ulp
+    difference of the normalised input); there the absolute difference is
+    bounded by one ulp of the RoPE terms (2^-7 for terms below 2)."""
+    ulp = ulp_diff(kd, k_ref)
+    diff = (kd.float().cpu() - k_ref.float()).abs().numpy()
+    assert (ulp <= 1).mean() >= 0.999, f"{(ulp > 1).sum()} elements beyond one ulp"
+    assert ((ulp <= 1) | (diff <= 2.0 ** -7)).all(), f"max abs difference {diff.max()}"
+
+
 @pytest.mark.parametrize("path", sorted(GOLDEN.glob("lfm2_prefill_*.npz")), ids=lambda p: p.stem)
 def test_prefill_matches_hf_golden(cuda, path):
     f = dict(np.load(path))
@@ -47,7 +59,7 @@ def test_prefill_matches_hf_golden(cuda, path):
     _, k_all, v_all = orc.prefill_step(qkv[0], k[0], v[0], past, w["q_gamma"], w["k_gamma"])
     kd, vd = cache.read_dense(0, 0, past + t)
     assert torch.equal(vd.cpu(), v_all)
-    assert ulp_diff(kd, k_all).max() <= 1
+    assert_k_close(kd, k_all)
 
 
 def test_prefill_ragged_batch(cuda):
