@@ -1340,6 +1340,9 @@ constexpr int kPfStages = 3;
 constexpr int kPfThreads = 7 * 32;  // 4 softmax warps + K TMA warp + MMA warp + V TMA warp
 constexpr int kPfTmemCols = 256;    // S buffers at columns 0 and 64, O at 128
 constexpr float kPfRebase = 8.0f;
+// Up to this many sequences, CTAs take the sequences longest first (blocks
+// launch in blockIdx order, so the longest runs start in the first wave).
+constexpr int kPfSortMax = 128;
 constexpr uint32_t kPfIdescS = (1u << 4) | (1u << 7) | (1u << 10) | (8u << 17) | (8u << 24);  // f32 <- bf16, M128 N64, K-major
 constexpr uint32_t kPfIdescPV = kPfIdescS | (1u << 16);  // B (V) MN-major
 
@@ -1454,7 +1457,25 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float v[64]) {
 __global__ void __launch_bounds__(kPfThreads, 2)
     prefill_attn_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                         const PrefillArgs a) {
-  const int tile = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int tile = blockIdx.x, kvh = blockIdx.y;
+  int b = blockIdx.z;
+  if (gridDim.z <= kPfSortMax) {
+    // sequence of rank blockIdx.z by total keys (past + chunk), descending
+    __shared__ int keys[kPfSortMax];
+    __shared__ int chosen;
+    const int nb = gridDim.z;
+    for (int i = threadIdx.x; i < nb; i += blockDim.x)
+      keys[i] = a.past_lens[i] + (a.chunk_lens ? a.chunk_lens[i] : a.tokens);
+    __syncthreads();
+    for (int i = threadIdx.x; i < nb; i += blockDim.x) {
+      const int ki = keys[i];
+      int rank = 0;
+      for (int j2 = 0; j2 < nb; ++j2) rank += (keys[j2] > ki) || (keys[j2] == ki && j2 < i);
+      if (rank == (int)blockIdx.z) chosen = i;
+    }
+    __syncthreads();
+    b = chosen;
+  }
   const int past = a.past_lens[b];
   const int T = a.chunk_lens ? a.chunk_lens[b] : a.tokens;
   const int t0 = tile * 64;
