@@ -103,3 +103,56 @@ def test_long_context_state_exchange_gloo(total):
             assert p.exitcode == 0
         for r in range(world):
             assert torch.allclose(result[r], full, atol=1e-5, rtol=1e-5)
+
+
+def _exchange_choice_worker(rank, world, port, result):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        dist_mod = load_pkg("distributed")
+        g = torch.ones(64, dtype=torch.bfloat16)
+        lc = dist_mod.LongContextDecode(1000, g, g, device="cpu", growth=64)
+        out = [lc.exchange, lc.start, lc.end, lc.is_tail]
+        for bad in ("p2p", "bogus"):
+            try:
+                dist_mod.LongContextDecode(1000, g, g, device="cpu", growth=64, exchange=bad)
+                out.append("accepted")
+            except ValueError:
+                out.append("ValueError")
+        result[rank] = out
+    finally:
+        dist.destroy_process_group()
+
+
+def test_long_context_exchange_choice_gloo():
+    """On CPU ranks (gloo) the exchange falls back to the collective; asking
+    for the P2P kernel, or an unknown exchange, is a ValueError."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as mgr:
+        result = mgr.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_exchange_choice_worker, args=(r, world, port, result)) for r in range(world)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(120)
+            assert p.exitcode == 0
+        assert result[0] == ["collective", 0, 512, False, "ValueError", "ValueError"]
+        assert result[1] == ["collective", 512, 1000, True, "ValueError", "ValueError"]
+
+
+def test_split_size_heuristic():
+    attn = load_pkg("attention")
+    # one long sequence: ~2 equal items per SM in one wave (8 KV heads x splits <= 296)
+    for blocks in (2049, 1026, 514, 258):
+        bps = attn.choose_blocks_per_split(1, blocks, fused=True)
+        splits = -(-blocks // bps)
+        assert 1 <= bps <= 64 and splits * 8 <= 2 * 148
+    assert attn.choose_blocks_per_split(1, 4097, fused=True) == 64      # capped: several equal waves
+    # many sequences: ~6 items per resident CTA, 4..32 blocks
+    assert attn.choose_blocks_per_split(64, 3715, fused=True) == 12
+    assert 4 <= attn.choose_blocks_per_split(512, 512 * 60, fused=True) <= 32
+    # three-kernel path: ~8 CTAs of work per SM
+    assert 2 <= attn.choose_blocks_per_split(64, 3715) <= 64
