@@ -72,6 +72,8 @@ def parse():
                         "c5: end-to-end greedy decode of the whole random-init model; "
                         "prefill: a chunk of --chunk new tokens per C3 sequence on the tcgen05 kernel")
     p.add_argument("--context", type=int, default=131072, help="c4: cached tokens of the sequence")
+    p.add_argument("--torch-glue", action="store_true",
+                   help="c5: run the layer glue (norms, SwiGLU, short conv) as torch ops")
     p.add_argument("--exchange", choices=["auto", "p2p", "collective"], default="auto",
                    help="c4: how the ranks' partial states are merged")
     return p.parse_args()
@@ -658,7 +660,8 @@ def run_c5(args):
     from oracle import lfm2_attention as orc   # seeded weight generator (set-up only)
     batch, prompt_len, new = 256, 32, 256
     sd = orc.lfm2_model_weights(args.seed)
-    runner = runner_mod.LFM2DecodeRunner(sd, max_batch=batch, max_context=prompt_len + new + 1, device=dev)
+    runner = runner_mod.LFM2DecodeRunner(sd, max_batch=batch, max_context=prompt_len + new + 1, device=dev,
+                                         fused_glue=not args.torch_glue)
     del sd
     g = torch.Generator().manual_seed(args.seed * 1000 + rank)
     prompts = torch.randint(0, 65536, (batch, prompt_len), generator=g)
@@ -681,6 +684,7 @@ def run_c5(args):
         "data": "synthetic",
         "config": {"workload": "C5 end-to-end greedy decode, LFM2.5-230M-shaped random-init model, "
                                "256 prompts x 32 ids, 256 new tokens, paged KV, CUDA graph per token",
+                   "layer_glue": "torch ops" if args.torch_glue else "libb2attn kernels",
                    "global_batch": batch * world, "prompt": prompt_len, "new_tokens": new,
                    "parallelism": f"replicas x{world}"},
         "generated_shape": list(out.shape), "clocks": clocks.summary(),

@@ -1,4 +1,5 @@
-"""ctypes binding of libb2attn.so (the C ABI in include/b2_decode_attn.h).
+"""ctypes binding of libb2attn.so (the C ABI in include/b2_decode_attn.h and
+include/b2_block.h).
 
 This module loads the in-tree shared library and nothing else: there is no
 fallback.  If the library is missing or fails to load, every entry point
@@ -108,6 +109,10 @@ SIGNATURES = {
         _p, _i32, _i32,      # areas (host array of world pointers), world, rank
         _p, _p, _p,          # out, dev_err, stream
     ]),
+    # include/b2_block.h
+    "b2_add_rmsnorm": (ctypes.c_int, [_p, _p, _p, _f32, _p, _p, _i32, _i32, _p]),
+    "b2_swiglu": (ctypes.c_int, [_p, _p, _i32, _i32, _p]),
+    "b2_shortconv_step": (ctypes.c_int, [_p, _p, _p, _p, _i32, _i32, _p]),
     "b2_merge_states": (ctypes.c_int, [
         _p, _i32, _i32,      # states, num_parts, batch
         _p, _p, _p, _p,      # out, state_ml, state_o, stream

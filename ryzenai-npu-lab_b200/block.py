@@ -1,0 +1,66 @@
+"""Torch-facing wrappers of the layer kernels around the attention path
+(include/b2_block.h): residual add + RMSNorm, SwiGLU gate, short-convolution
+decode step.  Same conventions as attention.py: host checks raise ValueError,
+library refusals raise B2Error, work is queued on the current CUDA stream."""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from .attention import _need, _ptr, _stream
+
+
+def add_rmsnorm(x: torch.Tensor, residual: torch.Tensor | None, gamma: torch.Tensor, eps: float, *,
+                out: torch.Tensor, sum_out: torch.Tensor | None = None,
+                stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """out = gamma * bf16(s * rsqrt(mean(s^2) + eps)) with s = bf16(x + residual)
+    (s = x without a residual); s is also written to sum_out (which may be
+    the residual or x itself).  x, residual, out, sum_out: bf16 [rows, width]."""
+    dev = x.device
+    if x.dim() != 2:
+        raise ValueError("x must be [rows, width]")
+    rows, width = x.shape
+    _need(x, "x", torch.bfloat16, dev)
+    if residual is not None:
+        _need(residual, "residual", torch.bfloat16, dev, (rows, width))
+    if sum_out is not None:
+        _need(sum_out, "sum_out", torch.bfloat16, dev, (rows, width))
+    _need(gamma, "gamma", torch.bfloat16, dev, (width,))
+    _need(out, "out", torch.bfloat16, dev, (rows, width))
+    rc = _lib.load().b2_add_rmsnorm(_ptr(x), _ptr(residual), _ptr(gamma), ctypes.c_float(eps), _ptr(sum_out),
+                                    _ptr(out), rows, width, _stream(dev, stream))
+    _lib.check(rc, "b2_add_rmsnorm")
+    return out
+
+
+def swiglu(gu: torch.Tensor, *, out: torch.Tensor, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """out = bf16(bf16(silu(g)) * u) for gu = [g | u] (bf16 [rows, 2 * ffn]) -> bf16 [rows, ffn]."""
+    dev = gu.device
+    if gu.dim() != 2 or gu.shape[1] % 2:
+        raise ValueError("gu must be [rows, 2 * ffn]")
+    rows, ffn = gu.shape[0], gu.shape[1] // 2
+    _need(gu, "gu", torch.bfloat16, dev)
+    _need(out, "out", torch.bfloat16, dev, (rows, ffn))
+    _lib.check(_lib.load().b2_swiglu(_ptr(gu), _ptr(out), rows, ffn, _stream(dev, stream)), "b2_swiglu")
+    return out
+
+
+def shortconv_step(bcx: torch.Tensor, conv_state: torch.Tensor, conv_w: torch.Tensor, *, out: torch.Tensor,
+                   stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """One decode step of the gated short convolution: bcx = [B | C | x]
+    (bf16 [rows, 3 * hidden]), conv_state bf16 [rows, hidden, 3] (rolled in
+    place), conv_w bf16 [hidden, 3] -> out bf16 [rows, hidden]."""
+    dev = bcx.device
+    if bcx.dim() != 2 or bcx.shape[1] % 3:
+        raise ValueError("bcx must be [rows, 3 * hidden]")
+    rows, hidden = bcx.shape[0], bcx.shape[1] // 3
+    _need(bcx, "bcx", torch.bfloat16, dev)
+    _need(conv_state, "conv_state", torch.bfloat16, dev, (rows, hidden, 3))
+    _need(conv_w, "conv_w", torch.bfloat16, dev, (hidden, 3))
+    _need(out, "out", torch.bfloat16, dev, (rows, hidden))
+    rc = _lib.load().b2_shortconv_step(_ptr(bcx), _ptr(conv_state), _ptr(conv_w), _ptr(out), rows, hidden,
+                                       _stream(dev, stream))
+    _lib.check(rc, "b2_shortconv_step")
+    return out

@@ -1,7 +1,7 @@
 """Build libb2attn.so in-tree with nvcc for sm_100a.
 
 The shared library is the product's compute path: it holds every CUDA kernel
-and the C ABI declared in include/b2_decode_attn.h.  It is built next to this
+and the C ABI declared in include/b2_decode_attn.h and include/b2_block.h.  It is built next to this
 file so that it travels with the source tree to the GPU host.
 """
 from __future__ import annotations
@@ -15,8 +15,8 @@ PKG = pathlib.Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libb2attn.so"
-SOURCES = [CSRC / "b2_attn.cu"]
-HEADERS = [ROOT / "include" / "b2_decode_attn.h"]
+SOURCES = [CSRC / "b2_attn.cu", CSRC / "b2_block.cu"]
+HEADERS = [ROOT / "include" / "b2_decode_attn.h", ROOT / "include" / "b2_block.h", CSRC / "b2_internal.h"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -25,6 +25,7 @@
 #include <mutex>
 
 #include "b2_decode_attn.h"
+#include "b2_internal.h"
 
 namespace {
 
@@ -1842,6 +1843,9 @@ int sm_count() {
 }  // namespace
 
 // ------------------------------------------------------------------ C ABI
+
+int b2_record_error(int code, const char *message) { return fail(code, "%s", message); }
+int b2_clear_error() { return ok(); }
 
 extern "C" int b2_version(void) { return 100; }
 

@@ -1,0 +1,186 @@
+// B200 (sm_100a) kernels of the LFM2.5 layer around the attention hot path:
+//
+//   add_rmsnorm_kernel    residual add + RMSNorm (one CTA of 128 threads per row)
+//   swiglu_kernel         silu(w1 x) * (w3 x), 8 values per thread
+//   shortconv_step_kernel one decode step of the gated short convolution
+//
+// Each replaces a chain of small framework kernels between the layer's
+// GEMMs; the rounding points are those of the bf16 tensors of the model
+// definition (transformers modeling_lfm2.py, see include/b2_block.h).
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "b2_block.h"
+#include "b2_decode_attn.h"
+#include "b2_internal.h"
+
+namespace {
+
+constexpr int kNormThreads = 128;
+constexpr int kNormMaxChunks = 4;  // 8-value chunks per thread: width <= 128 * 8 * 4
+
+__device__ __forceinline__ float bf2f(uint32_t bits16) { return __uint_as_float(bits16 << 16); }
+
+__device__ __forceinline__ uint32_t f2bf(float x) {
+  return static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(x)));
+}
+
+__device__ __forceinline__ float rnd(float x) { return bf2f(f2bf(x)); }
+
+__device__ __forceinline__ void unpack8(const uint4 &w, float f[8]) {
+  const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(u[i] << 16);
+    f[2 * i + 1] = __uint_as_float(u[i] & 0xffff0000u);
+  }
+}
+
+__device__ __forceinline__ uint4 pack8(const float f[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+    w[i] = *reinterpret_cast<const uint32_t *>(&h);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// sum_out may alias x or residual: every thread reads its own chunks before
+// the barrier and writes only those chunks after it.
+__global__ void __launch_bounds__(kNormThreads)
+    add_rmsnorm_kernel(const uint16_t *x, const uint16_t *residual, const uint16_t *__restrict__ gamma,
+                       float eps, uint16_t *sum_out, uint16_t *__restrict__ norm_out, int width) {
+  __shared__ float red[kNormThreads / 32];
+  const int64_t row = blockIdx.x;
+  const int chunks = width / 8;
+  float v[kNormMaxChunks][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < kNormMaxChunks; ++k) {
+    const int c = threadIdx.x + k * kNormThreads;
+    if (c < chunks) {
+      unpack8(reinterpret_cast<const uint4 *>(x + row * width)[c], v[k]);
+      if (residual) {
+        float r[8];
+        unpack8(reinterpret_cast<const uint4 *>(residual + row * width)[c], r);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[k][e] = rnd(v[k][e] + r[e]);  // bf16 tensor add
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss = fmaf(v[k][e], v[k][e], ss);
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int w = 0; w < kNormThreads / 32; ++w) tot += red[w];
+  const float inv = rsqrtf(tot / static_cast<float>(width) + eps);
+#pragma unroll
+  for (int k = 0; k < kNormMaxChunks; ++k) {
+    const int c = threadIdx.x + k * kNormThreads;
+    if (c < chunks) {
+      if (sum_out) reinterpret_cast<uint4 *>(sum_out + row * width)[c] = pack8(v[k]);
+      float g[8], o[8];
+      unpack8(reinterpret_cast<const uint4 *>(gamma)[c], g);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = g[e] * rnd(v[k][e] * inv);
+      reinterpret_cast<uint4 *>(norm_out + row * width)[c] = pack8(o);
+    }
+  }
+}
+
+// silu(g) = g / (1 + e^-g) in fp32, rounded to bf16 as the bf16 silu tensor is
+__global__ void swiglu_kernel(const uint16_t *__restrict__ gu, uint16_t *__restrict__ out, int rows, int ffn) {
+  const int chunks = ffn / 8;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= static_cast<int64_t>(rows) * chunks) return;
+  const int64_t r = i / chunks;
+  const int c = static_cast<int>(i - r * chunks);
+  float g[8], u[8], o[8];
+  unpack8(reinterpret_cast<const uint4 *>(gu + r * 2 * ffn)[c], g);
+  unpack8(reinterpret_cast<const uint4 *>(gu + r * 2 * ffn + ffn)[c], u);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) o[e] = rnd(g[e] / (1.0f + __expf(-g[e]))) * u[e];
+  reinterpret_cast<uint4 *>(out + r * ffn)[c] = pack8(o);
+}
+
+// one thread per (row, channel); state [rows][hidden][3], weights [hidden][3]
+__global__ void shortconv_step_kernel(const uint16_t *__restrict__ bcx, uint16_t *__restrict__ state,
+                                      const uint16_t *__restrict__ w, uint16_t *__restrict__ out, int rows,
+                                      int hidden) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t r = blockIdx.y;
+  if (c >= hidden) return;
+  const uint16_t *in = bcx + r * 3 * hidden;
+  const float B = bf2f(in[c]), C = bf2f(in[hidden + c]), xx = bf2f(in[2 * hidden + c]);
+  const float bx = rnd(B * xx);
+  uint16_t *st = state + (r * hidden + c) * 3;
+  const float s1 = bf2f(st[1]), s2 = bf2f(st[2]);
+  st[0] = static_cast<uint16_t>(f2bf(s1));
+  st[1] = static_cast<uint16_t>(f2bf(s2));
+  st[2] = static_cast<uint16_t>(f2bf(bx));
+  const float p0 = rnd(s1 * bf2f(w[c * 3])), p1 = rnd(s2 * bf2f(w[c * 3 + 1])), p2 = rnd(bx * bf2f(w[c * 3 + 2]));
+  const float conv = rnd((p0 + p1) + p2);
+  out[r * hidden + c] = static_cast<uint16_t>(f2bf(C * conv));
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int launched(const char *what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return b2_record_error(B2_ERR_CUDA, what);
+  return b2_clear_error();
+}
+
+}  // namespace
+
+extern "C" int b2_add_rmsnorm(const uint16_t *x, const uint16_t *residual, const uint16_t *gamma, float eps,
+                              uint16_t *sum_out, uint16_t *norm_out, int32_t rows, int32_t width, void *stream) {
+  if (rows < 0) return b2_record_error(B2_ERR_ARG, "b2_add_rmsnorm: rows must be >= 0");
+  if (rows == 0) return b2_clear_error();
+  if (!x || !gamma || !norm_out) return b2_record_error(B2_ERR_ARG, "b2_add_rmsnorm: null pointer argument");
+  if (width <= 0 || width % 8 || width > kNormThreads * 8 * kNormMaxChunks)
+    return b2_record_error(B2_ERR_ARG, "b2_add_rmsnorm: width must be a positive multiple of 8, at most 4096");
+  if (!aligned16(x) || !aligned16(gamma) || !aligned16(norm_out) || (residual && !aligned16(residual)) ||
+      (sum_out && !aligned16(sum_out)))
+    return b2_record_error(B2_ERR_ARG, "b2_add_rmsnorm: pointers must be 16-byte aligned");
+  if (!(eps >= 0.f)) return b2_record_error(B2_ERR_ARG, "b2_add_rmsnorm: eps must be >= 0");
+  add_rmsnorm_kernel<<<rows, kNormThreads, 0, static_cast<cudaStream_t>(stream)>>>(x, residual, gamma, eps, sum_out,
+                                                                                 norm_out, width);
+  return launched("add_rmsnorm_kernel launch failed");
+}
+
+extern "C" int b2_swiglu(const uint16_t *gu, uint16_t *out, int32_t rows, int32_t ffn, void *stream) {
+  if (rows < 0) return b2_record_error(B2_ERR_ARG, "b2_swiglu: rows must be >= 0");
+  if (rows == 0) return b2_clear_error();
+  if (!gu || !out) return b2_record_error(B2_ERR_ARG, "b2_swiglu: null pointer argument");
+  if (ffn <= 0 || ffn % 8) return b2_record_error(B2_ERR_ARG, "b2_swiglu: ffn must be a positive multiple of 8");
+  if (!aligned16(gu) || !aligned16(out)) return b2_record_error(B2_ERR_ARG, "b2_swiglu: pointers must be 16-byte aligned");
+  const int64_t n = static_cast<int64_t>(rows) * (ffn / 8);
+  const int threads = 256;
+  const int64_t blocks = (n + threads - 1) / threads;
+  if (blocks > 0x7fffffff) return b2_record_error(B2_ERR_ARG, "b2_swiglu: too many rows");
+  swiglu_kernel<<<static_cast<unsigned>(blocks), threads, 0, static_cast<cudaStream_t>(stream)>>>(gu, out, rows, ffn);
+  return launched("swiglu_kernel launch failed");
+}
+
+extern "C" int b2_shortconv_step(const uint16_t *bcx, uint16_t *conv_state, const uint16_t *conv_w, uint16_t *out,
+                                 int32_t rows, int32_t hidden, void *stream) {
+  if (rows < 0) return b2_record_error(B2_ERR_ARG, "b2_shortconv_step: rows must be >= 0");
+  if (rows == 0) return b2_clear_error();
+  if (!bcx || !conv_state || !conv_w || !out)
+    return b2_record_error(B2_ERR_ARG, "b2_shortconv_step: null pointer argument");
+  if (hidden <= 0) return b2_record_error(B2_ERR_ARG, "b2_shortconv_step: hidden must be positive");
+  if (rows > 65535) return b2_record_error(B2_ERR_ARG, "b2_shortconv_step: rows must be <= 65535");
+  const int threads = 256;
+  const dim3 grid((hidden + threads - 1) / threads, rows);
+  shortconv_step_kernel<<<grid, threads, 0, static_cast<cudaStream_t>(stream)>>>(bcx, conv_state, conv_w, out, rows,
+                                                                                hidden);
+  return launched("shortconv_step_kernel launch failed");
+}

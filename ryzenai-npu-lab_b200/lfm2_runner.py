@@ -7,15 +7,17 @@ one.  Like the x8 engine's one submission per token
 (experiments/lfm25_x8.py:227-313, README.md:83-85), a whole token (14 layers
 and the head) is one CUDA-graph replay.
 
-Only the attention layers' hot path is this project's: q/k RMSNorm + RoPE +
-paged KV append + split-KV attention run in libb2attn.so's fused decode step.
-Everything else — token embedding, the gated short convolution, SwiGLU MLP,
-RMSNorm, the tied vocabulary head — is plain torch/cuBLAS (the harness around
-the hot path), written to the model definition the reference's CPU path
-uses (transformers modeling_lfm2.py: Lfm2RMSNorm 59-64, Lfm2MLP 135-152,
+The attention layers' hot path — q/k RMSNorm + RoPE + paged KV append +
+split-KV attention — runs in libb2attn.so's fused decode step.  Around it
+(fused_glue=True, the default) the layer's residual adds + RMSNorms, the
+SwiGLU gate and the short-convolution step are libb2attn.so kernels too
+(b2_add_rmsnorm, b2_swiglu, b2_shortconv_step), between cuBLAS GEMMs (w1 and
+w3 stacked into one); fused_glue=False runs that glue as plain torch ops.
+Both follow the model definition the reference's CPU path uses
+(transformers modeling_lfm2.py: Lfm2RMSNorm 59-64, Lfm2MLP 135-152,
 Lfm2ShortConv.slow_forward 356-387, Lfm2DecoderLayer.forward 413-442,
-Lfm2Model.forward 483-538) and to its cache update
-(cache_utils.py:771-786: the 3-token conv state rolls by one per token).
+Lfm2Model.forward 483-538) and its cache update (cache_utils.py:771-786: the
+3-token conv state rolls by one per token).
 
 Weights come from a state dict with the Hugging Face parameter names
 (model.layers.{i}.self_attn.q_proj.weight, ...), e.g. a random-init model.
@@ -26,6 +28,7 @@ from dataclasses import dataclass, field
 
 import torch
 
+from . import block
 from .attention import PagedDecodeAttention
 from .paged_cache import PagedKVCache, blocks_for
 
@@ -66,7 +69,7 @@ class LFM2DecodeRunner:
 
     def __init__(self, state_dict: dict, config: LFM2Config = LFM2Config(), *, max_batch: int,
                  max_context: int, device: torch.device | str = "cuda", use_graph: bool = True,
-                 blocks_per_split: int | None = None):
+                 blocks_per_split: int | None = None, fused_glue: bool = True):
         self.cfg = config
         self.device = torch.device(device)
         self.max_batch = max_batch
@@ -87,6 +90,7 @@ class LFM2DecodeRunner:
             lw = {"kind": kind, "op_norm": w(p + "operator_norm.weight"), "ffn_norm": w(p + "ffn_norm.weight"),
                   "w1": w(p + "feed_forward.w1.weight"), "w3": w(p + "feed_forward.w3.weight"),
                   "w2": w(p + "feed_forward.w2.weight")}
+            lw["w13"] = torch.cat([lw["w1"], lw["w3"]]).contiguous()      # [2 * ffn, hidden]
             if kind == "attention":
                 lw["qkv"] = torch.cat([w(p + "self_attn.q_proj.weight"), w(p + "self_attn.k_proj.weight"),
                                        w(p + "self_attn.v_proj.weight")]).contiguous()
@@ -121,11 +125,59 @@ class LFM2DecodeRunner:
         self.position = 0
         self.use_graph = use_graph and self.device.type == "cuda"
         self._graph = None
+        self.fused_glue = fused_glue
+        if fused_glue:
+            ffn = self.layers[0]["w1"].shape[0]
+            hd = config.hidden
+
+            def buf(*shape):
+                return torch.empty(*shape, dtype=bf, device=dev)
+            self.h, self.x, self.o, self.y = buf(max_batch, hd), buf(max_batch, hd), buf(max_batch, hd), \
+                buf(max_batch, hd)
+            self.qkv = buf(max_batch, (config.heads + 2 * config.kv_heads) * config.head_dim)
+            self.bcx, self.gu, self.m = buf(max_batch, 3 * hd), buf(max_batch, 2 * ffn), buf(max_batch, ffn)
 
     # ---------------------------------------------------------------- model
 
     def _token(self) -> None:
         """One token for every sequence: ids -> logits, next_ids; advances past."""
+        if self.fused_glue:
+            self._token_fused()
+        else:
+            self._token_torch()
+
+    def _token_fused(self) -> None:
+        """The token with the layer glue in libb2attn.so: per layer two GEMMs
+        around the mixer (attention step or short-convolution step), then
+        residual + RMSNorm, the stacked w1/w3 GEMM, SwiGLU, w2 GEMM; each
+        residual add is fused into the RMSNorm that follows it."""
+        cfg, b = self.cfg, self.max_batch
+        h, x, o = self.h, self.x, self.o
+        torch.index_select(self.embed, 0, self.ids, out=h)
+        torch.add(self.past, 1, out=self.seq)
+        block.add_rmsnorm(h, None, self.layers[0]["op_norm"], cfg.eps, out=x)
+        n = len(self.layers)
+        for i, lw in enumerate(self.layers):
+            if lw["kind"] == "attention":
+                torch.matmul(x, lw["qkv"].t(), out=self.qkv)                     # [B, 2048]: q | k | v
+                ctx = self.attn[lw["att"]].step(lw["att"], self.qkv, self.past, self.seq, self.tables)
+                torch.matmul(ctx.reshape(b, cfg.heads * cfg.head_dim), lw["out"].t(), out=o)
+            else:
+                torch.matmul(x, lw["in"].t(), out=self.bcx)                      # [B, 3 * hidden]: B | C | x
+                block.shortconv_step(self.bcx, self.conv_state[lw["conv_id"]], lw["conv"], out=self.y)
+                torch.matmul(self.y, lw["out"].t(), out=o)
+            block.add_rmsnorm(o, h, lw["ffn_norm"], cfg.eps, out=x, sum_out=h)  # h += mixer; x = ffn_norm(h)
+            torch.matmul(x, lw["w13"].t(), out=self.gu)
+            block.swiglu(self.gu, out=self.m)
+            torch.matmul(self.m, lw["w2"].t(), out=o)
+            nxt = self.layers[i + 1]["op_norm"] if i + 1 < n else self.final_norm
+            block.add_rmsnorm(o, h, nxt, cfg.eps, out=x, sum_out=h)             # h += ffn; x = next norm(h)
+        torch.matmul(x, self.head.t(), out=self.logits)
+        torch.argmax(self.logits, dim=-1, out=self.next_ids)
+        self.past.add_(1)
+
+    def _token_torch(self) -> None:
+        """The token with the layer glue as torch ops."""
         cfg = self.cfg
         b = self.max_batch
         h = self.embed[self.ids]                                   # [B, hidden]
@@ -159,7 +211,7 @@ class LFM2DecodeRunner:
         if self._graph is None:
             # warm up on a side stream, then capture one token (state is
             # restored afterwards so the capture run does not count)
-            saved = (self.past.clone(), self.conv_state.clone())
+            saved = (self.past.clone(), self.conv_state.clone())  # restored after the capture run
             s = torch.cuda.Stream(self.device)
             s.wait_stream(torch.cuda.current_stream(self.device))
             with torch.cuda.stream(s):

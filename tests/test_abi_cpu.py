@@ -1,23 +1,35 @@
 """CPU checks of the C ABI: the in-tree library loads without a GPU and
-exports every entry point include/b2_decode_attn.h declares."""
+exports every entry point the headers under include/ declare."""
 import ctypes
 import pathlib
 import re
 
 from conftest import ROOT, load_pkg
 
-HEADER = ROOT / "include" / "b2_decode_attn.h"
+HEADERS = sorted((ROOT / "include").glob("*.h"))
 
 
 def declared_functions():
-    text = HEADER.read_text()
-    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return sorted(set(re.findall(r"\bint\s+(b2_\w+)\s*\(", text)))
+    names = set()
+    for h in HEADERS:
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        names |= set(re.findall(r"\b(?:int|int64_t)\s+(b2_\w+)\s*\(", text))
+    return sorted(names)
 
 
 def test_header_declares_entry_points():
     names = declared_functions()
-    assert {"b2_append_rope", "b2_decode_attn", "b2_combine", "b2_last_error", "b2_version"} <= set(names)
+    assert {"b2_append_rope", "b2_decode_attn", "b2_combine", "b2_last_error", "b2_version",
+            "b2_exchange_bytes", "b2_add_rmsnorm", "b2_swiglu", "b2_shortconv_step"} <= set(names)
+
+
+def test_block_entry_points_check_arguments_without_gpu():
+    lib = load_pkg("_lib")
+    cdll = lib.load()
+    assert cdll.b2_add_rmsnorm(None, None, None, ctypes.c_float(1e-5), None, None, 1, 1024, None) == lib.B2_ERR_ARG
+    assert "null pointer" in lib.last_error()
+    assert cdll.b2_swiglu(None, None, 0, 2560, None) == lib.B2_OK      # no rows: nothing to do
+    assert cdll.b2_shortconv_step(None, None, None, None, 2, 1024, None) == lib.B2_ERR_ARG
 
 
 def test_library_exports_every_declared_symbol():

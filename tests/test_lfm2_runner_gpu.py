@@ -33,15 +33,16 @@ def _weights(f):
     return sd
 
 
+@pytest.mark.parametrize("fused_glue", [True, False], ids=["kernels", "torch_glue"])
 @pytest.mark.parametrize("use_graph", [True, False], ids=["graph", "eager"])
-def test_greedy_teacher_forced_matches_reference(cuda, use_graph):
+def test_greedy_teacher_forced_matches_reference(cuda, use_graph, fused_glue):
     f = dict(np.load(GOLDEN))
     runner_mod = load_pkg("lfm2_runner")
     inputs = f["inputs"]                      # [B, T]
     top_v, top_i = f["top_values"], f["top_indices"]
     b, steps = inputs.shape
     runner = runner_mod.LFM2DecodeRunner(_weights(f), max_batch=b, max_context=64, device=cuda,
-                                         use_graph=use_graph)
+                                         use_graph=use_graph, fused_glue=fused_glue)
     exact = mismatches = 0
     worst = 0.0
     for t in range(steps):
@@ -76,3 +77,24 @@ def test_generate_and_reset(cuda):
     assert a.shape == (2, 6) and torch.equal(a, b)
     with pytest.raises(ValueError):
         runner.step(torch.zeros(3, dtype=torch.long))
+
+
+def test_kernel_glue_matches_torch_glue(cuda):
+    """The same model, token by token, with the layer glue in libb2attn.so and
+    as torch ops: logits within a few bf16 ulps of their scale."""
+    runner_mod = load_pkg("lfm2_runner")
+    f = dict(np.load(GOLDEN))
+    sd = _weights(f)
+    ids = torch.from_numpy(f["inputs"])
+    runs = []
+    for fused in (True, False):
+        r = runner_mod.LFM2DecodeRunner(sd, max_batch=ids.shape[0], max_context=40, device=cuda, fused_glue=fused)
+        logits = []
+        for t in range(12):
+            r.step(ids[:, t])
+            logits.append(r.logits.float().clone())
+        r.check()
+        runs.append(torch.stack(logits))
+    scale = runs[1].abs().max().item()
+    err = (runs[0] - runs[1]).abs().max().item()
+    assert err <= max(0.0625, 4 * 2.0 ** (np.floor(np.log2(scale)) - 7)), f"logits differ by {err} (scale {scale})"
