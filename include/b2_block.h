@@ -54,6 +54,14 @@ int b2_swiglu(const uint16_t *gu, uint16_t *out, int32_t rows, int32_t ffn, void
 int b2_shortconv_step(const uint16_t *bcx, uint16_t *conv_state, const uint16_t *conv_w,
                       uint16_t *out, int32_t rows, int32_t hidden, void *stream);
 
+/*
+ * out[r] = index of the largest of the `cols` bf16 values of row r (the
+ * first one on ties; NaN counts as the largest), as torch.argmax returns it,
+ * for the greedy token choice after the vocabulary head (the reference's
+ * X8Model.step select, experiments/lfm25_x8_model.py:133-148).
+ */
+int b2_argmax_rows(const uint16_t *logits, int32_t rows, int32_t cols, int64_t *out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

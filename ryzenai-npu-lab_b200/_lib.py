@@ -113,6 +113,7 @@ SIGNATURES = {
     "b2_add_rmsnorm": (ctypes.c_int, [_p, _p, _p, _f32, _p, _p, _i32, _i32, _p]),
     "b2_swiglu": (ctypes.c_int, [_p, _p, _i32, _i32, _p]),
     "b2_shortconv_step": (ctypes.c_int, [_p, _p, _p, _p, _i32, _i32, _p]),
+    "b2_argmax_rows": (ctypes.c_int, [_p, _i32, _i32, _p, _p]),
     "b2_merge_states": (ctypes.c_int, [
         _p, _i32, _i32,      # states, num_parts, batch
         _p, _p, _p, _p,      # out, state_ml, state_o, stream

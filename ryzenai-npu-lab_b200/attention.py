@@ -106,11 +106,17 @@ def choose_blocks_per_split(batch: int, work_blocks: int, sms: int = B200_SMS, f
     kernel: about 6 items per resident CTA (items stream back to back, so they
     can be smaller; the end-of-launch tail is one item).  Measured on the C3
     workload: the fused kernel is within 1 % of its best for 8-16 blocks.
+    With many sequences of at most 32 blocks, one split per sequence.
     With a few sequences (a long context split over the CTAs) the items are
     all alike: about two per SM in one wave, every CTA streaming the same
     number of blocks (up to 64), finish together; measured on one 131 072-token
     sequence: 46.9 us at 296 items against 51.4 us at 432 and 52 us at 2 056."""
     if fused:
+        per_seq_max = math.ceil(work_blocks / max(1, batch))
+        if batch * HKV >= 2 * sms * 3 and per_seq_max <= 32:
+            # many short sequences: one split each (no cross-CTA merge; the
+            # item's own epilogue writes the context)
+            return int(max(1, per_seq_max))
         if batch <= 4:
             per_seq = math.ceil(work_blocks / max(1, batch))
             splits = max(1, (sms * 2) // (max(1, batch) * HKV))

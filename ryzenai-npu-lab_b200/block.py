@@ -1,6 +1,6 @@
 """Torch-facing wrappers of the layer kernels around the attention path
 (include/b2_block.h): residual add + RMSNorm, SwiGLU gate, short-convolution
-decode step.  Same conventions as attention.py: host checks raise ValueError,
+decode step, greedy argmax over the logits.  Same conventions as attention.py: host checks raise ValueError,
 library refusals raise B2Error, work is queued on the current CUDA stream."""
 from __future__ import annotations
 
@@ -63,4 +63,17 @@ def shortconv_step(bcx: torch.Tensor, conv_state: torch.Tensor, conv_w: torch.Te
     rc = _lib.load().b2_shortconv_step(_ptr(bcx), _ptr(conv_state), _ptr(conv_w), _ptr(out), rows, hidden,
                                        _stream(dev, stream))
     _lib.check(rc, "b2_shortconv_step")
+    return out
+
+
+def argmax_rows(logits: torch.Tensor, *, out: torch.Tensor, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """out[r] = torch.argmax(logits[r]) for bf16 logits [rows, cols] -> int64 [rows]."""
+    dev = logits.device
+    if logits.dim() != 2:
+        raise ValueError("logits must be [rows, cols]")
+    rows, cols = logits.shape
+    _need(logits, "logits", torch.bfloat16, dev)
+    _need(out, "out", torch.int64, dev, (rows,))
+    _lib.check(_lib.load().b2_argmax_rows(_ptr(logits), rows, cols, _ptr(out), _stream(dev, stream)),
+               "b2_argmax_rows")
     return out

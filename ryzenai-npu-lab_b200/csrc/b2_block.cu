@@ -3,6 +3,7 @@
 //   add_rmsnorm_kernel    residual add + RMSNorm (one CTA of 128 threads per row)
 //   swiglu_kernel         silu(w1 x) * (w3 x), 8 values per thread
 //   shortconv_step_kernel one decode step of the gated short convolution
+//   argmax_rows_kernel    greedy token choice over the vocabulary logits
 //
 // Each replaces a chain of small framework kernels between the layer's
 // GEMMs; the rounding points are those of the bf16 tensors of the model
@@ -10,6 +11,7 @@
 
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
+#include <math.h>
 #include <stdint.h>
 
 #include "b2_block.h"
@@ -130,6 +132,60 @@ __global__ void shortconv_step_kernel(const uint16_t *__restrict__ bcx, uint16_t
   out[r * hidden + c] = static_cast<uint16_t>(f2bf(C * conv));
 }
 
+// (value, index) pairs: a beats b when larger, NaN beating numbers, and the
+// smaller index on ties (torch.argmax's first maximum)
+__device__ __forceinline__ bool better(float va, int ia, float vb, int ib) {
+  const bool na = va != va, nb = vb != vb;
+  if (na != nb) return na;
+  if (!na && va != vb) return va > vb;
+  return ia < ib;
+}
+
+constexpr int kArgmaxThreads = 512;
+
+// one CTA per row; 8 values per 16-byte load (cols % 8 == 0)
+__global__ void __launch_bounds__(kArgmaxThreads)
+    argmax_rows_kernel(const uint16_t *__restrict__ logits, int cols, int64_t *__restrict__ out) {
+  __shared__ float sv[kArgmaxThreads / 32];
+  __shared__ int si[kArgmaxThreads / 32];
+  const int64_t row = blockIdx.x;
+  const uint4 *p = reinterpret_cast<const uint4 *>(logits + row * cols);
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int c = threadIdx.x; c < cols / 8; c += kArgmaxThreads) {
+    float v[8];
+    unpack8(p[c], v);
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      if (better(v[e], c * 8 + e, bv, bi)) {
+        bv = v[e];
+        bi = c * 8 + e;
+      }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+    if (better(ov, oi, bv, bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  if ((threadIdx.x & 31) == 0) {
+    sv[threadIdx.x >> 5] = bv;
+    si[threadIdx.x >> 5] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < kArgmaxThreads / 32; ++w)
+      if (better(sv[w], si[w], bv, bi)) {
+        bv = sv[w];
+        bi = si[w];
+      }
+    out[row] = bi;
+  }
+}
+
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 int launched(const char *what) {
@@ -183,4 +239,14 @@ extern "C" int b2_shortconv_step(const uint16_t *bcx, uint16_t *conv_state, cons
   shortconv_step_kernel<<<grid, threads, 0, static_cast<cudaStream_t>(stream)>>>(bcx, conv_state, conv_w, out, rows,
                                                                                 hidden);
   return launched("shortconv_step_kernel launch failed");
+}
+
+extern "C" int b2_argmax_rows(const uint16_t *logits, int32_t rows, int32_t cols, int64_t *out, void *stream) {
+  if (rows < 0) return b2_record_error(B2_ERR_ARG, "b2_argmax_rows: rows must be >= 0");
+  if (rows == 0) return b2_clear_error();
+  if (!logits || !out) return b2_record_error(B2_ERR_ARG, "b2_argmax_rows: null pointer argument");
+  if (cols <= 0 || cols % 8) return b2_record_error(B2_ERR_ARG, "b2_argmax_rows: cols must be a positive multiple of 8");
+  if (!aligned16(logits)) return b2_record_error(B2_ERR_ARG, "b2_argmax_rows: logits must be 16-byte aligned");
+  argmax_rows_kernel<<<rows, kArgmaxThreads, 0, static_cast<cudaStream_t>(stream)>>>(logits, cols, out);
+  return launched("argmax_rows_kernel launch failed");
 }

@@ -173,7 +173,7 @@ class LFM2DecodeRunner:
             nxt = self.layers[i + 1]["op_norm"] if i + 1 < n else self.final_norm
             block.add_rmsnorm(o, h, nxt, cfg.eps, out=x, sum_out=h)             # h += ffn; x = next norm(h)
         torch.matmul(x, self.head.t(), out=self.logits)
-        torch.argmax(self.logits, dim=-1, out=self.next_ids)
+        block.argmax_rows(self.logits, out=self.next_ids)
         self.past.add_(1)
 
     def _token_torch(self) -> None:

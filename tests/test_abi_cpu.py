@@ -20,7 +20,7 @@ def declared_functions():
 def test_header_declares_entry_points():
     names = declared_functions()
     assert {"b2_append_rope", "b2_decode_attn", "b2_combine", "b2_last_error", "b2_version",
-            "b2_exchange_bytes", "b2_add_rmsnorm", "b2_swiglu", "b2_shortconv_step"} <= set(names)
+            "b2_exchange_bytes", "b2_add_rmsnorm", "b2_swiglu", "b2_shortconv_step", "b2_argmax_rows"} <= set(names)
 
 
 def test_block_entry_points_check_arguments_without_gpu():

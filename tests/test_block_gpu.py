@@ -99,3 +99,20 @@ def test_block_argument_errors(cuda):
     with pytest.raises(ValueError):
         blk.shortconv_step(torch.zeros(2, 3072, dtype=BF, device=cuda), torch.zeros(2, 1024, 2, dtype=BF, device=cuda),
                            torch.zeros(1024, 3, dtype=BF, device=cuda), out=torch.empty(2, 1024, dtype=BF, device=cuda))
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 65536), (256, 65536), (3, 8), (2, 4096)])
+def test_argmax_rows(cuda, rows, cols):
+    blk = load_pkg("block")
+    g = torch.Generator(device=cuda).manual_seed(rows + cols)
+    logits = torch.randn(rows, cols, generator=g, device=cuda).to(BF)
+    logits[0, cols // 3] = logits[0].max() + 1      # a clear winner
+    if rows > 1:                                    # ties: the first index wins
+        logits[1, :] = 0
+        logits[1, 5] = logits[1, cols - 1] = 7.0
+    if rows > 2:
+        logits[2, 2] = float("nan")                 # NaN counts as the maximum
+    out = torch.empty(rows, dtype=torch.int64, device=cuda)
+    blk.argmax_rows(logits, out=out)
+    torch.cuda.synchronize()
+    assert torch.equal(out, torch.argmax(logits, dim=-1))
