@@ -1637,7 +1637,37 @@ __global__ void __launch_bounds__(kPfThreads, 2)
       const bool got = mbar_wait(bar, parity);
       return !__any_sync(0xffffffffu, !got || tail->abort);
     };
-    for (int j = 0; j < nblk; ++j) {
+    // A warp whose 32 rows are all past the chunk (tiles of fewer than 33
+    // tokens) keeps step with the barriers but computes nothing: its P rows
+    // only feed O rows that are never stored.
+    const bool warp_active = __any_sync(0xffffffffu, row_ok);
+    for (int j = 0; j < nblk && !warp_active; ++j) {
+      const int s = j % kPfStages;
+      if (!warp_wait(smem_u32(&tail->sbar[j & 1]), (j >> 1) & 1)) {
+        ok = false;
+        break;
+      }
+      mbar_arrive(smem_u32(&tail->sfree[j & 1]));
+      if (j >= 2 && !warp_wait(smem_u32(&tail->pfree[j & 1]), ((j >> 1) - 1) & 1)) {
+        ok = false;
+        break;
+      }
+      const int key0 = j * kBlock;
+      if (key0 + kBlock - 1 > last_key) {
+        // this thread's share of zeroing the V rows past the tile (below)
+        if (!warp_wait(smem_u32(&tail->vfull[s]), (j / kPfStages) & 1)) {
+          ok = false;
+          break;
+        }
+        const int first_bad = last_key - key0 + 1;
+        uint8_t *v_gen = vring + s * kTileBytes;
+        for (int i = tid; i < (kBlock - first_bad) * 8; i += 128)
+          *reinterpret_cast<uint4 *>(v_gen + (first_bad + (i >> 3)) * 128 + ((i & 7) << 4)) = make_uint4(0, 0, 0, 0);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      }
+      mbar_arrive(smem_u32(&tail->pready[j & 1]));
+    }
+    for (int j = 0; j < nblk && warp_active; ++j) {
       const int s = j % kPfStages;
       if (!warp_wait(smem_u32(&tail->sbar[j & 1]), (j >> 1) & 1)) {
         ok = false;
