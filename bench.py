@@ -544,8 +544,9 @@ def run_c4(args):
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": f"C4 long-context decode: one sequence of {args.context} cached tokens "
                                f"split along the token axis over {world} GPU(s), partial softmax states "
-                               + {"p2p": "exchanged over NVLink peer memory and merged in one kernel "
-                                         "(b2_exchange_merge)",
+                               + {"p2p": "merged by the combine kernel, which exchanges them with the other "
+                                         "ranks over NVLink peer memory and merges the world's "
+                                         "(b2_decode_step_exchange)",
                                   "collective": "all-gathered over NCCL and merged",
                                   "direct": "(one GPU: merged in the step)"}[lc.exchange],
                    "context": args.context, "exchange": lc.exchange,
@@ -557,7 +558,8 @@ def run_c4(args):
                      "unit": "GB/s", "frac": local_bytes / (part_ms / 1e3) / 1e9 / peak, "traffic": None,
                      "algorithmic_bytes": local_bytes, "avg_launch_ms": part_ms},
         "clocks": clocks.summary(),
-        "gpu_launches": K * (1 + (lc.splits > 16) + {"p2p": 1, "collective": 2, "direct": 0}[lc.exchange]),
+        "gpu_launches": K * {"p2p": 2, "collective": 1 + (lc.splits > 16) + 2,
+                             "direct": 1 + (lc.splits > 16)}[lc.exchange],
     }
     if rank == 0:
         print(json.dumps(line), flush=True)

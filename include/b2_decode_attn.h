@@ -286,6 +286,25 @@ int b2_merge_states(const float *states, int32_t num_parts, int32_t batch,
  * Launched as a programmatic dependent of the previous kernel in the stream.
  */
 #define B2_XCHG_MAX_WORLD 8
+/*
+ * b2_decode_step with the exchange fused into its merge: the splits of every
+ * (sequence, query head) are merged by the combine kernel, which then runs
+ * the exchange of b2_exchange_merge itself (this rank's merged state into
+ * every rank's area, the world's states merged) and writes the context into
+ * out.  One call, two launches (the step kernel and the combine kernel as its
+ * programmatic dependent); the same rules for the areas as b2_exchange_merge.
+ */
+int b2_decode_step_exchange(const uint16_t *qkv, int64_t row_stride,
+                            const uint16_t *gamma_q, const uint16_t *gamma_k, float eps,
+                            const uint16_t *rope_cos, const uint16_t *rope_sin,
+                            int32_t rope_rows, const int32_t *past_lens,
+                            const int32_t *seq_lens, const int32_t *block_tables,
+                            int32_t max_blocks_per_seq, uint16_t *k_pool, uint16_t *v_pool,
+                            int32_t num_blocks, int32_t batch, int32_t blocks_per_split,
+                            float scale, int32_t mode, uint16_t *out, uint16_t *q_out,
+                            float *part_ml, float *part_o, int32_t *counters,
+                            int32_t max_ctas, void *const *areas, int32_t world,
+                            int32_t rank, int32_t *dev_err, void *stream);
 int64_t b2_exchange_bytes(int32_t world, int32_t batch);
 int b2_ipc_handle(const void *ptr, void *handle64, int64_t *offset);
 int b2_ipc_open(const void *handle64, int64_t offset, void **peer_ptr);

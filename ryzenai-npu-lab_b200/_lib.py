@@ -100,6 +100,19 @@ SIGNATURES = {
         _p,                  # stream
     ]),
     "b2_decode_step_host_join": (ctypes.c_int, [_p]),
+    "b2_decode_step_exchange": (ctypes.c_int, [
+        _p, ctypes.c_int64,  # qkv, row_stride
+        _p, _p, _f32,        # gamma_q, gamma_k, eps
+        _p, _p, _i32,        # rope_cos, rope_sin, rope_rows
+        _p, _p,              # past_lens, seq_lens
+        _p, _i32,            # block_tables, max_blocks_per_seq
+        _p, _p, _i32,        # k_pool, v_pool, num_blocks
+        _i32, _i32, _f32, _i32,  # batch, blocks_per_split, scale, mode
+        _p, _p,              # out, q_out
+        _p, _p, _p, _i32,    # part_ml, part_o, counters, max_ctas
+        _p, _i32, _i32,      # areas (host array of world pointers), world, rank
+        _p, _p,              # dev_err, stream
+    ]),
     "b2_exchange_bytes": (ctypes.c_int64, [_i32, _i32]),
     "b2_ipc_handle": (ctypes.c_int, [_p, _p, ctypes.POINTER(ctypes.c_int64)]),
     "b2_ipc_open": (ctypes.c_int, [_p, ctypes.c_int64, ctypes.POINTER(ctypes.c_void_p)]),

@@ -190,12 +190,15 @@ def decode_step(qkv: torch.Tensor, past_lens: torch.Tensor, *, k_pool: torch.Ten
                 seq_lens: torch.Tensor | None = None, state_ml: torch.Tensor | None = None,
                 state_o: torch.Tensor | None = None,
                 mode: int = _lib.B2_NORM_QK | _lib.B2_ROPE_QK | _lib.B2_STORE_KV, eps: float = EPS,
-                scale: float = SCALE, max_ctas: int = 0, stream: torch.cuda.Stream | None = None) -> int:
+                scale: float = SCALE, max_ctas: int = 0, stream: torch.cuda.Stream | None = None,
+                exchange=None) -> int:
     """Fused decode step in one persistent launch (b2_decode_step): norm + RoPE,
     append at past_lens[b], attention over past_lens[b] + 1 tokens (or
     seq_lens[b]), merge into `out` or into fp32 states (state_ml, state_o).
-    `counters` (int32[2 + 8 * batch]) must be zero on the first call; the
-    kernel leaves it zero.  Returns num_splits."""
+    With exchange = (areas, world, rank) (b2_decode_step_exchange) the merged
+    states are exchanged with the other ranks over peer memory and `out`
+    receives the world's context.  `counters` (int32[2 + 8 * batch]) must be
+    zero on the first call; the kernel leaves it zero.  Returns num_splits."""
     dev = qkv.device
     if qkv.dim() != 2 or qkv.shape[1] < QKV_WIDTH:
         raise ValueError(f"qkv must be [batch, >= {QKV_WIDTH}], got {tuple(qkv.shape)}")
@@ -213,7 +216,10 @@ def decode_step(qkv: torch.Tensor, past_lens: torch.Tensor, *, k_pool: torch.Ten
         _need(out, "out", torch.bfloat16, dev)
         if out.numel() != b * HQ * D:
             raise ValueError("out must hold batch x 16 x 64 elements")
-    if state_o is not None or out is None:
+    if exchange is not None:
+        if out is None or state_o is not None or state_ml is not None:
+            raise ValueError("a decode step with an exchange writes out and no state")
+    elif state_o is not None or out is None:
         _need(state_ml, "state_ml", torch.float32, dev, (b, HQ, 2))
         _need(state_o, "state_o", torch.float32, dev, (b, HQ, D))
     if seq_lens is not None:
@@ -238,12 +244,18 @@ def decode_step(qkv: torch.Tensor, past_lens: torch.Tensor, *, k_pool: torch.Ten
     _need(part_o, "part_o", torch.float32, dev)
     if part_ml.numel() < b * splits * HQ * 2 or part_o.numel() < b * splits * HQ * D:
         raise ValueError(f"partial-state buffers too small for {b} x {splits} splits")
-    rc = _lib.load().b2_decode_step(
-        _ptr(qkv), qkv.stride(0), _ptr(gamma_q), _ptr(gamma_k), ctypes.c_float(eps), _ptr(cos), _ptr(sin),
-        rope_rows, _ptr(past_lens), _ptr(seq_lens), _ptr(block_tables), max_blocks, _ptr(k_pool), _ptr(v_pool),
-        k_pool.shape[0], b, blocks_per_split, ctypes.c_float(scale), mode, _ptr(out), _ptr(q_out),
-        _ptr(state_ml), _ptr(state_o), _ptr(part_ml), _ptr(part_o), _ptr(counters), max_ctas, _ptr(dev_err),
-        _stream(dev, stream))
+    common = (_ptr(qkv), qkv.stride(0), _ptr(gamma_q), _ptr(gamma_k), ctypes.c_float(eps), _ptr(cos), _ptr(sin),
+              rope_rows, _ptr(past_lens), _ptr(seq_lens), _ptr(block_tables), max_blocks, _ptr(k_pool),
+              _ptr(v_pool), k_pool.shape[0], b, blocks_per_split, ctypes.c_float(scale), mode, _ptr(out),
+              _ptr(q_out))
+    if exchange is not None:
+        areas, world, rank = exchange
+        rc = _lib.load().b2_decode_step_exchange(*common, _ptr(part_ml), _ptr(part_o), _ptr(counters), max_ctas,
+                                                 areas, world, rank, _ptr(dev_err), _stream(dev, stream))
+        _lib.check(rc, "b2_decode_step_exchange")
+        return splits
+    rc = _lib.load().b2_decode_step(*common, _ptr(state_ml), _ptr(state_o), _ptr(part_ml), _ptr(part_o),
+                                    _ptr(counters), max_ctas, _ptr(dev_err), _stream(dev, stream))
     _lib.check(rc, "b2_decode_step")
     return splits
 

@@ -532,6 +532,106 @@ __global__ void __launch_bounds__(kDecodeThreads, 3)
 }
 
 
+// ------------------------------------------------------------------ multi-GPU state exchange (NVLink P2P)
+
+// One sequence's KV cache split along the token axis over `world` GPUs: every
+// rank holds a partial softmax state (max, sum, unnormalised output) per
+// (sequence, query head).  Instead of an all-gather collective followed by a
+// merge launch, one kernel writes this rank's state straight into every
+// rank's exchange area over NVLink (peer pointers from CUDA IPC) and merges
+// the world's states once they have arrived in its own area.
+//
+// Every value travels as one 8-byte word {float bits, tag}, written with a
+// single 8-byte store, where tag = step number + 1 (the low-latency protocol
+// of collective libraries): a reader polls the words themselves until their
+// tags show the current step, so no fence or separate flag is needed.
+// Exchange area (every rank, same layout; zeroed before first use):
+//   uint2 word[2 slots][world][batch][16][kXState]   (m, l, 2 unused, o[64])
+//   int   step[batch][16]                            (local step counter)
+// Steps alternate slots.  A rank can be at most one step ahead of another
+// (its next merge needs the other's words of that step, written after the
+// other's previous merge finished reading), so a slot is never overwritten
+// while it is read.
+
+constexpr int kXState = 4 + kDim;
+constexpr int kXMaxWorld = B2_XCHG_MAX_WORLD;
+constexpr uint64_t kXWaitNs = 5000000000ull;  // 5 s, then B2_DEV_TIMEOUT
+
+struct XchgArgs {
+  const float *state_ml;  // [batch][16][2]
+  const float *state_o;   // [batch][16][64]
+  int batch, world, rank;
+  uint16_t *out;  // [batch][16][64]
+  int32_t *err;
+  char *area[kXMaxWorld];  // rank r's exchange area as mapped on this GPU
+};
+
+__host__ __device__ constexpr int64_t x_words(int world, int batch) {
+  return 2ll * world * batch * kHq * kXState;
+}
+
+__device__ __forceinline__ void st_word(uint2 *p, float v, uint32_t tag) {
+  asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(__float_as_uint(v)), "r"(tag)
+               : "memory");
+}
+
+__device__ __forceinline__ uint2 ld_word(const uint2 *p) {
+  uint2 w;
+  asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(w.x), "=r"(w.y) : "l"(p) : "memory");
+  return w;
+}
+
+
+// Exchange this rank's state (m, l, o[d] of thread d) for (sequence b, query
+// head h) with every rank and write the world-merged context.  Run by 64
+// threads (d = 0..63) that can sync on named barrier 2; see the exchange
+// area layout above.
+__device__ __forceinline__ void xchg_merge(const XchgArgs &a, int b, int h, int d, float m, float l, float o) {
+  const int bh = b * kHq + h;
+  const uint2 *own = reinterpret_cast<const uint2 *>(a.area[a.rank]);
+  int32_t *steps = reinterpret_cast<int32_t *>(reinterpret_cast<uint2 *>(a.area[a.rank]) + x_words(a.world, a.batch));
+  const int32_t step = steps[bh];
+  const int slot = step & 1;
+  const uint32_t tag = static_cast<uint32_t>(step) + 1u;
+  const int64_t mine = (((static_cast<int64_t>(slot) * a.world + a.rank) * a.batch + b) * kHq + h) * kXState;
+  for (int r = 0; r < a.world; ++r) {
+    uint2 *dst = reinterpret_cast<uint2 *>(a.area[r]) + mine;
+    st_word(dst + 4 + d, o, tag);
+    if (d == 0) {
+      st_word(dst, m, tag);
+      st_word(dst + 1, l, tag);
+    }
+  }
+  float M = -1.0e30f, L = 0.f, O = 0.f;
+  bool ok = true;
+  const uint64_t t0 = global_ns();
+  for (int r = 0; r < a.world && ok; ++r) {
+    const uint2 *src = own + (((static_cast<int64_t>(slot) * a.world + r) * a.batch + b) * kHq + h) * kXState;
+    uint2 wm, wl, wo;
+    for (;;) {
+      wm = ld_word(src);
+      wl = ld_word(src + 1);
+      wo = ld_word(src + 4 + d);
+      if (wm.y == tag && wl.y == tag && wo.y == tag) break;
+      if (global_ns() - t0 > kXWaitNs) {
+        atomicOr(a.err, B2_DEV_TIMEOUT);
+        ok = false;
+        break;
+      }
+    }
+    if (!ok) break;
+    const float ms = __uint_as_float(wm.x), ls = __uint_as_float(wl.x), os = __uint_as_float(wo.x);
+    const float nm = fmaxf(M, ms);
+    const float c1 = ex2(M - nm), c2 = ex2(ms - nm);
+    L = L * c1 + ls * c2;
+    O = O * c1 + os * c2;
+    M = nm;
+  }
+  if (ok) a.out[(int64_t)bh * kDim + d] = static_cast<uint16_t>(bf16_bits(L > 0.f ? O / L : 0.f));
+  asm volatile("bar.sync 2, 64;" ::: "memory");  // every thread has read its words of this step
+  if (d == 0) steps[bh] = step + 1;
+}
+
 // ------------------------------------------------------------------ combine
 
 struct CombineArgs {
@@ -549,7 +649,8 @@ struct CombineArgs {
   // float strides between sequences (b) and parts (s); 0 = the default
   // [batch][num_parts][16][2 | 64] layout
   int64_t ml_b, ml_s, o_b, o_s;
-  int groups;  // part groups per CTA (blockDim.x / 64), 1..16
+  int groups;  // part groups per CTA (blockDim.x / 64), 1..8
+  XchgArgs x;  // x.world > 0: exchange the merged state with the other ranks (out = x.out)
 };
 
 // Part groups for a merge of up to num_parts parts: enough threads to merge
@@ -579,13 +680,16 @@ __global__ void __launch_bounds__(kCombineGroups * kDim) combine_kernel(const Co
   const int h = blockIdx.y;
   const int grp = threadIdx.x >> 6;
   const int d = threadIdx.x & 63;
+  const bool exchange = a.x.world > 0;
   int parts = a.num_parts;
   if (a.seq_lens) {
     const int len = a.seq_lens[b] + a.len_offset;
-    if (len > a.max_tokens) return;  // flagged by the decode kernel
-    const int nblk = len > 0 ? (len + kBlock - 1) / kBlock : 0;
+    // an invalid length (flagged by the decode kernel) still takes part in an
+    // exchange, with an empty state, so that no rank waits for it in vain
+    if (len > a.max_tokens && !exchange) return;
+    const int nblk = len > 0 && len <= a.max_tokens ? (len + kBlock - 1) / kBlock : 0;
     parts = min(parts, (nblk + a.blocks_per_split - 1) / a.blocks_per_split);
-    if (a.skip_single && parts == 1) return;  // written by the decode kernel
+    if (a.skip_single && parts == 1 && !exchange) return;  // written by the decode kernel
   }
   const int64_t ml_s = a.ml_s ? a.ml_s : kHq * 2;
   const int64_t ml_b = a.ml_b ? a.ml_b : a.num_parts * ml_s;
@@ -628,6 +732,10 @@ __global__ void __launch_bounds__(kCombineGroups * kDim) combine_kernel(const Co
     const float c = ex2(sm[g] - MM);
     LL = fmaf(sl[g], c, LL);
     OO = fmaf(so[g][d], c, OO);
+  }
+  if (exchange) {
+    xchg_merge(a.x, b, h, d, MM, LL, OO);  // this rank's merged state to every rank; world merge
+    return;
   }
   const int64_t oi = ((int64_t)b * kHq + h) * kDim + d;
   if (a.out) a.out[oi] = static_cast<uint16_t>(bf16_bits(LL > 0.f ? OO / LL : 0.f));
@@ -836,9 +944,9 @@ __device__ __forceinline__ void step_producer(const StepArgs &a, StepTail *tail,
         mask &= mask - 1;
         for (int i = lane; i < kHq * kDim; i += 32) {
           if (a.direct_out) a.out[(int64_t)e * kHq * kDim + i] = 0;
-          else a.state_o[(int64_t)e * kHq * kDim + i] = 0.f;
+          else if (a.state_o) a.state_o[(int64_t)e * kHq * kDim + i] = 0.f;
         }
-        if (!a.direct_out && lane < kHq) {
+        if (!a.direct_out && a.state_ml && lane < kHq) {
           a.state_ml[((int64_t)e * kHq + lane) * 2] = -1.0e30f;
           a.state_ml[((int64_t)e * kHq + lane) * 2 + 1] = 0.f;
         }
@@ -1971,18 +2079,23 @@ extern "C" int b2_combine(const float *part_ml, const float *part_o, int32_t num
 
 extern "C" int b2_decode_step_counters(int32_t batch) { return batch < 0 ? 0 : 2 + batch * kHkv; }
 
-extern "C" int b2_decode_step(const uint16_t *qkv, int64_t row_stride, const uint16_t *gamma_q,
-                              const uint16_t *gamma_k, float eps, const uint16_t *rope_cos,
-                              const uint16_t *rope_sin, int32_t rope_rows, const int32_t *past_lens,
-                              const int32_t *seq_lens, const int32_t *block_tables, int32_t max_blocks_per_seq,
-                              uint16_t *k_pool, uint16_t *v_pool, int32_t num_blocks, int32_t batch,
-                              int32_t blocks_per_split, float scale, int32_t mode, uint16_t *out,
-                              uint16_t *q_out, float *state_ml, float *state_o, float *part_ml, float *part_o,
-                              int32_t *counters, int32_t max_ctas, int32_t *dev_err, void *stream) {
+namespace {
+
+// The decode step; with `x` (a multi-GPU exchange), the splits are always
+// merged by the combine kernel, which exchanges the merged state with the
+// other ranks and writes the world's context into out.
+int decode_step_impl(const uint16_t *qkv, int64_t row_stride, const uint16_t *gamma_q, const uint16_t *gamma_k,
+                     float eps, const uint16_t *rope_cos, const uint16_t *rope_sin, int32_t rope_rows,
+                     const int32_t *past_lens, const int32_t *seq_lens, const int32_t *block_tables,
+                     int32_t max_blocks_per_seq, uint16_t *k_pool, uint16_t *v_pool, int32_t num_blocks,
+                     int32_t batch, int32_t blocks_per_split, float scale, int32_t mode, uint16_t *out,
+                     uint16_t *q_out, float *state_ml, float *state_o, float *part_ml, float *part_o,
+                     int32_t *counters, int32_t max_ctas, int32_t *dev_err, void *stream, const XchgArgs *x) {
   if (batch < 0) return fail(B2_ERR_ARG, "batch must be >= 0 (got %d)", batch);
   if (batch == 0) return ok();
   if (!qkv || !past_lens || !block_tables || !k_pool || !v_pool || !part_ml || !part_o || !counters || !dev_err)
     return fail(B2_ERR_ARG, "null pointer argument");
+  if (x && (!out || state_o || state_ml)) return fail(B2_ERR_ARG, "an exchange writes out and no state");
   if (!out && !state_o) return fail(B2_ERR_ARG, "one of out or state_o is required");
   if ((state_o == nullptr) != (state_ml == nullptr)) return fail(B2_ERR_ARG, "state_ml and state_o go together");
   if (mode & ~(B2_NORM_QK | B2_ROPE_QK | B2_STORE_KV)) return fail(B2_ERR_ARG, "unknown mode bits 0x%x", mode);
@@ -2011,15 +2124,16 @@ extern "C" int b2_decode_step(const uint16_t *qkv, int64_t row_stride, const uin
   rc = make_pool_map(&mv, v_pool, num_blocks);
   if (rc) return rc;
   if (!step_smem_ready()) return fail(B2_ERR_CUDA, "cannot set the decode-step kernel's shared memory size");
-  const int direct_out = state_o == nullptr;
+  const int direct_out = state_o == nullptr && !x;
   // One warp merges a (sequence, kv head)'s splits serially: right for a
   // handful of splits; long single sequences with many splits are merged by
-  // the parallel combine kernel instead.
-  const int merge_here = splits <= kMergeInKernelSplits;
+  // the parallel combine kernel instead (always, with an exchange).
+  const int merge_here = splits <= kMergeInKernelSplits && !x;
   StepArgs a{qkv, row_stride, gamma_q, gamma_k, eps, rope_cos, rope_sin, rope_rows, past_lens, seq_lens,
              block_tables, max_blocks_per_seq, k_pool, v_pool, num_blocks, batch, blocks_per_split,
              static_cast<int>(splits), static_cast<int>(total), direct_out, merge_here,
-             scale * 1.4426950408889634f, mode, out, q_out, state_ml, state_o, part_ml, part_o, counters, dev_err};
+             scale * 1.4426950408889634f, mode, x ? nullptr : out, q_out, state_ml, state_o, part_ml, part_o,
+             counters, dev_err};
   int64_t ctas = static_cast<int64_t>(sm_count()) * 3;
   if (max_ctas > 0 && max_ctas < ctas) ctas = max_ctas;
   if (ctas > total) ctas = total;
@@ -2051,9 +2165,11 @@ extern "C" int b2_decode_step(const uint16_t *qkv, int64_t row_stride, const uin
   if (rc || merge_here) return rc;
   // Many splits: merge them with the parallel combine kernel, launched as a
   // programmatic dependent so that its launch overlaps the decode tail.
-  CombineArgs c{part_ml, part_o, static_cast<int>(splits), seq_lens ? seq_lens : past_lens, blocks_per_split, out,
-                state_ml, state_o, seq_lens ? 0 : 1, direct_out, static_cast<int>(splits) * blocks_per_split * kBlock,
-                0, 0, 0, 0, combine_groups(static_cast<int>(splits))};
+  CombineArgs c{part_ml, part_o, static_cast<int>(splits), seq_lens ? seq_lens : past_lens, blocks_per_split,
+                x ? nullptr : out, state_ml, state_o, seq_lens ? 0 : 1, direct_out,
+                static_cast<int>(splits) * blocks_per_split * kBlock, 0, 0, 0, 0,
+                combine_groups(static_cast<int>(splits))};
+  if (x) c.x = *x;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(batch), kHq);
   cfg.blockDim = dim3(c.groups * kDim);
@@ -2066,6 +2182,47 @@ extern "C" int b2_decode_step(const uint16_t *qkv, int64_t row_stride, const uin
     return fail(B2_ERR_CUDA, "combine_kernel launch failed: %s", cudaGetErrorString(e));
   }
   return launch_status("combine_kernel (decode step)");
+}
+
+}  // namespace
+
+extern "C" int b2_decode_step(const uint16_t *qkv, int64_t row_stride, const uint16_t *gamma_q,
+                              const uint16_t *gamma_k, float eps, const uint16_t *rope_cos,
+                              const uint16_t *rope_sin, int32_t rope_rows, const int32_t *past_lens,
+                              const int32_t *seq_lens, const int32_t *block_tables, int32_t max_blocks_per_seq,
+                              uint16_t *k_pool, uint16_t *v_pool, int32_t num_blocks, int32_t batch,
+                              int32_t blocks_per_split, float scale, int32_t mode, uint16_t *out,
+                              uint16_t *q_out, float *state_ml, float *state_o, float *part_ml, float *part_o,
+                              int32_t *counters, int32_t max_ctas, int32_t *dev_err, void *stream) {
+  return decode_step_impl(qkv, row_stride, gamma_q, gamma_k, eps, rope_cos, rope_sin, rope_rows, past_lens, seq_lens,
+                          block_tables, max_blocks_per_seq, k_pool, v_pool, num_blocks, batch, blocks_per_split,
+                          scale, mode, out, q_out, state_ml, state_o, part_ml, part_o, counters, max_ctas, dev_err,
+                          stream, nullptr);
+}
+
+extern "C" int b2_decode_step_exchange(const uint16_t *qkv, int64_t row_stride, const uint16_t *gamma_q,
+                                       const uint16_t *gamma_k, float eps, const uint16_t *rope_cos,
+                                       const uint16_t *rope_sin, int32_t rope_rows, const int32_t *past_lens,
+                                       const int32_t *seq_lens, const int32_t *block_tables,
+                                       int32_t max_blocks_per_seq, uint16_t *k_pool, uint16_t *v_pool,
+                                       int32_t num_blocks, int32_t batch, int32_t blocks_per_split, float scale,
+                                       int32_t mode, uint16_t *out, uint16_t *q_out, float *part_ml, float *part_o,
+                                       int32_t *counters, int32_t max_ctas, void *const *areas, int32_t world,
+                                       int32_t rank, int32_t *dev_err, void *stream) {
+  if (batch > 65535) return fail(B2_ERR_ARG, "batch must be <= 65535");
+  if (world < 1 || world > kXMaxWorld) return fail(B2_ERR_ARG, "world must be in [1, %d]", kXMaxWorld);
+  if (rank < 0 || rank >= world) return fail(B2_ERR_ARG, "rank must be in [0, world)");
+  if (!areas || !dev_err) return fail(B2_ERR_ARG, "null pointer argument");
+  XchgArgs x{nullptr, nullptr, batch, world, rank, out, dev_err, {}};
+  for (int r = 0; r < world; ++r) {
+    if (!areas[r] || (reinterpret_cast<uintptr_t>(areas[r]) & 15))
+      return fail(B2_ERR_ARG, "exchange area %d is null or not 16-byte aligned", r);
+    x.area[r] = static_cast<char *>(areas[r]);
+  }
+  return decode_step_impl(qkv, row_stride, gamma_q, gamma_k, eps, rope_cos, rope_sin, rope_rows, past_lens, seq_lens,
+                          block_tables, max_blocks_per_seq, k_pool, v_pool, num_blocks, batch, blocks_per_split,
+                          scale, mode, out, q_out, nullptr, nullptr, part_ml, part_o, counters, max_ctas, dev_err,
+                          stream, &x);
 }
 
 extern "C" int b2_merge_states(const float *states, int32_t num_parts, int32_t batch, uint16_t *out,
@@ -2276,104 +2433,15 @@ extern "C" int b2_decode_step_host_join(void *stream) {
 
 namespace {
 
-// ------------------------------------------------------------------ multi-GPU state exchange (NVLink P2P)
-
-// One sequence's KV cache split along the token axis over `world` GPUs: every
-// rank holds a partial softmax state (max, sum, unnormalised output) per
-// (sequence, query head).  Instead of an all-gather collective followed by a
-// merge launch, one kernel writes this rank's state straight into every
-// rank's exchange area over NVLink (peer pointers from CUDA IPC) and merges
-// the world's states once they have arrived in its own area.
-//
-// Every value travels as one 8-byte word {float bits, tag}, written with a
-// single 8-byte store, where tag = step number + 1 (the low-latency protocol
-// of collective libraries): a reader polls the words themselves until their
-// tags show the current step, so no fence or separate flag is needed.
-// Exchange area (every rank, same layout; zeroed before first use):
-//   uint2 word[2 slots][world][batch][16][kXState]   (m, l, 2 unused, o[64])
-//   int   step[batch][16]                            (local step counter)
-// Steps alternate slots.  A rank can be at most one step ahead of another
-// (its next merge needs the other's words of that step, written after the
-// other's previous merge finished reading), so a slot is never overwritten
-// while it is read.
-
-constexpr int kXState = 4 + kDim;
-constexpr int kXMaxWorld = B2_XCHG_MAX_WORLD;
-constexpr uint64_t kXWaitNs = 5000000000ull;  // 5 s, then B2_DEV_TIMEOUT
-
-struct XchgArgs {
-  const float *state_ml;  // [batch][16][2]
-  const float *state_o;   // [batch][16][64]
-  int batch, world, rank;
-  uint16_t *out;  // [batch][16][64]
-  int32_t *err;
-  char *area[kXMaxWorld];  // rank r's exchange area as mapped on this GPU
-};
-
-__host__ __device__ constexpr int64_t x_words(int world, int batch) {
-  return 2ll * world * batch * kHq * kXState;
-}
-
-__device__ __forceinline__ void st_word(uint2 *p, float v, uint32_t tag) {
-  asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(__float_as_uint(v)), "r"(tag)
-               : "memory");
-}
-
-__device__ __forceinline__ uint2 ld_word(const uint2 *p) {
-  uint2 w;
-  asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(w.x), "=r"(w.y) : "l"(p) : "memory");
-  return w;
-}
+// ------------------------------------------------------------------ multi-GPU state exchange: standalone kernel, IPC
 
 // grid (batch, 16 heads), block 64 threads (one per output dim).
 __global__ void __launch_bounds__(kDim) exchange_merge_kernel(const XchgArgs a) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  const int b = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
-  const int bh = b * kHq + h;
-  const uint2 *own = reinterpret_cast<const uint2 *>(a.area[a.rank]);
-  int32_t *steps = reinterpret_cast<int32_t *>(reinterpret_cast<uint2 *>(a.area[a.rank]) + x_words(a.world, a.batch));
-  const int32_t step = steps[bh];
-  const int slot = step & 1;
-  const uint32_t tag = static_cast<uint32_t>(step) + 1u;
-  const float m = a.state_ml[bh * 2], l = a.state_ml[bh * 2 + 1], o = a.state_o[(int64_t)bh * kDim + d];
-  const int64_t mine = (((static_cast<int64_t>(slot) * a.world + a.rank) * a.batch + b) * kHq + h) * kXState;
-  for (int r = 0; r < a.world; ++r) {
-    uint2 *dst = reinterpret_cast<uint2 *>(a.area[r]) + mine;
-    st_word(dst + 4 + d, o, tag);
-    if (d == 0) {
-      st_word(dst, m, tag);
-      st_word(dst + 1, l, tag);
-    }
-  }
-  float M = -1.0e30f, L = 0.f, O = 0.f;
-  bool ok = true;
-  const uint64_t t0 = global_ns();
-  for (int r = 0; r < a.world && ok; ++r) {
-    const uint2 *src = own + (((static_cast<int64_t>(slot) * a.world + r) * a.batch + b) * kHq + h) * kXState;
-    uint2 wm, wl, wo;
-    for (;;) {
-      wm = ld_word(src);
-      wl = ld_word(src + 1);
-      wo = ld_word(src + 4 + d);
-      if (wm.y == tag && wl.y == tag && wo.y == tag) break;
-      if (global_ns() - t0 > kXWaitNs) {
-        atomicOr(a.err, B2_DEV_TIMEOUT);
-        ok = false;
-        break;
-      }
-    }
-    if (!ok) break;
-    const float ms = __uint_as_float(wm.x), ls = __uint_as_float(wl.x), os = __uint_as_float(wo.x);
-    const float nm = fmaxf(M, ms);
-    const float c1 = ex2(M - nm), c2 = ex2(ms - nm);
-    L = L * c1 + ls * c2;
-    O = O * c1 + os * c2;
-    M = nm;
-  }
-  if (ok) a.out[(int64_t)bh * kDim + d] = static_cast<uint16_t>(bf16_bits(L > 0.f ? O / L : 0.f));
-  __syncthreads();
-  if (d == 0) steps[bh] = step + 1;
+  const int bh = blockIdx.x * kHq + blockIdx.y, d = threadIdx.x;
+  xchg_merge(a, blockIdx.x, blockIdx.y, d, a.state_ml[bh * 2], a.state_ml[bh * 2 + 1],
+             a.state_o[(int64_t)bh * kDim + d]);
 }
 
 using PFN_memGetAddressRange = CUresult (*)(CUdeviceptr *, size_t *, CUdeviceptr);

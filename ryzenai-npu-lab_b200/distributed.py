@@ -247,26 +247,36 @@ class LongContextDecode:
 
     def step(self, qkv: torch.Tensor, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
         """qkv: bf16 [1, >= 2048] raw projections of the new token.  Lengths come
-        from set_lengths(); the call is capturable in a CUDA graph (NCCL included)."""
+        from set_lengths(); the call is capturable in a CUDA graph (NCCL included).
+        With the P2P exchange the whole step is one call (b2_decode_step_exchange):
+        the step kernel, then the combine kernel merging this rank's splits and
+        exchanging the result with the other ranks over peer memory."""
+        if self.exchange == "p2p":
+            self._run(qkv, stream, exchange=(self.peer.areas, self.world, self.rank))
+            return self.out[0]
         self.partial(qkv, stream)
         return self.merge(stream)
 
     def partial(self, qkv: torch.Tensor, stream: torch.cuda.Stream | None = None) -> None:
         """This rank's part, one fused launch (b2_decode_step): q/k norm + RoPE at
         the global position (and the append on the last rank), split-KV
-        attention over the local tokens, merged into one local fp32 state."""
+        attention over the local tokens, merged into one local fp32 state (the
+        context itself for a world of one)."""
+        self._run(qkv, stream)
+
+    def _run(self, qkv: torch.Tensor, stream: torch.cuda.Stream | None, exchange=None) -> None:
         mode = _lib.B2_NORM_QK | _lib.B2_ROPE_QK | (_lib.B2_STORE_KV if self.is_tail else 0)
         kp, vp = self.cache.pool(0)
         # RoPE rows are read at past_lens; offsetting the table by this rank's
         # first global token turns the local slot into the global position.
-        direct = self.exchange == "direct"
+        direct = self.exchange == "direct" or exchange is not None
         decode_step(qkv, self.past, k_pool=kp, v_pool=vp, block_tables=self.tables, blocks_per_split=self.bps,
                     out=self.out if direct else None, part_ml=self.part_ml, part_o=self.part_o,
                     counters=self.counters, dev_err=self.dev_err, gamma_q=self.gamma_q, gamma_k=self.gamma_k,
                     cos=self.cos_all[self.start:], sin=self.sin_all[self.start:], q_out=self.q,
                     seq_lens=None if self.is_tail else self.seq,
                     state_ml=None if direct else self.state_ml, state_o=None if direct else self.state_o,
-                    mode=mode, eps=self.eps, max_ctas=self.max_ctas, stream=stream)
+                    mode=mode, eps=self.eps, max_ctas=self.max_ctas, stream=stream, exchange=exchange)
 
     def merge(self, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
         """Exchange the local states and merge them into the context: one P2P
