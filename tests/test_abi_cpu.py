@@ -56,3 +56,32 @@ def test_version_and_error_text_without_gpu():
 def test_library_lives_in_tree():
     lib = load_pkg("_lib")
     assert pathlib.Path(lib.LIB_PATH).parent.name == "ryzenai-npu-lab_b200"
+
+
+def test_decode_step_exchange_argument_checks_without_gpu():
+    """The torch wrapper refuses an exchange without an output or with states
+    (host checks before any launch), and the C entry rejects a bad world."""
+    import torch
+    attn = load_pkg("attention")
+    lib = load_pkg("_lib")
+    bf, i32 = torch.bfloat16, torch.int32
+    qkv = torch.zeros(1, 2048, dtype=bf)
+    past = torch.zeros(1, dtype=i32)
+    pool = torch.zeros(2, 8, 64, 64, dtype=bf)
+    tables = torch.zeros(1, 2, dtype=i32)
+    part_ml = torch.zeros(1, 2, 16, 2)
+    part_o = torch.zeros(1, 2, 16, 64)
+    counters = torch.zeros(10, dtype=i32)
+    err = torch.zeros(1, dtype=i32)
+    kw = dict(k_pool=pool, v_pool=pool, block_tables=tables, blocks_per_split=1, part_ml=part_ml, part_o=part_o,
+              counters=counters, dev_err=err, mode=lib.B2_STORE_KV, exchange=(None, 2, 0))
+    import pytest
+    with pytest.raises(ValueError, match="exchange"):
+        attn.decode_step(qkv, past, out=None, **kw)
+    with pytest.raises(ValueError, match="exchange"):
+        attn.decode_step(qkv, past, out=torch.zeros(1, 16, 64, dtype=bf), state_ml=torch.zeros(1, 16, 2),
+                         state_o=torch.zeros(1, 16, 64), **kw)
+    rc = lib.load().b2_decode_step_exchange(None, 2048, None, None, ctypes.c_float(1e-5), None, None, 0, None, None,
+                                            None, 1, None, None, 1, 1, 1, ctypes.c_float(0.125), 0, None, None,
+                                            None, None, None, 0, None, 9, 0, None, None)
+    assert rc == lib.B2_ERR_ARG and "world" in lib.last_error()
