@@ -664,13 +664,15 @@ int combine_groups(int num_parts) {
 }
 
 // grid (batch, 16 heads), block (groups x 64 dims).  Group g merges parts
-// g, g + groups, ... with a running (max, sum, output); the group states
-// are then merged in shared memory, so a sequence split into hundreds of
-// parts is still merged by many threads in one pass.
+// g, g + groups, ... with a running (max, sum, output), loading four parts
+// per round; the group states are then merged in shared memory, so a
+// sequence split into hundreds of parts is still merged by many threads.
+// With an exchange (a.x.world > 0) group 0 then runs xchg_merge with the
+// merged state instead of writing it.
 // When launched as a programmatic dependent of the decode-step kernel it may
 // start early; griddepcontrol.wait holds it until that kernel has completed
 // and its memory is visible (a no-op for an ordinary launch).
-constexpr int kCombineGroups = 16;
+constexpr int kCombineGroups = 16;  // upper bound of the arrays; combine_groups() uses at most 8
 
 __global__ void __launch_bounds__(kCombineGroups * kDim) combine_kernel(const CombineArgs a) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
