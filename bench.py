@@ -66,6 +66,8 @@ def parse():
                    help="run append, decode and combine as three launches instead of the fused kernel")
     p.add_argument("--max-ctas", type=int, default=0, help="cap on the fused kernel's persistent grid")
     p.add_argument("--chunk", type=int, default=64, help="prefill: new tokens per sequence")
+    p.add_argument("--prefill-bps", type=int, default=-1,
+                   help="prefill: blocks per key split (-1 = heuristic, 0 = no split)")
     p.add_argument("--config", choices=["c3", "c4", "c2", "c5", "prefill"], default="c3",
                    help="c3: batched paged decode (default); c4: one long sequence split over the GPUs; "
                         "c2: 6 attention layers x 64 consecutive decode steps of one sequence; "
@@ -733,7 +735,8 @@ def run_prefill(args):
 
     def step():
         attn.prefill(qkv, past, k_pool=kp, v_pool=vp, block_tables=tables, gamma_q=gq, gamma_k=gk, cos=cos,
-                     sin=sin, dev_err=err, out=out, q_out=q_out)
+                     sin=sin, dev_err=err, out=out, q_out=q_out,
+                     blocks_per_split=None if args.prefill_bps < 0 else args.prefill_bps)
 
     with torch.cuda.stream(stream):
         for _ in range(max(args.warmup, 1)):

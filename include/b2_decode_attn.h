@@ -348,6 +348,23 @@ int b2_prefill_attn(const uint16_t *q, const uint16_t *k_pool,
                     uint16_t *out, int32_t *dev_err, void *stream);
 
 /*
+ * b2_prefill_attn with the keys of every query tile split in ranges of
+ * blocks_per_split 64-token blocks over more CTAs (for short chunks the
+ * longest sequence otherwise bounds the launch): each CTA writes the partial
+ * softmax state of its rows into part_ml [nsplit][batch][tokens][16][2] and
+ * part_o [nsplit][batch][tokens][16][64] (fp32, nsplit = ceil(max_blocks_per_seq
+ * / blocks_per_split)), and the combine kernel merges them into out (rows past
+ * a sequence's chunk become 0).  batch * nsplit <= 65535.
+ */
+int b2_prefill_attn_split(const uint16_t *q, const uint16_t *k_pool,
+                          const uint16_t *v_pool, int32_t num_blocks,
+                          const int32_t *block_tables, int32_t max_blocks_per_seq,
+                          const int32_t *past_lens, const int32_t *chunk_lens,
+                          int32_t tokens, int32_t batch, float scale,
+                          int32_t blocks_per_split, float *part_ml, float *part_o,
+                          uint16_t *out, int32_t *dev_err, void *stream);
+
+/*
  * Allocation-free decode: b2_decode_attn followed by b2_combine, with the
  * partial softmax states kept in a static device array inside this library
  * instead of caller-provided part_ml / part_o buffers.  It has no counterpart

@@ -100,6 +100,13 @@ SIGNATURES = {
         _p,                  # stream
     ]),
     "b2_decode_step_host_join": (ctypes.c_int, [_p]),
+    "b2_prefill_attn_split": (ctypes.c_int, [
+        _p, _p, _p, _i32,    # q, k_pool, v_pool, num_blocks
+        _p, _i32,            # block_tables, max_blocks_per_seq
+        _p, _p, _i32, _i32,  # past_lens, chunk_lens, tokens, batch
+        _f32, _i32,          # scale, blocks_per_split
+        _p, _p, _p, _p, _p,  # part_ml, part_o, out, dev_err, stream
+    ]),
     "b2_decode_step_exchange": (ctypes.c_int, [
         _p, ctypes.c_int64,  # qkv, row_stride
         _p, _p, _f32,        # gamma_q, gamma_k, eps

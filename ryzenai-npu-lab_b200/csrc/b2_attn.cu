@@ -1483,7 +1483,24 @@ struct PrefillArgs {
   float scale_log2;
   uint16_t *out;  // [batch][tokens][16][64]
   int32_t *err;
+  // split-KV (bps > 0): blocks [split * bps, (split + 1) * bps) of each tile,
+  // partial states to part_ml [nsplit][batch][tokens][16][2] (max in log2
+  // units, sum) and part_o [nsplit][batch][tokens][16][64] (unnormalised)
+  int bps, nsplit;
+  float *part_ml, *part_o;
 };
+
+// Split-KV prefill: the partial state of (split, sequence b, token row, head)
+__device__ __forceinline__ void pf_store_part(const PrefillArgs &a, int split, int b, int row, int head, float m,
+                                              float l, const float *o) {
+  const int64_t r = ((static_cast<int64_t>(split) * gridDim.z / a.nsplit + b) * a.tokens + row) * kHq + head;
+  a.part_ml[r * 2] = m;
+  a.part_ml[r * 2 + 1] = l;
+  float4 *dst = reinterpret_cast<float4 *>(a.part_o + r * kDim);
+#pragma unroll
+  for (int c = 0; c < kDim; c += 4) dst[c >> 2] = o ? make_float4(o[c], o[c + 1], o[c + 2], o[c + 3])
+                                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+}
 
 // Shared-memory matrix descriptor for tcgen05.mma: 128-byte swizzle, rows of
 // 128 bytes, 8-row groups 1024 bytes apart (SBO); LBO as given (unused for a
@@ -1569,12 +1586,14 @@ __global__ void __launch_bounds__(kPfThreads, 2)
     prefill_attn_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                         const PrefillArgs a) {
   const int tile = blockIdx.x, kvh = blockIdx.y;
-  int b = blockIdx.z;
-  if (gridDim.z <= kPfSortMax) {
-    // sequence of rank blockIdx.z by total keys (past + chunk), descending
+  const int nsplit = a.bps > 0 ? a.nsplit : 1;
+  const int zb = blockIdx.z / nsplit, split = blockIdx.z % nsplit;  // splits of a sequence are adjacent
+  const int nb = gridDim.z / nsplit;
+  int b = zb;
+  if (nb <= kPfSortMax) {
+    // sequence of rank zb by total keys (past + chunk), descending
     __shared__ int keys[kPfSortMax];
     __shared__ int chosen;
-    const int nb = gridDim.z;
     for (int i = threadIdx.x; i < nb; i += blockDim.x)
       keys[i] = a.past_lens[i] + (a.chunk_lens ? a.chunk_lens[i] : a.tokens);
     __syncthreads();
@@ -1582,7 +1601,7 @@ __global__ void __launch_bounds__(kPfThreads, 2)
       const int ki = keys[i];
       int rank = 0;
       for (int j2 = 0; j2 < nb; ++j2) rank += (keys[j2] > ki) || (keys[j2] == ki && j2 < i);
-      if (rank == (int)blockIdx.z) chosen = i;
+      if (rank == zb) chosen = i;
     }
     __syncthreads();
     b = chosen;
@@ -1590,14 +1609,32 @@ __global__ void __launch_bounds__(kPfThreads, 2)
   const int past = a.past_lens[b];
   const int T = a.chunk_lens ? a.chunk_lens[b] : a.tokens;
   const int t0 = tile * 64;
-  if (t0 >= T) return;
+  if (t0 >= T) {
+    if (a.bps > 0)  // split-KV: empty states for the rows of a tile past the chunk
+      for (int i = threadIdx.x; i < 128; i += blockDim.x) {
+        const int t = i & 63, hl = i >> 6;
+        if (t0 + t < a.tokens) pf_store_part(a, split, b, t0 + t, 2 * kvh + hl, -1.0e30f, 0.f, nullptr);
+      }
+    return;
+  }
   if (past < 0 || T > a.tokens || past + T > a.max_blocks * kBlock) {
     if (threadIdx.x == 0 && tile == 0 && kvh == 0) atomicOr(a.err, B2_DEV_BAD_LENGTH);
     return;
   }
   const int rows_t = min(64, T - t0);
   const int last_key = past + t0 + rows_t - 1;  // the tile's highest query position
-  const int nblk = last_key / kBlock + 1;
+  const int nblk_all = last_key / kBlock + 1;
+  // this CTA's blocks [j0, j0 + nblk): all of them, or one split's
+  const int j0 = a.bps > 0 ? split * a.bps : 0;
+  const int nblk = a.bps > 0 ? min(nblk_all - j0, a.bps) : nblk_all;
+  if (nblk <= 0) {
+    // a split past the tile's last key: empty states for the tile's rows
+    for (int i = threadIdx.x; i < 128; i += blockDim.x) {
+      const int t = i & 63, hl = i >> 6;
+      if (t0 + t < a.tokens) pf_store_part(a, split, b, t0 + t, 2 * kvh + hl, -1.0e30f, 0.f, nullptr);
+    }
+    return;
+  }
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t *sQ = reinterpret_cast<uint8_t *>(
@@ -1670,7 +1707,7 @@ __global__ void __launch_bounds__(kPfThreads, 2)
           break;
         }
         if (tail->abort) break;
-        int blk = tbl[j];
+        int blk = tbl[j0 + j];
         if (blk < 0 || blk >= a.num_blocks) {
           if (is_k) atomicOr(a.err, B2_DEV_BAD_BLOCK);
           blk = 0;
@@ -1762,7 +1799,7 @@ __global__ void __launch_bounds__(kPfThreads, 2)
         ok = false;
         break;
       }
-      const int key0 = j * kBlock;
+      const int key0 = (j0 + j) * kBlock;
       if (key0 + kBlock - 1 > last_key) {
         // this thread's share of zeroing the V rows past the tile (below)
         if (!warp_wait(smem_u32(&tail->vfull[s]), (j / kPfStages) & 1)) {
@@ -1790,7 +1827,7 @@ __global__ void __launch_bounds__(kPfThreads, 2)
       mbar_arrive(smem_u32(&tail->sfree[j & 1]));  // S_j is in registers: its buffer may be reused
       // scores of this row, masked: causal within the chunk, nothing past the
       // tile; max in 8 independent chains
-      const int key0 = j * kBlock;
+      const int key0 = (j0 + j) * kBlock;
       const int lim = row_ok ? qpos - key0 : -1;  // columns c <= lim are visible
       float bm8[8];
 #pragma unroll
@@ -1879,7 +1916,12 @@ __global__ void __launch_bounds__(kPfThreads, 2)
       tmem_fence_after();
       float o[64];
       tmem_ld64(trow + 128, o);
-      if (row_ok && !tail->abort) {
+      if (a.bps > 0 && !tail->abort) {
+        // split-KV: the partial state (rows past the chunk get empty states)
+        if (t0 + t < a.tokens)
+          pf_store_part(a, split, b, t0 + t, 2 * kvh + hl, row_ok ? m : -1.0e30f, row_ok ? l : 0.f,
+                        row_ok ? o : nullptr);
+      } else if (row_ok && !tail->abort) {
         const float inv = 1.0f / l;
         uint4 *dst =
             reinterpret_cast<uint4 *>(a.out + (((int64_t)b * a.tokens + t0 + t) * kHq + 2 * kvh + hl) * kDim);
@@ -2311,6 +2353,51 @@ extern "C" int b2_prefill_attn(const uint16_t *q, const uint16_t *k_pool, const 
   const dim3 grid((tokens + 63) / 64, kHkv, batch);
   prefill_attn_kernel<<<grid, kPfThreads, kPfSmem, static_cast<cudaStream_t>(stream)>>>(mk, mv, a);
   return launch_status("prefill_attn_kernel");
+}
+
+extern "C" int b2_prefill_attn_split(const uint16_t *q, const uint16_t *k_pool, const uint16_t *v_pool,
+                                     int32_t num_blocks, const int32_t *block_tables, int32_t max_blocks_per_seq,
+                                     const int32_t *past_lens, const int32_t *chunk_lens, int32_t tokens,
+                                     int32_t batch, float scale, int32_t blocks_per_split, float *part_ml,
+                                     float *part_o, uint16_t *out, int32_t *dev_err, void *stream) {
+  if (batch < 0 || tokens < 0) return fail(B2_ERR_ARG, "batch and tokens must be >= 0");
+  if (batch == 0 || tokens == 0) return ok();
+  if (!q || !k_pool || !v_pool || !block_tables || !past_lens || !out || !dev_err || !part_ml || !part_o)
+    return fail(B2_ERR_ARG, "null pointer argument");
+  if (num_blocks <= 0 || static_cast<int64_t>(num_blocks) * kHkv * kBlock >= (int64_t(1) << 31))
+    return fail(B2_ERR_ARG, "num_blocks must be in [1, 2^22) (got %d)", num_blocks);
+  if (max_blocks_per_seq <= 0) return fail(B2_ERR_ARG, "max_blocks_per_seq must be positive");
+  if (blocks_per_split <= 0) return fail(B2_ERR_ARG, "blocks_per_split must be positive");
+  const int64_t nsplit = (static_cast<int64_t>(max_blocks_per_seq) + blocks_per_split - 1) / blocks_per_split;
+  if (static_cast<int64_t>(batch) * nsplit > 65535) return fail(B2_ERR_ARG, "batch x splits must be <= 65535");
+  if (static_cast<int64_t>(batch) * tokens * nsplit * kHq * kDim >= (int64_t(1) << 40))
+    return fail(B2_ERR_ARG, "partial-state buffers too large");
+  if (!aligned16(q) || !aligned16(out) || !aligned16(k_pool) || !aligned16(v_pool) || !aligned16(part_o) ||
+      (reinterpret_cast<uintptr_t>(part_ml) & 7))
+    return fail(B2_ERR_ARG, "q, out, the pools and part_o must be 16-byte aligned, part_ml 8-byte aligned");
+  if (!(scale > 0.f)) return fail(B2_ERR_ARG, "scale must be positive");
+  CUtensorMap mk, mv;
+  int rc = make_pool_map(&mk, k_pool, num_blocks);
+  if (rc) return rc;
+  rc = make_pool_map(&mv, v_pool, num_blocks);
+  if (rc) return rc;
+  if (!prefill_smem_ready()) return fail(B2_ERR_CUDA, "cannot set the prefill kernel's shared memory size");
+  PrefillArgs a{q, block_tables, max_blocks_per_seq, past_lens, chunk_lens, tokens, num_blocks,
+                scale * 1.4426950408889634f, out, dev_err, blocks_per_split, static_cast<int>(nsplit),
+                part_ml, part_o};
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const dim3 grid((tokens + 63) / 64, kHkv, static_cast<unsigned>(batch * nsplit));
+  prefill_attn_kernel<<<grid, kPfThreads, kPfSmem, st>>>(mk, mv, a);
+  rc = launch_status("prefill_attn_kernel (split)");
+  if (rc) return rc;
+  // merge the splits of every (sequence, token, head): rows b * tokens + t
+  const int64_t rows = static_cast<int64_t>(batch) * tokens;
+  if (rows > 0x7fffffff) return fail(B2_ERR_ARG, "batch x tokens too large");
+  const int64_t ml_s = rows * kHq * 2, o_s = rows * kHq * kDim;
+  CombineArgs c{part_ml, part_o, static_cast<int>(nsplit), nullptr, 1, out, nullptr, nullptr, 0, 0, 0,
+                kHq * 2, ml_s, kHq * kDim, o_s, combine_groups(static_cast<int>(nsplit))};
+  combine_kernel<<<dim3(static_cast<unsigned>(rows), kHq), c.groups * kDim, 0, st>>>(c);
+  return launch_status("combine_kernel (prefill splits)");
 }
 
 extern "C" int b2_decode_step_host(const uint16_t *qkv_host, const int32_t *past_host, uint16_t *out_host,

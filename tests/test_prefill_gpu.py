@@ -17,7 +17,7 @@ pytestmark = pytest.mark.gpu
 GOLDEN = pathlib.Path(__file__).resolve().parent / "golden"
 
 
-def _run_prefill(cuda, cache, qkv, past, chunk, gq, gk):
+def _run_prefill(cuda, cache, qkv, past, chunk, gq, gk, blocks_per_split=None):
     attn = load_pkg("attention")
     rope = load_pkg("rope")
     cos, sin = rope.rope_table(4096, device=cuda)
@@ -25,7 +25,7 @@ def _run_prefill(cuda, cache, qkv, past, chunk, gq, gk):
     err = torch.zeros(1, dtype=torch.int32, device=cuda)
     out = attn.prefill(qkv.to(cuda), torch.tensor(past, dtype=torch.int32, device=cuda), k_pool=kp, v_pool=vp,
                        block_tables=cache.block_tables(), gamma_q=gq.to(cuda), gamma_k=gk.to(cuda), cos=cos,
-                       sin=sin, dev_err=err,
+                       sin=sin, dev_err=err, blocks_per_split=blocks_per_split,
                        chunk_lens=None if chunk is None else torch.tensor(chunk, dtype=torch.int32, device=cuda))
     torch.cuda.synchronize()
     assert err.item() == 0
@@ -73,6 +73,37 @@ def test_prefill_ragged_batch(cuda):
     for i, (p, c) in enumerate(zip(past, chunk)):
         ctx, _, _ = orc.prefill_step(qkv[i, :c], hist[i][0], hist[i][1], p, w["q_gamma"], w["k_gamma"])
         check_close(out[i, :c], ctx, f"seq {i} past {p} chunk {c}")
+
+
+@pytest.mark.parametrize("bps", [1, 3, 16])
+def test_prefill_split_keys_ragged(cuda, bps):
+    """Keys split over CTAs (b2_prefill_attn_split) for short chunks: against
+    the oracle, with splits past a sequence's keys and chunks shorter than the
+    tile; rows past a chunk come out 0."""
+    past = [0, 63, 64, 500, 7, 2000]
+    chunk = [1, 5, 16, 3, 32, 4]
+    tmax = 32
+    w = orc.attention_weights(0)
+    cache, hist = build_batch(past, cuda, seed=23, capacity=max(p + c for p, c in zip(past, chunk)) + 1)
+    qkv = torch.stack([rand_qkv(tmax, 900 + i) for i in range(len(past))])     # [B, tmax, 2048]
+    out = _run_prefill(cuda, cache, qkv, past, chunk, w["q_gamma"], w["k_gamma"], blocks_per_split=bps)
+    for i, (p, c) in enumerate(zip(past, chunk)):
+        ctx, _, _ = orc.prefill_step(qkv[i, :c], hist[i][0], hist[i][1], p, w["q_gamma"], w["k_gamma"])
+        check_close(out[i, :c], ctx, f"seq {i} past {p} chunk {c} bps {bps}")
+        assert not out[i, c:].float().abs().any(), f"seq {i}: rows past the chunk not zero"
+
+
+def test_prefill_split_matches_unsplit(cuda):
+    """The same chunk with and without the key split: contexts within the
+    attention tolerance of each other (fp32 merges in another order)."""
+    past = [3000, 100, 4000]
+    w = orc.attention_weights(0)
+    outs = []
+    for bps in (0, 7):
+        cache, _ = build_batch(past, cuda, seed=24, capacity=max(past) + 9)
+        qkv = torch.stack([rand_qkv(8, 950 + i) for i in range(len(past))])
+        outs.append(_run_prefill(cuda, cache, qkv, past, None, w["q_gamma"], w["k_gamma"], blocks_per_split=bps))
+    check_close(outs[1], outs[0].float().cpu(), "split vs unsplit")
 
 
 def test_prefill_then_decode(cuda):
