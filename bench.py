@@ -3,8 +3,9 @@
     python bench.py --gpus N --steps K --warmup W [--impl b200|reference]
 
 Workload (batched paged decode): per GPU, 64 sequences
-with cached lengths uniform in [128, 8192] (one seeded global batch of
-64 x N sequences, sharded over the N GPUs by token count), K/V ~ N(0, 1)
+with cached lengths uniform in [128, 8192] (one seeded draw of 64 lengths;
+with N GPUs the global batch is N copies of it, sharded over the GPUs by token
+count, so every GPU does the one-GPU run's work), K/V ~ N(0, 1)
 bf16 in a pool of 64-token blocks handed out in shuffled order, 16 q heads /
 8 KV heads / head_dim 64.  One step = one decode token per sequence through
 one attention layer: fused q/k RMSNorm + RoPE + KV append, split-KV
@@ -165,14 +166,16 @@ class ClockSampler:
 # ----------------------------------------------------------------- workload
 
 def seq_lengths(args, rank: int, world: int = 1) -> list[int]:
-    """Cached lengths of this rank's sequences.  The global batch (batch per GPU
-    x world) is drawn from one seeded generator and sharded over the ranks by
-    token count (longest-first bin packing), so every GPU gets the same
-    amount of work; with one GPU it is the 64-sequence C3 batch."""
+    """Cached lengths of this rank's sequences.  The 64-sequence C3 batch is
+    drawn from one seeded generator; with N GPUs the global batch is N such
+    batches (the same lengths, different K/V contents per rank), sharded over
+    the ranks by token count (longest-first bin packing), so every GPU gets
+    exactly the work of the one-GPU run (weak scaling)."""
     g = torch.Generator().manual_seed(args.seed * 1000)
-    lengths = torch.randint(args.min_len, args.max_len + 1, (args.batch * world,), generator=g).tolist()
+    base = torch.randint(args.min_len, args.max_len + 1, (args.batch,), generator=g).tolist()
     if world == 1:
-        return lengths
+        return base
+    lengths = base * world
     dmod = importlib.import_module(PKG + ".distributed")
     return [lengths[i] for i in dmod.shard_sequences(lengths, world)[rank]]
 
