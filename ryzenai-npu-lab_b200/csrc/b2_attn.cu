@@ -22,6 +22,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "b2_decode_attn.h"
@@ -1949,14 +1950,14 @@ __global__ void __launch_bounds__(kPfThreads, 2)
 // ------------------------------------------------------------------ host helpers
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (!fn) {
+  static const PFN_cuTensorMapEncodeTiled_v12000 fn = [] {  // initialised once, thread-safe
     void *p = nullptr;
     cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
+      return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    return static_cast<PFN_cuTensorMapEncodeTiled_v12000>(nullptr);
+  }();
   return fn;
 }
 
@@ -1985,7 +1986,7 @@ int launch_status(const char *what) {
 
 bool decode_smem_ready() {
   // cudaFuncSetAttribute is per device; remember which devices are set up.
-  static bool done[128] = {};
+  static std::atomic<bool> done[128];  // per device; several host threads may launch at once
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return false;
   if (!done[dev]) {
@@ -1998,7 +1999,7 @@ bool decode_smem_ready() {
 }
 
 bool step_smem_ready() {
-  static bool done[128] = {};
+  static std::atomic<bool> done[128];  // per device; several host threads may launch at once
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return false;
   if (!done[dev]) {
@@ -2011,7 +2012,7 @@ bool step_smem_ready() {
 }
 
 int sm_count() {
-  static int count[128] = {};
+  static std::atomic<int> count[128];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return 148;
   if (!count[dev]) {
@@ -2284,7 +2285,7 @@ extern "C" int b2_merge_states(const float *states, int32_t num_parts, int32_t b
 }
 
 bool prefill_smem_ready() {
-  static bool done[128] = {};
+  static std::atomic<bool> done[128];  // per device; several host threads may launch at once
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return false;
   if (!done[dev]) {
@@ -2536,14 +2537,14 @@ __global__ void __launch_bounds__(kDim) exchange_merge_kernel(const XchgArgs a) 
 using PFN_memGetAddressRange = CUresult (*)(CUdeviceptr *, size_t *, CUdeviceptr);
 
 PFN_memGetAddressRange address_range_fn() {
-  static PFN_memGetAddressRange fn = nullptr;
-  if (!fn) {
+  static const PFN_memGetAddressRange fn = [] {  // initialised once, thread-safe
     void *p = nullptr;
     cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
     if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_memGetAddressRange>(p);
-  }
+      return reinterpret_cast<PFN_memGetAddressRange>(p);
+    return static_cast<PFN_memGetAddressRange>(nullptr);
+  }();
   return fn;
 }
 
