@@ -69,8 +69,9 @@ def parse():
     p.add_argument("--chunk", type=int, default=64, help="prefill: new tokens per sequence")
     p.add_argument("--prefill-bps", type=int, default=-1,
                    help="prefill: blocks per key split (-1 = heuristic, 0 = no split)")
-    p.add_argument("--config", choices=["c3", "c4", "c2", "c5", "prefill"], default="c3",
+    p.add_argument("--config", choices=["c3", "c4", "c1", "c2", "c5", "prefill"], default="c3",
                    help="c3: batched paged decode (default); c4: one long sequence split over the GPUs; "
+                        "c1: one attention layer (projections included) for one token at 512 cached tokens; "
                         "c2: 6 attention layers x 64 consecutive decode steps of one sequence; "
                         "c5: end-to-end greedy decode of the whole random-init model; "
                         "prefill: a chunk of --chunk new tokens per C3 sequence on the tcgen05 kernel")
@@ -574,6 +575,84 @@ def run_c4(args):
     torch.distributed.destroy_process_group()
 
 
+def run_c1(args):
+    """Config C1: one attention layer for one decode token of one sequence at
+    --context cached tokens (512 by default here): x -> q/k/v projections
+    (cuBLAS) -> fused step (norm + RoPE + append + attention) -> out_proj,
+    the C1 layer of the golden fixtures.  value = steps per second (latency =
+    ms_per_step); every step is the same token at the same position, so the
+    cache does not grow.  Replicas across GPUs."""
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    attn = importlib.import_module(PKG + ".attention")
+    pc = importlib.import_module(PKG + ".paged_cache")
+    from oracle import lfm2_attention as orc   # seeded weight generator (set-up only)
+    L = args.context if args.context != 131072 else 512
+    cache = pc.PagedKVCache(pc.blocks_for(L + 1), L + 1, device=dev, shuffle_seed=args.seed * 1000 + 17)
+    cache.add_sequence(L, capacity=L + 1)
+    gen = torch.Generator(device=dev).manual_seed(args.seed * 1000 + rank + 29)
+    cache.k.normal_(generator=gen)
+    cache.v.normal_(generator=gen)
+    w = orc.attention_weights(args.seed)
+    wqkv = torch.cat([w["q_proj"], w["k_proj"], w["v_proj"]]).to(dev).contiguous()
+    wo = w["out_proj"].to(dev).contiguous()
+    runner = attn.PagedDecodeAttention(cache, w["q_gamma"], w["k_gamma"], 1, L + 2)
+    x = torch.randn(1, 1024, generator=gen, device=dev).to(torch.bfloat16)
+    qkv = torch.empty(1, 2048, dtype=torch.bfloat16, device=dev)
+    y = torch.empty(1, 1024, dtype=torch.bfloat16, device=dev)
+    past = torch.tensor([L], dtype=torch.int32, device=dev)
+    seq, tables = past + 1, cache.block_tables()
+    stream = torch.cuda.Stream(dev)
+
+    def layer():
+        torch.matmul(x, wqkv.t(), out=qkv)
+        ctx = runner.step(0, qkv, past, seq, tables)
+        torch.matmul(ctx.reshape(1, 1024), wo.t(), out=y)
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            layer()
+    stream.synchronize()
+    runner.check()
+    K = args.steps
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for _ in range(K):
+            layer()
+    graph.replay()
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        with torch.cuda.stream(stream):
+            t0.record()
+            graph.replay()
+            t1.record()
+        torch.cuda.synchronize()
+    runner.check()
+    ms = t0.elapsed_time(t1)
+    nbytes = KV_BYTES_PER_TOKEN * (L + 4) + 4 * pc.blocks_for(L + 1) + 2 * (2048 * 1024 + 1024 * 1024)
+    peak, peak_kind = measured_hbm_peak()
+    gbs = nbytes / (ms / K / 1e3) / 1e9
+    line = {
+        "metric": METRIC, "value": K / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": K,
+        "warmup": args.warmup, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "replicas",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"C1: one attention layer (q/k/v and out projections + fused decode step) for "
+                               f"one token of one sequence at {L} cached tokens, CUDA graph of {K} steps",
+                   "context": L, "global_batch": 1, "blocks_per_split": runner.blocks_per_split,
+                   "parallelism": "replicas", "l2": "6 MB of weights and 1 MB of K/V stay in L2 across steps"},
+        "hbm_gbs_per_gpu": gbs,
+        "roofline": {"bound": "latency", "kernel": "qkv GEMM + decode_step_kernel + out GEMM",
+                     "achieved": gbs, "peak": peak, "peak_source": peak_kind, "unit": "GB/s", "frac": gbs / peak,
+                     "traffic": None, "algorithmic_bytes": nbytes},
+        "clocks": clocks.summary(), "gpu_launches": K,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def run_c2(args):
     """Config C2: one sequence, the 6 attention layers of LFM2.5-230M, 64
     consecutive decode steps from --context cached tokens (each step appends
@@ -795,6 +874,8 @@ def main():
         run_reference(args)
     elif args.config == "c4":
         run_c4(args)
+    elif args.config == "c1":
+        run_c1(args)
     elif args.config == "c2":
         run_c2(args)
     elif args.config == "c5":
