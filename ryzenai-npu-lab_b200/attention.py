@@ -99,7 +99,8 @@ def num_splits_for(max_blocks: int, blocks_per_split: int) -> int:
     return max(1, (max_blocks + blocks_per_split - 1) // blocks_per_split)
 
 
-def choose_blocks_per_split(batch: int, work_blocks: int, sms: int = B200_SMS, fused: bool = False) -> int:
+def choose_blocks_per_split(batch: int, work_blocks: int, sms: int = B200_SMS, fused: bool = False,
+                            max_blocks_per_seq: int | None = None) -> int:
     """Blocks per work item.  work_blocks: total 64-token blocks over the
     batch (one head).  Three-kernel path: about 8 CTAs of real work per SM
     (3 are resident at a time; the rest balance the tail).  Fused persistent
@@ -112,7 +113,8 @@ def choose_blocks_per_split(batch: int, work_blocks: int, sms: int = B200_SMS, f
     number of blocks (up to 64), finish together; measured on one 131 072-token
     sequence: 46.9 us at 296 items against 51.4 us at 432 and 52 us at 2 056."""
     if fused:
-        per_seq_max = math.ceil(work_blocks / max(1, batch))
+        # the longest sequence (the block-table width) when known, else the mean
+        per_seq_max = max_blocks_per_seq or math.ceil(work_blocks / max(1, batch))
         if batch * HKV >= 2 * sms * 3 and per_seq_max <= 32:
             # many short sequences: one split each (no cross-CTA merge; the
             # item's own epilogue writes the context)
@@ -396,7 +398,8 @@ class PagedDecodeAttention:
         self.cos, self.sin = rope_table(rope_positions, device=dev)
         if blocks_per_split is None:
             wb = work_blocks if work_blocks is not None else max_batch * cache.max_blocks
-            blocks_per_split = choose_blocks_per_split(max_batch, wb, fused=fused)
+            blocks_per_split = choose_blocks_per_split(max_batch, wb, fused=fused,
+                                                       max_blocks_per_seq=cache.max_blocks)
         if fused and blocks_per_split > 64:
             raise ValueError("the fused kernel takes at most 64 blocks per split")
         self.blocks_per_split = blocks_per_split
