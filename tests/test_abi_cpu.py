@@ -85,3 +85,34 @@ def test_decode_step_exchange_argument_checks_without_gpu():
                                             None, 1, None, None, 1, 1, 1, ctypes.c_float(0.125), 0, None, None,
                                             None, None, None, 0, None, 9, 0, None, None)
     assert rc == lib.B2_ERR_ARG and "world" in lib.last_error()
+
+
+def test_argument_errors_without_gpu():
+    """Host-side refusals (B2_ERR_ARG with a message, before any CUDA call)."""
+    lib = load_pkg("_lib")
+    c = lib.load()
+    f = ctypes.c_float
+    buf = ctypes.create_string_buffer(64)
+
+    def refused(rc, text):
+        assert rc == lib.B2_ERR_ARG, rc
+        assert text in lib.last_error(), lib.last_error()
+
+    # decode step: more than 64 blocks per split
+    refused(c.b2_decode_step(buf, 2048, None, None, f(1e-5), None, None, 0, buf, None, buf, 70, buf, buf, 10,
+                             1, 65, f(0.125), 0, buf, None, None, None, buf, buf, buf, 0, buf, None),
+            "blocks_per_split")
+    # prefill split: batch x splits beyond the grid limit
+    refused(c.b2_prefill_attn_split(buf, buf, buf, 10, buf, 100000, buf, None, 4, 2, f(0.125), 1, buf, buf, buf,
+                                    buf, None), "65535")
+    # exchange: world beyond the maximum, rank outside the world
+    areas = (ctypes.c_void_p * 2)(ctypes.addressof(buf), ctypes.addressof(buf))
+    refused(c.b2_exchange_merge(buf, buf, 1, areas, 9, 0, buf, buf, None), "world")
+    refused(c.b2_exchange_merge(buf, buf, 1, areas, 2, 2, buf, buf, None), "rank")
+    # layer kernels: width not a multiple of 8, odd SwiGLU width
+    refused(c.b2_add_rmsnorm(buf, None, buf, f(1e-5), None, buf, 1, 1020, None), "width")
+    refused(c.b2_swiglu(buf, buf, 1, 7, None), "ffn")
+    refused(c.b2_argmax_rows(buf, 1, 12, None, None), "null pointer")
+    # host-fed pipeline: slot outside 0 / 1
+    refused(c.b2_decode_step_host2(buf, buf, buf, buf, buf, buf, 2, None, None, f(1e-5), None, None, 0, buf, 1,
+                                   buf, buf, 1, 1, 1, f(0.125), buf, buf, buf, buf, None), "slot")
