@@ -20,6 +20,8 @@
  *   k_pool/v_pool bf16 [num_blocks][8 kv heads][64 tokens][64 dims]: one
  *                (block, head) tile is 8 KiB contiguous
  *   block_tables int32 [batch][max_blocks_per_seq]: logical block -> pool block
+ *                (max_blocks_per_seq <= 2^25 - 1, so that every length in
+ *                tokens fits an int32; wider tables are refused)
  *   past_lens    int32 [batch]: tokens cached before this step (the slot the
  *                new token is written to, and its RoPE position)
  *   seq_lens     int32 [batch]: tokens attended (cached + the new one)

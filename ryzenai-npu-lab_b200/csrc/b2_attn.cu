@@ -68,6 +68,14 @@ int ok() {
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Widest block table (and largest split) accepted: width x 64 tokens must stay
+// an int32 token count, which every length check on the device computes.
+constexpr int32_t kMaxTableWidth = (1 << 25) - 1;
+
+int table_width_error(int32_t max_blocks_per_seq) {
+  return fail(B2_ERR_ARG, "max_blocks_per_seq must be <= %d (got %d)", kMaxTableWidth, max_blocks_per_seq);
+}
+
 // ------------------------------------------------------------------ device helpers
 
 __device__ __forceinline__ void unpack8(const uint4 &w, float f[8]) {
@@ -2062,6 +2070,7 @@ extern "C" int b2_append_rope(const uint16_t *qkv, int64_t row_stride, const uin
   if ((mode & B2_ROPE_QK) &&
       (!rope_cos || !rope_sin || rope_rows <= 0 || !aligned16(rope_cos) || !aligned16(rope_sin)))
     return fail(B2_ERR_ARG, "B2_ROPE_QK needs 16-byte aligned cos/sin tables with rope_rows > 0");
+  if (max_blocks_per_seq > kMaxTableWidth) return table_width_error(max_blocks_per_seq);
   if (mode & B2_STORE_KV) {
     if (!block_tables || !k_pool || !v_pool || max_blocks_per_seq <= 0 || num_blocks <= 0)
       return fail(B2_ERR_ARG, "B2_STORE_KV needs block_tables, k_pool, v_pool and positive sizes");
@@ -2087,6 +2096,9 @@ extern "C" int b2_decode_attn(const uint16_t *q, const uint16_t *k_pool, const u
     return fail(B2_ERR_ARG, "num_blocks must be in [1, 2^22) (got %d)", num_blocks);
   if (max_blocks_per_seq <= 0 || blocks_per_split <= 0)
     return fail(B2_ERR_ARG, "max_blocks_per_seq and blocks_per_split must be positive");
+  if (max_blocks_per_seq > kMaxTableWidth) return table_width_error(max_blocks_per_seq);
+  if (blocks_per_split > kMaxTableWidth)
+    return fail(B2_ERR_ARG, "blocks_per_split must be <= %d (got %d)", kMaxTableWidth, blocks_per_split);
   if (static_cast<int64_t>(num_splits) * blocks_per_split < max_blocks_per_seq)
     return fail(B2_ERR_ARG, "num_splits * blocks_per_split (%d * %d) < max_blocks_per_seq (%d)",
                 num_splits, blocks_per_split, max_blocks_per_seq);
@@ -2114,6 +2126,8 @@ extern "C" int b2_combine(const float *part_ml, const float *part_o, int32_t num
   if (batch == 0) return ok();
   if (!part_ml || !part_o || num_parts <= 0) return fail(B2_ERR_ARG, "partial states and num_parts > 0 required");
   if (seq_lens && blocks_per_split <= 0) return fail(B2_ERR_ARG, "blocks_per_split must be positive");
+  if (static_cast<int64_t>(num_parts) * (seq_lens ? blocks_per_split : 1) * kBlock > 0x7fffffff)
+    return fail(B2_ERR_ARG, "num_parts x blocks_per_split x 64 must fit an int32 token count");
   if (!out && !state_o) return fail(B2_ERR_ARG, "one of out or state_o is required");
   if ((state_o == nullptr) != (state_ml == nullptr)) return fail(B2_ERR_ARG, "state_ml and state_o go together");
   CombineArgs a{part_ml, part_o, num_parts, seq_lens, blocks_per_split, out, state_ml, state_o, 0, 0,
@@ -2157,6 +2171,7 @@ int decode_step_impl(const uint16_t *qkv, int64_t row_stride, const uint16_t *ga
   if (num_blocks <= 0 || static_cast<int64_t>(num_blocks) * kHkv * kBlock >= (int64_t(1) << 31))
     return fail(B2_ERR_ARG, "num_blocks must be in [1, 2^22) (got %d)", num_blocks);
   if (max_blocks_per_seq <= 0) return fail(B2_ERR_ARG, "max_blocks_per_seq must be positive");
+  if (max_blocks_per_seq > kMaxTableWidth) return table_width_error(max_blocks_per_seq);
   if (blocks_per_split < 1 || blocks_per_split > kStepMaxBlocksPerSplit)
     return fail(B2_ERR_ARG, "blocks_per_split must be in [1, %d] (got %d)", kStepMaxBlocksPerSplit, blocks_per_split);
   if (!(scale > 0.f)) return fail(B2_ERR_ARG, "scale must be positive");
@@ -2316,6 +2331,7 @@ extern "C" int b2_prefill_append(const uint16_t *qkv, int64_t row_stride, const 
   if ((mode & B2_ROPE_QK) &&
       (!rope_cos || !rope_sin || rope_rows <= 0 || !aligned16(rope_cos) || !aligned16(rope_sin)))
     return fail(B2_ERR_ARG, "B2_ROPE_QK needs 16-byte aligned cos/sin tables with rope_rows > 0");
+  if (max_blocks_per_seq > kMaxTableWidth) return table_width_error(max_blocks_per_seq);
   if (mode & B2_STORE_KV) {
     if (!block_tables || !k_pool || !v_pool || max_blocks_per_seq <= 0 || num_blocks <= 0)
       return fail(B2_ERR_ARG, "B2_STORE_KV needs block_tables, k_pool, v_pool and positive sizes");
@@ -2339,6 +2355,7 @@ extern "C" int b2_prefill_attn(const uint16_t *q, const uint16_t *k_pool, const 
   if (num_blocks <= 0 || static_cast<int64_t>(num_blocks) * kHkv * kBlock >= (int64_t(1) << 31))
     return fail(B2_ERR_ARG, "num_blocks must be in [1, 2^22) (got %d)", num_blocks);
   if (max_blocks_per_seq <= 0) return fail(B2_ERR_ARG, "max_blocks_per_seq must be positive");
+  if (max_blocks_per_seq > kMaxTableWidth) return table_width_error(max_blocks_per_seq);
   if (batch > 65535) return fail(B2_ERR_ARG, "batch must be <= 65535");
   if (!aligned16(q) || !aligned16(out) || !aligned16(k_pool) || !aligned16(v_pool))
     return fail(B2_ERR_ARG, "q, out and the pools must be 16-byte aligned");
@@ -2368,7 +2385,9 @@ extern "C" int b2_prefill_attn_split(const uint16_t *q, const uint16_t *k_pool, 
   if (num_blocks <= 0 || static_cast<int64_t>(num_blocks) * kHkv * kBlock >= (int64_t(1) << 31))
     return fail(B2_ERR_ARG, "num_blocks must be in [1, 2^22) (got %d)", num_blocks);
   if (max_blocks_per_seq <= 0) return fail(B2_ERR_ARG, "max_blocks_per_seq must be positive");
-  if (blocks_per_split <= 0) return fail(B2_ERR_ARG, "blocks_per_split must be positive");
+  if (max_blocks_per_seq > kMaxTableWidth) return table_width_error(max_blocks_per_seq);
+  if (blocks_per_split <= 0 || blocks_per_split > kMaxTableWidth)
+    return fail(B2_ERR_ARG, "blocks_per_split must be in [1, %d]", kMaxTableWidth);
   const int64_t nsplit = (static_cast<int64_t>(max_blocks_per_seq) + blocks_per_split - 1) / blocks_per_split;
   if (static_cast<int64_t>(batch) * nsplit > 65535) return fail(B2_ERR_ARG, "batch x splits must be <= 65535");
   if (static_cast<int64_t>(batch) * tokens * nsplit * kHq * kDim >= (int64_t(1) << 40))
@@ -2670,6 +2689,9 @@ extern "C" int b2_decode_attn_noalloc(const uint16_t *q, const uint16_t *k_pool,
     return fail(B2_ERR_ARG, "null pointer argument");
   if (max_blocks_per_seq <= 0 || blocks_per_split <= 0)
     return fail(B2_ERR_ARG, "max_blocks_per_seq and blocks_per_split must be positive");
+  if (max_blocks_per_seq > kMaxTableWidth) return table_width_error(max_blocks_per_seq);
+  if (blocks_per_split > kMaxTableWidth)
+    return fail(B2_ERR_ARG, "blocks_per_split must be <= %d (got %d)", kMaxTableWidth, blocks_per_split);
   const int64_t splits = (static_cast<int64_t>(max_blocks_per_seq) + blocks_per_split - 1) / blocks_per_split;
   if (splits * batch > B2_NOALLOC_MAX_PARTS)
     return fail(B2_ERR_ARG,

@@ -102,6 +102,20 @@ def test_argument_errors_without_gpu():
     refused(c.b2_decode_step(buf, 2048, None, None, f(1e-5), None, None, 0, buf, None, buf, 70, buf, buf, 10,
                              1, 65, f(0.125), 0, buf, None, None, None, buf, buf, buf, 0, buf, None),
             "blocks_per_split")
+    # block tables wider than an int32 token count can address (2^25 blocks of 64 tokens)
+    wide = 1 << 25
+    refused(c.b2_decode_step(buf, 2048, None, None, f(1e-5), None, None, 0, buf, None, buf, wide, buf, buf, 10,
+                             1, 1, f(0.125), 0, buf, None, None, None, buf, buf, buf, 0, buf, None),
+            "max_blocks_per_seq")
+    refused(c.b2_decode_attn(buf, buf, buf, 10, buf, wide, buf, 1, 1, wide, f(0.125), buf, buf, buf, None),
+            "max_blocks_per_seq")
+    refused(c.b2_decode_attn(buf, buf, buf, 10, buf, 4, buf, 1, wide, 1, f(0.125), buf, buf, buf, None),
+            "blocks_per_split")
+    refused(c.b2_prefill_attn(buf, buf, buf, 10, buf, wide, buf, None, 4, 1, f(0.125), buf, buf, None),
+            "max_blocks_per_seq")
+    refused(c.b2_append_rope(buf, 2048, None, None, f(1e-5), None, None, 0, buf, buf, wide, buf, buf, 10, None,
+                             1, 4, buf, None), "max_blocks_per_seq")
+    refused(c.b2_combine(buf, buf, 1 << 20, buf, 64, 1, buf, None, None, None), "int32 token count")
     # prefill split: batch x splits beyond the grid limit
     refused(c.b2_prefill_attn_split(buf, buf, buf, 10, buf, 100000, buf, None, 4, 2, f(0.125), 1, buf, buf, buf,
                                     buf, None), "65535")
