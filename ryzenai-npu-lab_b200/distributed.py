@@ -84,10 +84,48 @@ def p2p_possible(hosts: list[str], devices: list[str]) -> bool:
     return len(set(hosts)) == 1 and len(set(devices)) == len(devices) and 1 < len(devices) <= _lib.B2_XCHG_MAX_WORLD
 
 
+def agree(failure: str | None, group=None) -> list[str]:
+    """Every rank's failure text (None when it succeeded), on every rank: one
+    all_gather_object, so that all ranks take the same branch afterwards."""
+    outcomes: list[str | None] = [None] * dist.get_world_size(group)
+    dist.all_gather_object(outcomes, failure, group=group)
+    return [f"rank {r}: {o}" for r, o in enumerate(outcomes) if o]
+
+
+def open_peer_areas(entries: list, rank: int, open_fn, close_fn, group=None) -> tuple[list, list]:
+    """Map every other rank's exchange area; `entries[r]` is what open_fn needs
+    for rank r, and open_fn returns the mapped pointer.  The ranks agree on
+    the outcome: if any rank fails, every rank unmaps what it mapped and all
+    raise ValueError together (instead of the others waiting in the next
+    collective for a rank that gave up)."""
+    opened, ptrs, failure = [], [], None
+    for r, entry in enumerate(entries):
+        if r == rank:
+            ptrs.append(None)
+            continue
+        try:
+            ptr = open_fn(entry)
+        except Exception as e:  # noqa: BLE001 - reported to every rank below
+            failure = f"mapping rank {r}'s area: {e}"
+            break
+        opened.append((ptr, entry))
+        ptrs.append(ptr)
+    failed = agree(failure, group)
+    if failed:
+        for ptr, entry in opened:
+            try:
+                close_fn(ptr, entry)
+            except Exception:  # noqa: BLE001 - already failing; keep unmapping the rest
+                pass
+        raise ValueError("P2P exchange setup failed: " + "; ".join(failed))
+    return opened, ptrs
+
+
 class PeerExchange:
     """Exchange areas for b2_exchange_merge: one in this rank's memory, the
     other ranks' mapped through CUDA IPC (peer access over NVLink).  All ranks
-    of `group` construct it together; close() together."""
+    of `group` construct it together; close() together.  A setup failure on
+    any rank is a ValueError on every rank."""
 
     def __init__(self, batch: int, group=None, device: torch.device | str = "cuda"):
         lib = _lib.load()
@@ -101,23 +139,29 @@ class PeerExchange:
         self.area = torch.zeros(nbytes // 4, dtype=torch.int32, device=self.device)
         handle = ctypes.create_string_buffer(64)
         offset = ctypes.c_int64(0)
-        _lib.check(lib.b2_ipc_handle(ctypes.c_void_p(self.area.data_ptr()), handle, ctypes.byref(offset)),
-                   "b2_ipc_handle")
+        failure = None
+        if lib.b2_ipc_handle(ctypes.c_void_p(self.area.data_ptr()), handle, ctypes.byref(offset)) != _lib.B2_OK:
+            failure = "b2_ipc_handle: " + _lib.last_error()
         uuid = str(torch.cuda.get_device_properties(self.device).uuid)
         info = [None] * self.world
-        dist.all_gather_object(info, (handle.raw, offset.value, socket.gethostname(), uuid), group=group)
+        dist.all_gather_object(info, (handle.raw, offset.value, socket.gethostname(), uuid, failure), group=group)
+        failed = [f"rank {r}: {i[4]}" for r, i in enumerate(info) if i[4]]
+        if failed:
+            raise ValueError("P2P exchange setup failed: " + "; ".join(failed))
         if not p2p_possible([i[2] for i in info], [i[3] for i in info]):
             raise ValueError("the P2P exchange needs all ranks on one host, each on its own GPU")
-        self.opened = []
-        ptrs = []
-        for r, (h, off, _, _) in enumerate(info):
-            if r == self.rank:
-                ptrs.append(self.area.data_ptr())
-                continue
+
+        def open_fn(entry):
             peer = ctypes.c_void_p()
-            _lib.check(lib.b2_ipc_open(h, off, ctypes.byref(peer)), "b2_ipc_open")
-            self.opened.append((peer.value, off))
-            ptrs.append(peer.value)
+            _lib.check(lib.b2_ipc_open(entry[0], entry[1], ctypes.byref(peer)), "b2_ipc_open")
+            return peer.value
+
+        def close_fn(ptr, entry):
+            _lib.check(lib.b2_ipc_close(ctypes.c_void_p(ptr), entry[1]), "b2_ipc_close")
+
+        opened, ptrs = open_peer_areas(info, self.rank, open_fn, close_fn, group)
+        self.opened = [(ptr, entry[1]) for ptr, entry in opened]
+        ptrs[self.rank] = self.area.data_ptr()
         self.areas = (ctypes.c_void_p * self.world)(*ptrs)
         dist.barrier(group=group)
 

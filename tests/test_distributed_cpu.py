@@ -1,6 +1,7 @@
 """Host-side multi-GPU logic on CPU: sequence sharding, token ranges, and the
 long-context state exchange over a world-size-2 gloo group (the partial
 states come from the CPU oracle; on GPUs they come from libb2attn.so)."""
+import ctypes
 import os
 import socket
 
@@ -156,3 +157,148 @@ def test_split_size_heuristic():
     assert 4 <= attn.choose_blocks_per_split(512, 512 * 60, fused=True) <= 32
     # three-kernel path: ~8 CTAs of work per SM
     assert 2 <= attn.choose_blocks_per_split(64, 3715) <= 64
+
+
+def _open_peers_worker(rank, world, port, fail_on, result):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        dist_mod = load_pkg("distributed")
+        closed = []
+
+        def open_fn(entry):
+            if (rank, entry) == fail_on:
+                raise RuntimeError("b2_ipc_open failed")
+            return 1000 + entry
+
+        def close_fn(ptr, entry):
+            closed.append(ptr)
+
+        entries = list(range(world))      # rank r's "handle" is r
+        try:
+            opened, ptrs = dist_mod.open_peer_areas(entries, rank, open_fn, close_fn)
+            out = ["ok", [p for p, _ in opened], ptrs]
+        except ValueError as e:
+            out = ["ValueError", str(e)]
+        dist.barrier()                     # every rank reaches the next collective
+        result[rank] = out + [sorted(closed)]
+    finally:
+        dist.destroy_process_group()
+
+
+def _run_open_peers(world, fail_on):
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as mgr:
+        result = mgr.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_open_peers_worker, args=(r, world, port, fail_on, result))
+                 for r in range(world)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(120)
+            assert p.exitcode == 0
+        return dict(result)
+
+
+def test_peer_setup_agrees_on_failure_gloo():
+    """One rank that cannot map a peer's area makes every rank raise ValueError
+    (so an automatic choice falls back to the collective on all of them), and
+    the ranks that did map areas unmap them."""
+    res = _run_open_peers(3, fail_on=(1, 2))
+    for r in range(3):
+        assert res[r][0] == "ValueError" and "rank 1: mapping rank 2's area" in res[r][1]
+    assert res[0][2] == [1001, 1002]       # rank 0 mapped ranks 1 and 2, then unmapped both
+    assert res[1][2] == [1000]             # rank 1 mapped rank 0 before failing on rank 2
+    assert res[2][2] == [1000, 1001]
+
+
+def test_peer_setup_success_gloo():
+    res = _run_open_peers(2, fail_on=None)
+    assert res[0] == ["ok", [1001], [None, 1001], []]
+    assert res[1] == ["ok", [1000], [1000, None], []]
+
+
+class _FakeIpcLib:
+    """Stands in for libb2attn.so's exchange entry points on CPU ranks."""
+
+    def __init__(self, rank, fail_handle):
+        self.rank, self.fail_handle, self.closed = rank, fail_handle, []
+
+    def b2_exchange_bytes(self, world, batch):
+        return 256
+
+    def b2_ipc_handle(self, ptr, handle, offset_ref):
+        if self.fail_handle:
+            return -2
+        ctypes.memmove(handle, b"rank%d" % self.rank, 5)
+        offset_ref._obj.value = 16 * (self.rank + 1)
+        return 0
+
+    def b2_ipc_open(self, handle, offset, peer_ref):
+        peer_ref._obj.value = 4096 * (int(handle[4:5]) + 1) + offset
+        return 0
+
+    def b2_ipc_close(self, ptr, offset):
+        self.closed.append((ptr.value, offset))
+        return 0
+
+
+def _peer_exchange_worker(rank, world, port, fail_handle_rank, result):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        lib_mod = load_pkg("_lib")
+        dist_mod = load_pkg("distributed")
+        fake = _FakeIpcLib(rank, rank == fail_handle_rank)
+        lib_mod.load = lambda: fake
+        lib_mod.last_error = lambda: "fake failure"
+        torch.cuda.get_device_properties = lambda dev: type("P", (), {"uuid": f"GPU-{rank}"})()
+        torch.cuda.synchronize = lambda dev=None: None
+        try:
+            px = dist_mod.PeerExchange(1, device="cpu")
+            areas = list(px.areas)
+            areas[rank] = "own" if areas[rank] == px.area.data_ptr() else areas[rank]
+            px.close()
+            result[rank] = ["ok", areas, fake.closed]
+        except ValueError as e:
+            dist.barrier()
+            result[rank] = ["ValueError", str(e)]
+    finally:
+        dist.destroy_process_group()
+
+
+def _run_peer_exchange(world, fail_handle_rank):
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as mgr:
+        result = mgr.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_peer_exchange_worker, args=(r, world, port, fail_handle_rank, result))
+                 for r in range(world)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(120)
+            assert p.exitcode == 0
+        return dict(result)
+
+
+def test_peer_exchange_setup_and_close_gloo():
+    """PeerExchange's host logic with a fake IPC library: every rank maps the
+    others' areas from the gathered handles and offsets, and close() unmaps
+    exactly those."""
+    res = _run_peer_exchange(3, fail_handle_rank=None)
+    for r in range(3):
+        status, areas, closed = res[r]
+        assert status == "ok" and areas[r] == "own"
+        peers = [(4096 * (p + 1) + 16 * (p + 1), 16 * (p + 1)) for p in range(3) if p != r]
+        assert [a for i, a in enumerate(areas) if i != r] == [a for a, _ in peers]
+        assert sorted(closed) == sorted(peers)
+
+
+def test_peer_exchange_handle_failure_is_everyones_gloo():
+    res = _run_peer_exchange(2, fail_handle_rank=1)
+    for r in range(2):
+        assert res[r][0] == "ValueError" and "rank 1: b2_ipc_handle: fake failure" in res[r][1]
