@@ -49,6 +49,15 @@ def _need(t: torch.Tensor, name: str, dtype: torch.dtype, device: torch.device, 
         raise ValueError(f"{name} must have shape {tuple(shape)}, got {tuple(t.shape)}")
 
 
+def _need_rope(cos, sin, device: torch.device) -> int:
+    """cos/sin tables bf16 [positions, 64] (one row per RoPE position); returns positions."""
+    _need(cos, "cos", torch.bfloat16, device)
+    _need(sin, "sin", torch.bfloat16, device, tuple(cos.shape))
+    if cos.dim() != 2 or cos.shape[1] != D or cos.shape[0] == 0:
+        raise ValueError(f"cos/sin must be [positions >= 1, {D}], got {tuple(cos.shape)}")
+    return cos.shape[0]
+
+
 def append_rope(qkv: torch.Tensor, past_lens: torch.Tensor, *, q_out: torch.Tensor | None,
                 dev_err: torch.Tensor, mode: int = _lib.B2_NORM_QK | _lib.B2_ROPE_QK | _lib.B2_STORE_KV,
                 gamma_q: torch.Tensor | None = None, gamma_k: torch.Tensor | None = None,
@@ -72,11 +81,7 @@ def append_rope(qkv: torch.Tensor, past_lens: torch.Tensor, *, q_out: torch.Tens
         _need(gamma_q, "gamma_q", torch.bfloat16, dev, (D,))
         _need(gamma_k, "gamma_k", torch.bfloat16, dev, (D,))
     if mode & _lib.B2_ROPE_QK:
-        _need(cos, "cos", torch.bfloat16, dev)
-        _need(sin, "sin", torch.bfloat16, dev, tuple(cos.shape))
-        if cos.dim() != 2 or cos.shape[1] != D:
-            raise ValueError("cos/sin must be [positions, 64]")
-        rope_rows = cos.shape[0]
+        rope_rows = _need_rope(cos, sin, dev)
     max_blocks = num_blocks = 0
     if mode & _lib.B2_STORE_KV:
         _need(k_pool, "k_pool", torch.bfloat16, dev)
@@ -237,9 +242,7 @@ def decode_step(qkv: torch.Tensor, past_lens: torch.Tensor, *, k_pool: torch.Ten
         _need(gamma_q, "gamma_q", torch.bfloat16, dev, (D,))
         _need(gamma_k, "gamma_k", torch.bfloat16, dev, (D,))
     if mode & _lib.B2_ROPE_QK:
-        _need(cos, "cos", torch.bfloat16, dev)
-        _need(sin, "sin", torch.bfloat16, dev, tuple(cos.shape))
-        rope_rows = cos.shape[0]
+        rope_rows = _need_rope(cos, sin, dev)
     max_blocks = block_tables.shape[1]
     splits = num_splits_for(max_blocks, blocks_per_split)
     _need(part_ml, "part_ml", torch.float32, dev)
@@ -318,9 +321,7 @@ def prefill(qkv: torch.Tensor, past_lens: torch.Tensor, *, k_pool: torch.Tensor,
         _need(gamma_q, "gamma_q", torch.bfloat16, dev, (D,))
         _need(gamma_k, "gamma_k", torch.bfloat16, dev, (D,))
     if mode & _lib.B2_ROPE_QK:
-        _need(cos, "cos", torch.bfloat16, dev)
-        _need(sin, "sin", torch.bfloat16, dev, tuple(cos.shape))
-        rope_rows = cos.shape[0]
+        rope_rows = _need_rope(cos, sin, dev)
     _need(dev_err, "dev_err", torch.int32, dev)
     if q_out is None:
         q_out = torch.empty(b, t, HQ, D, dtype=torch.bfloat16, device=dev)

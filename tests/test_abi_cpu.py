@@ -130,3 +130,31 @@ def test_argument_errors_without_gpu():
     # host-fed pipeline: slot outside 0 / 1
     refused(c.b2_decode_step_host2(buf, buf, buf, buf, buf, buf, 2, None, None, f(1e-5), None, None, 0, buf, 1,
                                    buf, buf, 1, 1, 1, f(0.125), buf, buf, buf, buf, None), "slot")
+
+
+def test_rope_tables_must_be_64_wide_without_gpu():
+    """Every wrapper that rotates q/k refuses cos/sin tables that are not
+    [positions, 64] before any launch (the kernels index rows of 64)."""
+    import pytest
+    import torch
+    attn = load_pkg("attention")
+    lib = load_pkg("_lib")
+    bf, i32 = torch.bfloat16, torch.int32
+    past = torch.zeros(1, dtype=i32)
+    pool = torch.zeros(2, 8, 64, 64, dtype=bf)
+    tables = torch.zeros(1, 2, dtype=i32)
+    err = torch.zeros(1, dtype=i32)
+    mode = lib.B2_ROPE_QK | lib.B2_STORE_KV
+    for cos in (torch.zeros(16, 32, dtype=bf), torch.zeros(1024, dtype=bf), torch.zeros(0, 64, dtype=bf)):
+        sin = cos.clone()
+        with pytest.raises(ValueError, match="cos/sin"):
+            attn.append_rope(torch.zeros(1, 2048, dtype=bf), past, q_out=None, dev_err=err, mode=mode, cos=cos,
+                             sin=sin, k_pool=pool, v_pool=pool, block_tables=tables)
+        with pytest.raises(ValueError, match="cos/sin"):
+            attn.decode_step(torch.zeros(1, 2048, dtype=bf), past, k_pool=pool, v_pool=pool, block_tables=tables,
+                             blocks_per_split=1, out=torch.zeros(1, 16, 64, dtype=bf),
+                             part_ml=torch.zeros(1, 2, 16, 2), part_o=torch.zeros(1, 2, 16, 64),
+                             counters=torch.zeros(10, dtype=i32), dev_err=err, mode=mode, cos=cos, sin=sin)
+        with pytest.raises(ValueError, match="cos/sin"):
+            attn.prefill(torch.zeros(1, 4, 2048, dtype=bf), past, k_pool=pool, v_pool=pool, block_tables=tables,
+                         gamma_q=None, gamma_k=None, cos=cos, sin=sin, dev_err=err, mode=mode)
