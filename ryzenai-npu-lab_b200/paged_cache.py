@@ -39,20 +39,34 @@ class BlockAllocator:
             g = torch.Generator().manual_seed(shuffle_seed)
             order = torch.randperm(num_blocks, generator=g).tolist()
         self._free = order[::-1]   # pop() hands out order[0], order[1], ...
+        self._used: set[int] = set()
 
     @property
     def free(self) -> int:
         return len(self._free)
 
     def alloc(self, n: int) -> list[int]:
+        if n < 0:
+            raise ValueError("n must be >= 0")
         if n > len(self._free):
             raise MemoryError(f"KV pool exhausted: need {n} blocks, {len(self._free)} free")
-        return [self._free.pop() for _ in range(n)]
+        out = [self._free.pop() for _ in range(n)]
+        self._used.update(out)
+        return out
 
     def release(self, blocks) -> None:
+        """Return blocks to the free list.  A block outside the pool, not
+        handed out, or listed twice is refused (nothing is released): two
+        sequences sharing a block would overwrite each other's keys."""
+        blocks = list(blocks)
         for b in blocks:
             if not 0 <= b < self.num_blocks:
                 raise ValueError(f"block {b} outside the pool")
+            if b not in self._used:
+                raise ValueError(f"block {b} is not allocated")
+        if len(set(blocks)) != len(blocks):
+            raise ValueError("a block is listed twice")
+        self._used.difference_update(blocks)
         self._free.extend(blocks)
 
 
@@ -96,6 +110,14 @@ class PagedKVCache:
         self._tables.append(self.allocator.alloc(blocks_for(cap)))
         self.lengths.append(length)
         return len(self._tables) - 1
+
+    def release_sequence(self, seq: int) -> None:
+        """Return a finished sequence's blocks to the pool.  Its row stays (block
+        tables keep their batch index) with no blocks and length 0: it must
+        not be stepped again, since a row of -1 entries is a device error."""
+        self.allocator.release(self._tables[seq])
+        self._tables[seq] = []
+        self.lengths[seq] = 0
 
     def block_tables(self) -> torch.Tensor:
         """int32 [batch, max_blocks_per_seq]; unused entries are -1."""
