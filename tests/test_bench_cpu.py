@@ -33,3 +33,16 @@ def test_every_rank_gets_the_one_gpu_batch():
     for world in (2, 4, 8):
         for rank in range(world):
             assert sorted(bench.seq_lengths(a, rank, world)) == base
+
+
+def test_reference_arm_other_ranks_exit_quietly():
+    """Under torchrun with N > 1 only rank 0 runs the reference arm; rank 1
+    prints nothing and exits 0 (its environment is what torchrun sets)."""
+    import os
+    env = dict(os.environ, RANK="1", LOCAL_RANK="1", WORLD_SIZE="2", MASTER_ADDR="127.0.0.1",
+               MASTER_PORT="29599")
+    proc = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--gpus", "2",
+                           "--steps", "2", "--warmup", "1"], cwd=ROOT, env=env, capture_output=True, text=True,
+                          timeout=300)
+    assert proc.returncode == 0, proc.stderr[-2000:]
+    assert proc.stdout.strip() == ""
