@@ -158,3 +158,18 @@ def test_rope_tables_must_be_64_wide_without_gpu():
         with pytest.raises(ValueError, match="cos/sin"):
             attn.prefill(torch.zeros(1, 4, 2048, dtype=bf), past, k_pool=pool, v_pool=pool, block_tables=tables,
                          gamma_q=None, gamma_k=None, cos=cos, sin=sin, dev_err=err, mode=mode)
+
+
+def test_integration_stub_matches_the_library_signatures():
+    """The ctypes stub in INTEGRATION.md (what a maintainer would paste into
+    the reference's code) declares the same argument types as _lib.py."""
+    lib = load_pkg("_lib")
+    code = {ctypes.c_void_p: "p", ctypes.c_int64: "i64", ctypes.c_int32: "i32", ctypes.c_float: "f32"}
+    text = (ROOT / "INTEGRATION.md").read_text()
+    stubs = re.findall(r"lib\.(b2_\w+)\.argtypes = \[([^\]]*)\]", text, flags=re.S)
+    assert {"b2_append_rope", "b2_decode_attn", "b2_combine", "b2_decode_step"} <= {n for n, _ in stubs}
+    for name, args in stubs:
+        if name == "b2_last_error":
+            continue
+        doc = [a.strip() for a in args.replace("\n", " ").split(",") if a.strip()]
+        assert doc == [code[t] for t in lib.SIGNATURES[name][1]], name
