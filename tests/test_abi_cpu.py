@@ -173,3 +173,41 @@ def test_integration_stub_matches_the_library_signatures():
             continue
         doc = [a.strip() for a in args.replace("\n", " ").split(",") if a.strip()]
         assert doc == [code[t] for t in lib.SIGNATURES[name][1]], name
+
+
+def test_last_error_is_per_thread_without_gpu():
+    """b2_last_error reports the calling thread's own last error: two threads
+    fail different calls in turn, then each reads its own message."""
+    import threading
+    lib = load_pkg("_lib")
+    c = lib.load()
+    buf = ctypes.create_string_buffer(64)
+    gate = threading.Barrier(2)
+    seen = {}
+
+    def worker(name, call, expect):
+        def text():
+            out = ctypes.create_string_buffer(512)
+            c.b2_last_error(out, 512)
+            return out.value.decode()
+        if name == "a":
+            call()
+            gate.wait()      # a has failed
+            gate.wait()      # b has failed too
+        else:
+            gate.wait()
+            call()
+            gate.wait()
+        seen[name] = (expect in text(), text())
+
+    calls = {
+        "a": (lambda: c.b2_swiglu(buf, buf, 1, 7, None), "ffn"),
+        "b": (lambda: c.b2_argmax_rows(buf, 1, 12, None, None), "null pointer"),
+    }
+    threads = [threading.Thread(target=worker, args=(n, *calls[n])) for n in calls]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join(30)
+    assert seen["a"][0] and "ffn" in seen["a"][1] and "null pointer" not in seen["a"][1], seen
+    assert seen["b"][0] and "ffn" not in seen["b"][1], seen
