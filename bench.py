@@ -539,6 +539,11 @@ def run_c4(args):
         part_ms = ms / K
     local_tokens = lc.local_len + (1 if lc.is_tail else 0)
     local_bytes = KV_BYTES_PER_TOKEN * local_tokens + 2048 * 2 + 2 * 1024
+    # every rank's own step time, partial time and tokens (which rank is the slow one), then the max
+    per_rank = torch.empty(world, 3, dtype=torch.float64, device=dev)
+    torch.distributed.all_gather_into_tensor(
+        per_rank, torch.tensor([[1e3 * ms / K, 1e3 * part_ms, local_tokens]], dtype=torch.float64, device=dev))
+    per_rank_rows = [[round(r[0], 2), round(r[1], 2), int(r[2])] for r in per_rank.tolist()]
     times = torch.tensor([ms, part_ms], dtype=torch.float64, device=dev)
     torch.distributed.all_reduce(times, op=torch.distributed.ReduceOp.MAX)
     ms, part_ms = times.tolist()
@@ -559,6 +564,7 @@ def run_c4(args):
                    "global_batch": 1, "blocks_per_split": lc.bps, "parallelism": f"split-kv x{world}",
                    "l2": "inputs larger than L2 (268 MB of K/V), no flush"},
         "hbm_gbs_aggregate": total_bytes / (ms / K / 1e3) / 1e9,
+        "per_rank": {"columns": ["step_us", "partial_us", "local_tokens"], "rows": per_rank_rows},
         "roofline": {"bound": "hbm", "kernel": "decode_step_kernel (+ combine of its splits)",
                      "achieved": local_bytes / (part_ms / 1e3) / 1e9, "peak": peak, "peak_source": peak_kind,
                      "unit": "GB/s", "frac": local_bytes / (part_ms / 1e3) / 1e9 / peak, "traffic": None,
