@@ -239,6 +239,36 @@ def test_fused_step_matches_three_kernels(cuda, max_ctas):
     assert torch.equal(v0.nan_to_num(7.0), v1.nan_to_num(7.0))
 
 
+@pytest.mark.parametrize("bps", [1, 3])
+def test_fused_step_large_batch_dense_items(cuda, bps):
+    """More than 512 sequences: the fused kernel enumerates the dense (split,
+    sequence, head) space and skips splits past each sequence's end (a table
+    20 blocks wide, histories of at most 5 blocks).  bps 1 gives 20 splits
+    (merged by the combine kernel), bps 3 gives 7 (merged in the kernel).
+    Against the three-kernel path, and the oracle on a few sequences."""
+    g = torch.Generator().manual_seed(40 + bps)
+    lengths = torch.randint(0, 300, (600,), generator=g).tolist()
+    b = len(lengths)
+    w = orc.attention_weights(0)
+    raw = rand_qkv(b, 41)
+    outs = []
+    for fused in (False, True):
+        cache, hist = build_batch(lengths, cuda, seed=9, capacity=64 * 20)
+        runner = _attn().PagedDecodeAttention(cache, w["q_gamma"], w["k_gamma"], b, 4096, blocks_per_split=bps,
+                                              fused=fused)
+        past = torch.tensor(lengths, dtype=torch.int32, device=cuda)
+        out = runner.step(0, raw.to(cuda), past, past + 1, cache.block_tables()).clone()
+        torch.cuda.synchronize()
+        runner.check()
+        if fused:
+            assert int(runner.counters.abs().sum().item()) == 0
+        outs.append(out)
+    check_close(outs[1], outs[0], f"600 sequences, bps {bps}: fused vs three kernels")
+    for i in (0, 1, 2, 299, 599):
+        ctx, _, _, _ = orc.decode_step(raw[i], hist[i][0], hist[i][1], lengths[i], w["q_gamma"], w["k_gamma"])
+        check_close(outs[1][i], ctx, f"seq {i} len {lengths[i] + 1} bps {bps}")
+
+
 def test_fused_multi_step_decode_vs_oracle(cuda):
     """Eight consecutive decode steps crossing a block edge, each attending
     over the tokens appended by the previous steps."""
