@@ -1476,6 +1476,7 @@ struct __align__(8) PrefillTail {
   uint64_t pready[2];         // P_j written (and O re-based) by all 128 softmax threads
   uint64_t pfree[2];          // P buffer read by its P.V MMA (commit)
   uint64_t pvbar;             // P_j.V_j accumulated (commit, once per block)
+  uint64_t obar;              // every product issued done (one commit after the last)
   uint32_t tmem_base;
   int abort;
 };
@@ -1671,6 +1672,7 @@ __global__ void __launch_bounds__(kPfThreads, 2)
       mbar_init(smem_u32(&tail->pfree[i]), 1);
     }
     mbar_init(smem_u32(&tail->pvbar), 1);
+    mbar_init(smem_u32(&tail->obar), 1);
     tail->abort = 0;
     mbar_fence_init();
   }
@@ -1751,7 +1753,6 @@ __global__ void __launch_bounds__(kPfThreads, 2)
         return true;
       };
       bool ok = issue_s(0) && (nblk < 2 || issue_s(1));
-      int done = 0;  // P.V products issued
       for (int j = 0; ok && j < nblk; ++j) {
         const int s = j % kPfStages;
         if (!mbar_wait(smem_u32(&tail->pready[j & 1]), (j >> 1) & 1) || tail->abort ||
@@ -1769,15 +1770,19 @@ __global__ void __launch_bounds__(kPfThreads, 2)
         umma_commit(smem_u32(&tail->pvbar));
         umma_commit(smem_u32(&tail->pfree[j & 1]));
         umma_commit(smem_u32(&tail->vempty[s]));
-        done = j + 1;
         if (j + 2 < nblk) ok = issue_s(j + 2);
       }
       if (!ok) {
         if (!tail->abort) atomicOr(a.err, B2_DEV_TIMEOUT);
         tail->abort = 1;
       }
-      // the MMAs issued must finish before the CTA leaves (bounded)
-      if (done > 0) mbar_wait(smem_u32(&tail->pvbar), (done - 1) & 1);
+      // One commit after the last product tracks every product issued: its
+      // single phase tells this warp (before the CTA frees its TMEM) and the
+      // softmax warps (before they read O) that all of them are done.  A parity
+      // wait on pvbar could not: it is exact only while pvbar is within one
+      // phase of the completion waited for, and here it may lag by two.
+      umma_commit(smem_u32(&tail->obar));
+      if (!mbar_wait(smem_u32(&tail->obar), 0)) atomicOr(a.err, B2_DEV_TIMEOUT);
     }
   } else {
     // ---------------- softmax warps: thread = query row = TMEM lane
@@ -1920,7 +1925,7 @@ __global__ void __launch_bounds__(kPfThreads, 2)
     if (!ok) {
       if (!tail->abort) atomicOr(a.err, B2_DEV_TIMEOUT);
       tail->abort = 1;
-    } else if (warp_wait(smem_u32(&tail->pvbar), (nblk - 1) & 1)) {
+    } else if (warp_wait(smem_u32(&tail->obar), 0)) {
       // O = sum_j P_j . V_j, every product done
       tmem_fence_after();
       float o[64];
