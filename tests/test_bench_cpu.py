@@ -46,3 +46,17 @@ def test_reference_arm_other_ranks_exit_quietly():
                           timeout=300)
     assert proc.returncode == 0, proc.stderr[-2000:]
     assert proc.stdout.strip() == ""
+
+
+def test_algorithmic_bytes_follow_the_formula():
+    """bytes per step = sum over sequences of 2048 (L + 4) + 4 ceil((L + 1) / 64):
+    K and V of L cached tokens, the raw q/k/v read, the k/v append, the
+    context write, and the block-table entries."""
+    sys.path.insert(0, str(ROOT))
+    import bench
+    step, decode = bench.step_bytes([0, 63, 64])
+    assert step == (2048 * 4 + 4) + (2048 * 67 + 4) + (2048 * 68 + 8)
+    assert decode == (2048 * 1 + 2048 + 4) + (2048 * 64 + 2048 + 4) + (2048 * 65 + 2048 + 8)
+    a = types.SimpleNamespace(seed=3, min_len=128, max_len=8192, batch=64)
+    step, _ = bench.step_bytes(bench.seq_lengths(a, 0, 1))
+    assert 0.45e9 < step < 0.65e9          # ~546 MB per layer-step for 64 sequences of mean ~4 K
