@@ -2,17 +2,22 @@
 
     python bench.py --gpus N --steps K --warmup W [--impl b200|reference]
 
-Workload (batched paged decode): per GPU, 64 sequences
-with cached lengths uniform in [128, 8192] (one seeded draw of 64 lengths;
-with N GPUs the global batch is N copies of it, sharded over the GPUs by token
-count, so every GPU does the one-GPU run's work), K/V ~ N(0, 1)
-bf16 in a pool of 64-token blocks handed out in shuffled order, 16 q heads /
-8 KV heads / head_dim 64.  One step = one decode token per sequence through
-one attention layer: fused q/k RMSNorm + RoPE + KV append, split-KV
-flash-decode, combine.  Sequences are sharded across GPUs with no collective
-(weak scaling: every rank holds its own 64 sequences); the step time is the
-max over ranks.  The K/V pool (~0.55 GB per GPU) is larger than L2 (126 MB),
-so no L2 flush is needed between steps.
+Workload (batched paged decode): 64 sequences with
+cached lengths uniform in [128, 8192] (one seeded draw), K/V ~ N(0, 1) bf16 in
+a pool of 64-token blocks handed out in shuffled order, 16 q heads / 8 KV
+heads / head_dim 64.  One step = one decode token per sequence through one
+attention layer: fused q/k RMSNorm + RoPE + KV append, split-KV flash-decode,
+combine.  With N GPUs the 64 sequences are sharded over the GPUs by token
+count (64/32/16/8 per GPU at 1/2/4/8; strong scaling, the default) with no
+collective; `--scaling weak` gives every GPU its own copy of the 64-sequence
+batch instead.  The step time is the max over ranks.  The K/V pool (~0.49 GB)
+is larger than L2 (126 MB), so no L2 flush is needed between steps.
+
+At N = 1 the line also carries `contexts`: fixed-length batches of 32 and 64
+sequences at 1K/4K/8K/16K cached tokens (the metric's "vs context" axis) and
+config C2 (one sequence, 6 layers x 64 steps) from 1K/4K/16K.  Points whose
+K/V would fit in L2 rotate over enough copies of the batch (separate block
+tables in one pool) that every step reads memory the previous steps did not.
 
 The timed region replays a CUDA graph of exactly K steps with inputs already
 in HBM; `e2e` times the same steps through the public API
@@ -80,6 +85,9 @@ def parse():
                    help="c5: run the layer glue (norms, SwiGLU, short conv) as torch ops")
     p.add_argument("--exchange", choices=["auto", "p2p", "collective"], default="auto",
                    help="c4: how the ranks' partial states are merged")
+    p.add_argument("--scaling", choices=["strong", "weak"], default="strong",
+                   help="c3 with N GPUs: shard the one 64-sequence batch (strong) or give every GPU a copy (weak)")
+    p.add_argument("--no-sweep", action="store_true", help="c3: skip the vs-context points")
     return p.parse_args()
 
 
@@ -166,19 +174,29 @@ class ClockSampler:
 
 # ----------------------------------------------------------------- workload
 
-def seq_lengths(args, rank: int, world: int = 1) -> list[int]:
-    """Cached lengths of this rank's sequences.  The 64-sequence C3 batch is
-    drawn from one seeded generator; with N GPUs the global batch is N such
-    batches (the same lengths, different K/V contents per rank), sharded over
-    the ranks by token count (longest-first bin packing), so every GPU gets
-    exactly the work of the one-GPU run (weak scaling)."""
+def base_lengths(args) -> list[int]:
+    """The C3 batch: one seeded draw of --batch cached lengths."""
     g = torch.Generator().manual_seed(args.seed * 1000)
-    base = torch.randint(args.min_len, args.max_len + 1, (args.batch,), generator=g).tolist()
+    return torch.randint(args.min_len, args.max_len + 1, (args.batch,), generator=g).tolist()
+
+
+def seq_lengths(args, rank: int, world: int = 1) -> list[int]:
+    """Cached lengths of this rank's sequences.  Strong scaling (default): the
+    one C3 batch sharded over the ranks by token count (longest first to the
+    least-loaded rank), 64/32/16/8 sequences per GPU at 1/2/4/8.  Weak: the
+    global batch is N copies of it (different K/V per rank), so every GPU gets
+    exactly the work of the one-GPU run."""
+    base = base_lengths(args)
     if world == 1:
         return base
-    lengths = base * world
+    lengths = base * world if getattr(args, "scaling", "strong") == "weak" else base
     dmod = importlib.import_module(PKG + ".distributed")
     return [lengths[i] for i in dmod.shard_sequences(lengths, world)[rank]]
+
+
+def global_tokens_per_step(args, world: int) -> int:
+    """Decode tokens the whole job produces per step (one per sequence)."""
+    return args.batch * (world if getattr(args, "scaling", "strong") == "weak" else 1)
 
 
 def build_workload(args, rank: int, dev: torch.device, world: int = 1):
@@ -221,14 +239,15 @@ def cpu_reference_rate(lengths, seconds: float, seed: int = 0):
     """tokens/s of the reference CPU path (oracle restatement of transformers'
     Lfm2Attention decode + DynamicCache.update) over sequences of the given
     lengths, one sequence at a time (the reference decode loop is batch-1),
-    with all host threads.  Runs until `seconds` have elapsed (at least one
-    pass over 4 sequences)."""
+    with all host threads.  Every sequence of `lengths` takes part, so the
+    sample's mean context is the workload's; runs whole passes over them until
+    `seconds` have elapsed (at least one pass)."""
     from oracle import lfm2_attention as orc
 
     torch.set_num_threads(os.cpu_count() or 1)
     w = orc.attention_weights(seed)
     g = torch.Generator().manual_seed(seed + 1)
-    sample = lengths[: max(4, min(len(lengths), 16))]
+    sample = list(lengths)
     hist = [(torch.randn(HKV, n, D, generator=g).to(torch.bfloat16),
              torch.randn(HKV, n, D, generator=g).to(torch.bfloat16)) for n in sample]
     qkv = (torch.randn(len(sample), 2048, generator=g) * 0.6).to(torch.bfloat16)
@@ -249,11 +268,16 @@ def cpu_reference_rate(lengths, seconds: float, seed: int = 0):
                        "mean_context": round(sum(sample) / len(sample), 1)}
 
 
+def cpu_sample_info(info: dict) -> str:
+    return (f"batch-1 loop over all {info['sequences']} sequences of the workload (mean context "
+            f"{info['mean_context']}), {info['seq_steps']} sequence-steps in {info['seconds']} s")
+
+
 def run_reference(args):
     world, rank, _ = dist_env()
     if rank != 0:
         return
-    lengths = seq_lengths(args, 0)
+    lengths = base_lengths(args)
     per_step = max(0.02, min(1.0, 60.0 / max(1, args.steps)))   # whole run ~1 min
     for _ in range(args.warmup):
         cpu_reference_rate(lengths[:4], 0.0)
@@ -266,28 +290,169 @@ def run_reference(args):
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1000.0 * args.batch / value, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": 1000.0 * args.batch / value, "higher_is_better": True, "scaling": args.scaling,
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": config_block(args, lengths, None),
+        "config": config_block(args, lengths, None, args.gpus),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": f"median of {args.steps} samples, each {info}"},
+                         "sample": f"median of {args.steps} samples, each a {cpu_sample_info(info)}",
+                         "mean_context": info["mean_context"]},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-def config_block(args, lengths, bps):
+def config_block(args, lengths, bps, world: int = 1):
+    """lengths: every sequence of the job (all ranks)."""
+    weak = args.scaling == "weak" and world > 1
     return {
-        "workload": "C3 batched paged decode: 64 sequences per GPU, cached length ~U[128, 8192], "
-                    "64-token bf16 KV blocks in shuffled order, 16q/8kv heads x 64; one step = "
+        "workload": f"C3 batched paged decode: {args.batch} sequences, cached length ~U[{args.min_len}, "
+                    f"{args.max_len}], 64-token bf16 KV blocks in shuffled order, 16q/8kv heads x 64; one step = "
                     "one decode token per sequence through one attention layer "
-                    "(q/k norm + RoPE + KV append, split-KV flash-decode, combine)",
-        "batch_per_gpu": args.batch, "global_batch": args.batch * args.gpus,
+                    "(q/k norm + RoPE + KV append, split-KV flash-decode, combine); "
+                    + (f"every GPU decodes its own copy of the batch (weak scaling)" if weak else
+                       f"the sequences sharded over {world} GPU(s) by token count (strong scaling)"),
+        "global_batch": global_tokens_per_step(args, world), "batch_per_gpu": "sharded" if not weak else args.batch,
         "context_min": args.min_len, "context_max": args.max_len,
         "context_mean": round(sum(lengths) / len(lengths), 1),
-        "block_tokens": BLOCK, "blocks_per_split": bps, "parallelism": f"seq-shard x{args.gpus}",
+        "block_tokens": BLOCK, "blocks_per_split": bps, "parallelism": f"seq-shard x{world}",
         "l2": "inputs larger than L2 (KV pool > 126 MB per GPU), no flush",
     }
+
+
+# ----------------------------------------------------------------- vs-context points
+
+L2_BYTES = 126 * 2 ** 20
+
+
+def time_graph(graph, stream, reps: int = 1) -> float:
+    """ms of `reps` replays of a captured graph, CUDA events on its stream."""
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        t0.record()
+        for _ in range(reps):
+            graph.replay()
+        t1.record()
+    torch.cuda.synchronize()
+    return t0.elapsed_time(t1)
+
+
+def fixed_batch_point(args, dev, batch: int, L: int, steps: int = 96) -> dict:
+    """One decode step of `batch` sequences that all hold L cached tokens,
+    through the fused kernel (the C3 step at a fixed context).  If the K/V of
+    the batch would stay in L2, the step rotates over `copies` batches with
+    their own blocks (at least 4x L2 in all), so every step streams from HBM."""
+    attn = importlib.import_module(PKG + ".attention")
+    pc = importlib.import_module(PKG + ".paged_cache")
+    cap = L + 1
+    footprint = batch * KV_BYTES_PER_TOKEN * cap
+    copies = max(1, math.ceil(4 * L2_BYTES / footprint))
+    cache = pc.PagedKVCache(batch * copies * pc.blocks_for(cap), cap, device=dev,
+                            shuffle_seed=args.seed * 1000 + L + batch)
+    for _ in range(batch * copies):
+        cache.add_sequence(L, capacity=cap)
+    gen = torch.Generator(device=dev).manual_seed(args.seed * 1000 + L + batch + 29)
+    cache.k.normal_(generator=gen)
+    cache.v.normal_(generator=gen)
+    gg = torch.Generator().manual_seed(args.seed + 31)
+    gq = (1.0 + 0.1 * torch.randn(D, generator=gg)).to(torch.bfloat16)
+    gk = (1.0 + 0.1 * torch.randn(D, generator=gg)).to(torch.bfloat16)
+    runner = attn.PagedDecodeAttention(cache, gq, gk, batch, cap + 1, work_blocks=batch * pc.blocks_for(cap))
+    all_tables = cache.block_tables()
+    tables = [all_tables[c * batch:(c + 1) * batch].contiguous() for c in range(copies)]
+    ring = 4
+    qkv = (torch.randn(ring, batch, 2048, generator=gen, device=dev) * 0.6).to(torch.bfloat16)
+    past = torch.full((batch,), L, dtype=torch.int32, device=dev)
+    seq = past + 1
+    steps = copies * math.ceil(steps / copies)
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        for j in range(max(3, copies)):
+            runner.step(0, qkv[j % ring], past, seq, tables[j % copies])
+    stream.synchronize()
+    runner.check()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for j in range(steps):
+            runner.step(0, qkv[j % ring], past, seq, tables[j % copies])
+    time_graph(graph, stream)   # upload
+    ms = time_graph(graph, stream) / steps
+    runner.check()
+    nbytes = batch * (KV_BYTES_PER_TOKEN * (L + 4) + 4 * pc.blocks_for(cap))
+    peak, _ = measured_hbm_peak()
+    gbs = nbytes / (ms / 1e3) / 1e9
+    del graph, runner, cache
+    torch.cuda.empty_cache()
+    return {"batch": batch, "context": L, "us_per_step": round(1e3 * ms, 2),
+            "tokens_per_s": round(batch / (ms / 1e3), 1), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4),
+            "pct_of_8tbs": round(100 * gbs / 8000, 2), "copies": copies, "steps": steps}
+
+
+def c2_point(args, dev, L0: int, reps: int = 4, sampler=None) -> dict:
+    """Config C2 from L0 cached tokens: one sequence, 6 attention layers x 64
+    consecutive decode steps (each appends one token per layer), captured once
+    as a CUDA graph and replayed; per token = 6 fused steps."""
+    attn = importlib.import_module(PKG + ".attention")
+    pc = importlib.import_module(PKG + ".paged_cache")
+    layers, steps = 6, 64
+    cap = L0 + steps + 1
+    cache = pc.PagedKVCache(pc.blocks_for(cap), cap, num_layers=layers, device=dev,
+                            shuffle_seed=args.seed * 1000 + 17)
+    cache.add_sequence(L0, capacity=cap)
+    gen = torch.Generator(device=dev).manual_seed(args.seed * 1000 + 29)
+    cache.k.normal_(generator=gen)
+    cache.v.normal_(generator=gen)
+    gg = torch.Generator().manual_seed(args.seed + 31)
+    gammas = [((1.0 + 0.1 * torch.randn(D, generator=gg)).to(torch.bfloat16),
+               (1.0 + 0.1 * torch.randn(D, generator=gg)).to(torch.bfloat16)) for _ in range(layers)]
+    runners = [attn.PagedDecodeAttention(cache, gq, gk, 1, cap + 1, blocks_per_split=args.bps or None,
+                                         work_blocks=pc.blocks_for(cap)) for gq, gk in gammas]
+    qkv = (torch.randn(steps, layers, 1, 2048, generator=gen, device=dev) * 0.6).to(torch.bfloat16)
+    past = torch.arange(L0, L0 + steps, dtype=torch.int32, device=dev).reshape(steps, 1)
+    seq = past + 1
+    tables = cache.block_tables()
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        for t in range(3):
+            for layer in range(layers):
+                runners[layer].step(layer, qkv[t, layer], past[t], seq[t], tables)
+    stream.synchronize()
+    for r in runners:
+        r.check()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for t in range(steps):
+            for layer in range(layers):
+                runners[layer].step(layer, qkv[t, layer], past[t], seq[t], tables)
+    time_graph(graph, stream)   # upload
+    if sampler is not None:
+        with sampler:
+            ms = time_graph(graph, stream, reps) / (reps * steps)
+    else:
+        ms = time_graph(graph, stream, reps) / (reps * steps)
+    for r in runners:
+        r.check()
+    nbytes = sum(layers * (KV_BYTES_PER_TOKEN * (L0 + t + 4) + 4 * pc.blocks_for(L0 + t + 1))
+                 for t in range(steps)) / steps
+    peak, _ = measured_hbm_peak()
+    gbs = nbytes / (ms / 1e3) / 1e9
+    out = {"context": L0, "layers": layers, "us_per_token": round(1e3 * ms, 2),
+           "tokens_per_s": round(1 / (ms / 1e3), 1), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4),
+           "blocks_per_split": runners[0].blocks_per_split, "splits": runners[0].num_splits}
+    del graph, runners, cache
+    torch.cuda.empty_cache()
+    return out
+
+
+def context_sweep(args, dev) -> dict:
+    """The metric's 'vs context' axis on one GPU (after the headline run)."""
+    points = [fixed_batch_point(args, dev, b, L) for b in (32, 64) for L in (1024, 4096, 8192, 16384)]
+    return {"note": "fused decode step, one token per sequence and layer, all sequences at the given "
+                    "context; frac of the measured HBM copy peak; copies > 1: the step rotates over that "
+                    "many batches so that its K/V is not served from L2",
+            "batched": points,
+            "c2": [c2_point(args, dev, L0) for L0 in (1024, 4096, 16384)]}
 
 
 # ----------------------------------------------------------------- B200 path
@@ -412,6 +577,7 @@ def run_b200(args):
     e2e_ms = e0.elapsed_time(e1)
     runner.check()
 
+    ms_local = ms
     times = torch.tensor([ms, decode_ms, e2e_ms], dtype=torch.float64, device=dev)
     if pg is not None:
         torch.distributed.all_reduce(times, op=torch.distributed.ReduceOp.MAX)
@@ -422,19 +588,29 @@ def run_b200(args):
     kernel = "paged_decode_kernel"
     if runner.fused:
         dbytes, kernel = sbytes, "decode_step_kernel"
+    # every rank's own step time, sequences and cached tokens (which rank is the slow one)
+    per_rank = torch.empty(world, 3, dtype=torch.float64, device=dev)
+    mine = torch.tensor([[1e3 * ms_local / K, len(lengths), sum(lengths)]], dtype=torch.float64, device=dev)
+    if pg is not None:
+        torch.distributed.all_gather_into_tensor(per_rank, mine)
+    else:
+        per_rank.copy_(mine)
+    per_rank_rows = [[round(r[0], 2), int(r[1]), int(r[2])] for r in per_rank.tolist()]
     peak, peak_kind = measured_hbm_peak()
     ms_step = ms / K
-    tokens = args.batch * world
+    tokens = global_tokens_per_step(args, world)
     value = tokens * K / (ms / 1e3)
     achieved = dbytes / (decode_ms / 1e3) / 1e9
     tpt = profiled_traffic_per_kv_token(kernel)
     kv_tokens = sum(n + 1 for n in lengths)
     step_gbs = sbytes / (ms_step / 1e3) / 1e9
+    all_lengths = base_lengths(args) * (world if args.scaling == "weak" else 1)
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
-        "warmup": W, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "warmup": W, "ms_per_step": ms_step, "higher_is_better": True, "scaling": args.scaling,
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": config_block(args, lengths, runner.blocks_per_split),
+        "config": config_block(args, all_lengths, runner.blocks_per_split, world),
+        "per_rank": {"columns": ["step_us", "sequences", "cached_tokens"], "rows": per_rank_rows},
         "hbm_gbs_per_gpu": step_gbs, "hbm_pct_of_8tbs": 100.0 * step_gbs / 8000.0,
         "roofline": {"bound": "hbm", "kernel": kernel, "achieved": achieved,
                      "peak": peak, "peak_source": peak_kind, "unit": "GB/s", "frac": achieved / peak,
@@ -446,11 +622,14 @@ def run_b200(args):
                 "d2h_bytes_per_step": nb * HQ * D * 2, "steps": e2e_steps},
         "gpu_launches": (1 if runner.fused else 3) * K,
     }
+    if rank == 0 and world == 1 and not args.no_sweep:
+        line["contexts"] = context_sweep(args, dev)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        rate, info = cpu_reference_rate(lengths, args.cpu_seconds)
+        rate, info = cpu_reference_rate(base_lengths(args), args.cpu_seconds)
         line["cpu_baseline"] = {"value": rate, "unit": "tokens/s", "cores": torch.get_num_threads(),
-                                "kind": "port", "sample": f"reference CPU path (transformers Lfm2Attention "
-                                f"restated, DynamicCache cat + sdpa), batch-1 loop over {info}"}
+                                "kind": "port", "sample": "reference CPU path (transformers Lfm2Attention "
+                                f"restated, DynamicCache cat + sdpa), {cpu_sample_info(info)}",
+                                "mean_context": info["mean_context"]}
     if rank == 0:
         print(json.dumps(line), flush=True)
     del graph
@@ -668,72 +847,23 @@ def run_c2(args):
     world, rank, local = dist_env()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    attn = importlib.import_module(PKG + ".attention")
-    pc = importlib.import_module(PKG + ".paged_cache")
-    layers, steps = 6, 64
     L0 = args.context
-    cap = L0 + steps + 1
-    cache = pc.PagedKVCache(pc.blocks_for(cap), cap, num_layers=layers, device=dev,
-                            shuffle_seed=args.seed * 1000 + 17)
-    cache.add_sequence(L0, capacity=cap)
-    gen = torch.Generator(device=dev).manual_seed(args.seed * 1000 + rank + 29)
-    cache.k.normal_(generator=gen)
-    cache.v.normal_(generator=gen)
-    gg = torch.Generator().manual_seed(args.seed + 31)
-    gammas = [((1.0 + 0.1 * torch.randn(D, generator=gg)).to(torch.bfloat16),
-               (1.0 + 0.1 * torch.randn(D, generator=gg)).to(torch.bfloat16)) for _ in range(layers)]
-    runners = [attn.PagedDecodeAttention(cache, gq, gk, 1, cap + 1, blocks_per_split=args.bps or None,
-                                         work_blocks=pc.blocks_for(cap)) for gq, gk in gammas]
-    qkv = (torch.randn(steps, layers, 1, 2048, generator=gen, device=dev) * 0.6).to(torch.bfloat16)
-    past = torch.arange(L0, L0 + steps, dtype=torch.int32, device=dev).reshape(steps, 1)
-    tables = cache.block_tables()
-    stream = torch.cuda.Stream(dev)
-
-    seq = past + 1
-    with torch.cuda.stream(stream):
-        for t in range(max(args.warmup, 1)):
-            for layer in range(layers):
-                runners[layer].step(layer, qkv[t % steps, layer], past[t % steps], seq[t % steps], tables)
-    stream.synchronize()
-    for r in runners:
-        r.check()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
-        for t in range(steps):
-            for layer in range(layers):
-                runners[layer].step(layer, qkv[t, layer], past[t], seq[t], tables)
-    graph.replay()
-    torch.cuda.synchronize()
-    reps = max(1, args.steps // steps)
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
-        with torch.cuda.stream(stream):
-            t0.record()
-            for _ in range(reps):
-                graph.replay()
-            t1.record()
-        torch.cuda.synchronize()
-    for r in runners:
-        r.check()
-    ms = t0.elapsed_time(t1)
-    K = reps * steps
-    step_bytes_all = sum(layers * (KV_BYTES_PER_TOKEN * (L0 + t + 4) + 4 * pc.blocks_for(L0 + t + 1))
-                         for t in range(steps)) / steps
+    reps = max(1, args.steps // 64)
+    clocks = ClockSampler(local)
+    pt = c2_point(args, dev, L0, reps, sampler=clocks)
     peak, peak_kind = measured_hbm_peak()
-    gbs = step_bytes_all / (ms / K / 1e3) / 1e9
     line = {
-        "metric": METRIC, "value": K / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": K,
-        "warmup": args.warmup, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "replicas",
+        "metric": METRIC, "value": pt["tokens_per_s"], "unit": "tokens/s", "n_gpus": 1, "steps": reps * 64,
+        "warmup": 3, "ms_per_step": pt["us_per_token"] / 1e3, "higher_is_better": True, "scaling": "replicas",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": f"C2: one sequence, 6 attention layers x 64 consecutive decode steps from "
                                f"{L0} cached tokens (CUDA graph of the 64 steps, replayed {reps}x)",
-                   "context": L0, "global_batch": 1, "blocks_per_split": runners[0].blocks_per_split,
+                   "context": L0, "global_batch": 1, "blocks_per_split": pt["blocks_per_split"],
                    "parallelism": "replicas", "l2": "K/V of 6 layers; the step re-reads its cache once"},
-        "hbm_gbs_per_gpu": gbs, "hbm_pct_of_8tbs": 100 * gbs / 8000,
-        "roofline": {"bound": "hbm", "kernel": "decode_step_kernel x 6 layers", "achieved": gbs, "peak": peak,
-                     "peak_source": peak_kind, "unit": "GB/s", "frac": gbs / peak, "traffic": None},
-        "clocks": clocks.summary(), "gpu_launches": K * layers * 2,
+        "hbm_gbs_per_gpu": pt["gbs"], "hbm_pct_of_8tbs": 100 * pt["gbs"] / 8000,
+        "roofline": {"bound": "hbm", "kernel": "decode_step_kernel x 6 layers", "achieved": pt["gbs"],
+                     "peak": peak, "peak_source": peak_kind, "unit": "GB/s", "frac": pt["frac"], "traffic": None},
+        "clocks": clocks.summary(), "gpu_launches": reps * 64 * 6 * (1 + (pt["splits"] > 16)),
     }
     if rank == 0:
         print(json.dumps(line), flush=True)

@@ -64,7 +64,13 @@ enum {
 enum {
   B2_NORM_QK = 1,   /* per-head RMSNorm of q and k, times gamma */
   B2_ROPE_QK = 2,   /* rotate-half RoPE of q and k at position past_lens[b] */
-  B2_STORE_KV = 4   /* write k and v into slot past_lens[b] of the pool */
+  B2_STORE_KV = 4,  /* write k and v into slot past_lens[b] of the pool */
+  /* b2_decode_step only, for tests of the failure path: one consumer warp of
+   * the first CTA waits on a barrier that nothing completes, gives up after
+   * the wait limit (b2_set_wait_limits), reports B2_DEV_TIMEOUT and leaves;
+   * the rest of the CTA then times out and unwinds the same way.  The step's
+   * results are invalid; the counters must be zeroed before the next step. */
+  B2_TEST_STALL = 0x100
 };
 
 /* Library ABI version (major * 100 + minor). */
@@ -73,6 +79,28 @@ int b2_version(void);
 /* Copy the calling thread's last error message into buf (NUL-terminated,
  * truncated to len).  Returns the message length. */
 int b2_last_error(char *buf, int len);
+
+/*
+ * Limits of the kernels' bounded waits, for every launch of this process
+ * after the call (a per-process setting read at launch):
+ *   wait_ns  a wait of one warp on another warp of its CTA (mbarrier phases
+ *            of the TMA rings, epilogue barrier, merger queue); default 2 s.
+ *            It must exceed the longest legitimate wait, about one work
+ *            item's streaming time (microseconds at the benchmark sizes).
+ *   poll_ns  the multi-GPU exchange's poll for the other ranks' state words
+ *            (b2_exchange_merge, b2_decode_step_exchange); default 5 s.
+ * A value <= 0 restores the default; values above 60 s are refused.  A wait
+ * of a CTA for its own copies or tensor-core products keeps a fixed 2 s.
+ * On expiry the kernel ORs B2_DEV_TIMEOUT into dev_err and returns.
+ *
+ * The reference's analogue is the watchdog around an NPU run and the raise
+ * on a run that did not complete (scripts/run_npu_timeout.ps1:1-19,
+ * experiments/npu_direct.py:110-114).
+ */
+int b2_set_wait_limits(int64_t wait_ns, int64_t poll_ns);
+
+/* The limits in force (nanoseconds); either pointer may be NULL. */
+int b2_get_wait_limits(int64_t *wait_ns, int64_t *poll_ns);
 
 /*
  * Fused q/k RMSNorm + RoPE + KV append for one decode token per sequence.

@@ -25,6 +25,7 @@ B2_DEV_TIMEOUT = 8
 B2_NORM_QK = 1
 B2_ROPE_QK = 2
 B2_STORE_KV = 4
+B2_TEST_STALL = 0x100         # b2_decode_step test mode: one warp's wait runs out
 
 B2_NOALLOC_MAX_PARTS = 1024   # batch * num_splits limit of b2_decode_attn_noalloc
 B2_XCHG_MAX_WORLD = 8         # ranks of b2_exchange_merge
@@ -45,6 +46,8 @@ _f32 = ctypes.c_float
 SIGNATURES = {
     "b2_version": (ctypes.c_int, []),
     "b2_last_error": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_int]),
+    "b2_set_wait_limits": (ctypes.c_int, [_i64, _i64]),
+    "b2_get_wait_limits": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64)]),
     "b2_append_rope": (ctypes.c_int, [
         _p, _i64,            # qkv, row_stride
         _p, _p, _f32,        # gamma_q, gamma_k, eps
@@ -207,6 +210,18 @@ def last_error() -> str:
 def check(status: int, call: str) -> None:
     if status != B2_OK:
         raise B2Error(status, f"{call}: {last_error()}")
+
+
+def set_wait_limits(wait_ns: int = 0, poll_ns: int = 0) -> None:
+    """Limits of the kernels' bounded waits for later launches (0: defaults,
+    2 s for a wait on another warp, 5 s for the multi-GPU exchange's poll)."""
+    check(load().b2_set_wait_limits(int(wait_ns), int(poll_ns)), "b2_set_wait_limits")
+
+
+def get_wait_limits() -> tuple[int, int]:
+    w, p = ctypes.c_int64(), ctypes.c_int64()
+    check(load().b2_get_wait_limits(ctypes.byref(w), ctypes.byref(p)), "b2_get_wait_limits")
+    return w.value, p.value
 
 
 def decode_dev_err(word: int) -> list[str]:

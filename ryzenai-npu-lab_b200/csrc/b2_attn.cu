@@ -42,7 +42,12 @@ constexpr int kConsumerWarps = 4;
 constexpr int kDecodeThreads = (kConsumerWarps + 1) * 32;
 constexpr int kTileBytes = kBlock * kDim * 2;  // one (block, head) tile: 8 KiB
 constexpr int kStageBytes = 2 * kTileBytes;    // K tile + V tile
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s, then report and return
+// Default limit of a wait on another thread of the CTA (2 s), then the
+// kernel reports B2_DEV_TIMEOUT and unwinds; b2_set_wait_limits changes it
+// per process.  Waits for the CTA's own copies or tensor-core products (the
+// hardware, not another thread) always allow kDrainLimitNs.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+constexpr uint64_t kDrainLimitNs = 2000000000ull;
 
 struct __align__(8) DecodeTail {
   uint64_t full[kStages];
@@ -149,15 +154,15 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
 }
 
 // Wait for the phase with the given parity to complete; false after
-// kWaitLimitNs (the caller reports B2_DEV_TIMEOUT and unwinds).
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+// limit_ns (the caller reports B2_DEV_TIMEOUT and unwinds).
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint64_t limit_ns) {
   if (mbar_try(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   for (;;) {
 #pragma unroll 1
     for (int i = 0; i < 32; ++i)
       if (mbar_try(bar, parity)) return true;
-    if (global_ns() - t0 > kWaitLimitNs) return false;
+    if (global_ns() - t0 > limit_ns) return false;
   }
 }
 
@@ -220,14 +225,40 @@ struct AppendArgs {
 //    IEEE-rounded sqrt and divide, as torch's CPU rsqrt computes 1/sqrt.
 //  * RoPE: bf16(bf16(x*cos) + bf16(rotate_half(x)*sin)), rotate_half(x) =
 //    [-x[32:], x[:32]]; the partner chunk j^4 sits on lane^4.
+//
+// mean(x^2) is bit-identical to torch's CPU x.pow(2).mean(-1) of a contiguous
+// 64-float row: rounded squares, summed in the order of ATen's vectorised
+// inner-dimension sum, whose vectors are 8 floats wide on every CPU build
+// (the reduction is not dispatched to 16-wide vectors), then divided by 64
+// (exact).  With v_k = squares 8k..8k+7 (chunk k, held by lane k of the group):
+//   a_k = v_k + v_{k+4}              k = 0..3, lane-wise
+//   p   = ((a_0 + a_1) + a_2) + a_3   lane-wise
+//   sum = (((p[0] + p[1]) + p[2]) + ...) + p[7]
+// No fused multiply-add anywhere in the chain.
+__device__ __forceinline__ float sum_squares64(const float x[8]) {
+  const int base = (threadIdx.x & 31) & ~7;
+  float a[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float sq = __fmul_rn(x[e], x[e]);
+    a[e] = __fadd_rn(sq, __shfl_xor_sync(0xffffffffu, sq, 4));  // a_k on lanes k = 0..3
+  }
+  float s = 0.f;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float a0 = __shfl_sync(0xffffffffu, a[e], base);
+    const float a1 = __shfl_sync(0xffffffffu, a[e], base + 1);
+    const float a2 = __shfl_sync(0xffffffffu, a[e], base + 2);
+    const float a3 = __shfl_sync(0xffffffffu, a[e], base + 3);
+    const float p = __fadd_rn(__fadd_rn(__fadd_rn(a0, a1), a2), a3);
+    s = e == 0 ? p : __fadd_rn(s, p);
+  }
+  return s;
+}
+
 __device__ __forceinline__ void norm_rope8_v(float x[8], int j, bool norm, bool rope, const uint4 gam,
                                              float eps, const uint4 cos8, const uint4 sin8) {
-  float ss = 0.f;
-#pragma unroll
-  for (int e = 0; e < 8; ++e) ss = fmaf(x[e], x[e], ss);
-  ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-  ss += __shfl_xor_sync(0xffffffffu, ss, 2);
-  ss += __shfl_xor_sync(0xffffffffu, ss, 4);
+  const float ss = sum_squares64(x);
   if (norm) {
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ss * (1.0f / kDim), eps)));
     float g[8];
@@ -327,6 +358,7 @@ struct DecodeArgs {
   float *part_ml;
   float *part_o;
   int32_t *err;
+  uint64_t wait_ns;  // limit of a wait on another warp
 };
 
 // grid (num_splits, 8 kv heads, batch), 4 consumer warps + 1 producer warp.
@@ -387,7 +419,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 3)
     for (int i = 0; i < n; ++i) {
       const int s = i % kStages;
       const uint32_t ph = (i / kStages) & 1;
-      if (i >= kStages && !mbar_wait(smem_u32(&tail->empty[s]), ph ^ 1)) {
+      if (i >= kStages && !mbar_wait(smem_u32(&tail->empty[s]), ph ^ 1, a.wait_ns)) {
         atomicOr(a.err, B2_DEV_TIMEOUT);
         break;
       }
@@ -408,7 +440,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 3)
     // wait (bounded) for the last phase issued on every stage.
     for (int s = 0; s < kStages && s < issued; ++s) {
       const int last = s + kStages * ((issued - 1 - s) / kStages);
-      if (!mbar_wait(smem_u32(&tail->full[s]), (last / kStages) & 1)) atomicOr(a.err, B2_DEV_TIMEOUT);
+      if (!mbar_wait(smem_u32(&tail->full[s]), (last / kStages) & 1, kDrainLimitNs))
+        atomicOr(a.err, B2_DEV_TIMEOUT);
     }
     return;
   }
@@ -435,7 +468,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 3)
   for (int i = 0; i < n; ++i) {
     const int s = i % kStages;
     const uint32_t ph = (i / kStages) & 1;
-    if (!mbar_wait(smem_u32(&tail->full[s]), ph)) {
+    if (!mbar_wait(smem_u32(&tail->full[s]), ph, a.wait_ns)) {
       if (lane == 0) atomicOr(a.err, B2_DEV_TIMEOUT);
       break;
     }
@@ -564,7 +597,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 3)
 
 constexpr int kXState = 4 + kDim;
 constexpr int kXMaxWorld = B2_XCHG_MAX_WORLD;
-constexpr uint64_t kXWaitNs = 5000000000ull;  // 5 s, then B2_DEV_TIMEOUT
+constexpr uint64_t kXWaitNs = 5000000000ull;  // default poll limit (5 s), then B2_DEV_TIMEOUT
 
 struct XchgArgs {
   const float *state_ml;  // [batch][16][2]
@@ -573,6 +606,7 @@ struct XchgArgs {
   uint16_t *out;  // [batch][16][64]
   int32_t *err;
   char *area[kXMaxWorld];  // rank r's exchange area as mapped on this GPU
+  uint64_t poll_ns;        // limit of the poll for the other ranks' words
 };
 
 __host__ __device__ constexpr int64_t x_words(int world, int batch) {
@@ -622,7 +656,7 @@ __device__ __forceinline__ void xchg_merge(const XchgArgs &a, int b, int h, int 
       wl = ld_word(src + 1);
       wo = ld_word(src + 4 + d);
       if (wm.y == tag && wl.y == tag && wo.y == tag) break;
-      if (global_ns() - t0 > kXWaitNs) {
+      if (global_ns() - t0 > a.poll_ns) {
         atomicOr(a.err, B2_DEV_TIMEOUT);
         ok = false;
         break;
@@ -797,6 +831,7 @@ struct __align__(16) StepTail {
   uint64_t full[kStages];
   uint64_t empty[kStages];
   uint64_t ebar;  // consumer-warp barrier of the epilogue (bounded waits)
+  uint64_t stall;  // never completed: the wait of B2_TEST_STALL runs out on it
   uint64_t pub[kPubSlots];    // consumers -> merger: a partial state is in memory
   uint64_t pfree[kPubSlots];  // merger -> consumers: the slot may be reused
   int4 pubinfo[kPubSlots];    // (b, kv head, split, nsplit); b < 0 ends the work
@@ -829,14 +864,16 @@ struct StepArgs {
   float *part_ml, *part_o;
   int32_t *counters;  // [0] work counter, [1] finished CTAs, [2 + b * 8 + kv head] split arrivals
   int32_t *err;
+  uint64_t wait_ns;  // limit of a wait on another warp
 };
 
 // Barrier of the 4 consumer warps on an mbarrier, with a bounded wait (a
 // hardware named barrier could not give up if a warp had left on a timeout).
-__device__ __forceinline__ void consumers_sync(StepTail *tail, int lane, uint32_t &phase, int32_t *err) {
+__device__ __forceinline__ void consumers_sync(StepTail *tail, int lane, uint32_t &phase, int32_t *err,
+                                               uint64_t limit_ns) {
   __syncwarp();
   if (lane == 0) mbar_arrive(smem_u32(&tail->ebar));
-  const bool ok = mbar_wait(smem_u32(&tail->ebar), phase & 1);
+  const bool ok = mbar_wait(smem_u32(&tail->ebar), phase & 1, limit_ns);
   ++phase;
   if (!ok && lane == 0) atomicOr(err, B2_DEV_TIMEOUT);
   __syncwarp();
@@ -1027,7 +1064,7 @@ __device__ __forceinline__ void step_producer(const StepArgs &a, StepTail *tail,
       const int s = issued % kStages;
       const uint32_t ph = (issued / kStages) & 1;
       int wait_ok = 1;
-      if (issued >= kStages && lane == 0) wait_ok = mbar_wait(smem_u32(&tail->empty[s]), ph ^ 1);
+      if (issued >= kStages && lane == 0) wait_ok = mbar_wait(smem_u32(&tail->empty[s]), ph ^ 1, a.wait_ns);
       wait_ok = __shfl_sync(0xffffffffu, wait_ok, 0);
       if (!wait_ok) {
         if (lane == 0) atomicOr(a.err, B2_DEV_TIMEOUT);
@@ -1071,21 +1108,29 @@ __device__ __forceinline__ void step_producer(const StepArgs &a, StepTail *tail,
     if (nxt.valid == 0) nxt = next_item();
   }
   if (lane != 0) return;
+  int marker = -1;  // stage holding the end-of-work marker
   if (ok) {
     // end-of-work marker: a plain arrival completes the stage's phase
     const int s = issued % kStages;
     const uint32_t ph = (issued / kStages) & 1;
-    if (issued < kStages || mbar_wait(smem_u32(&tail->empty[s]), ph ^ 1)) {
+    if (issued < kStages || mbar_wait(smem_u32(&tail->empty[s]), ph ^ 1, a.wait_ns)) {
       tail->meta[s].flags = kFlagEnd;
       mbar_arrive(smem_u32(&tail->full[s]));
-      return;  // consumers wait for every issued copy before they see the marker
+      marker = s;
+    } else {
+      atomicOr(a.err, B2_DEV_TIMEOUT);
     }
-    atomicOr(a.err, B2_DEV_TIMEOUT);
   }
-  // Aborting: wait (bounded) for the copies this CTA issued, then leave.
+  // Wait (bounded) for the copies this CTA issued before leaving.  Normally
+  // the consumers have waited for all of them already; a consumer that gave
+  // up on a wait may not have.  The marker's stage needs no wait: its last
+  // copy was released by the consumers before the marker was placed (the
+  // empty wait above), and a parity wait on it would name the wrong phase.
   for (int s = 0; s < kStages && s < issued; ++s) {
+    if (s == marker) continue;
     const int last = s + kStages * ((issued - 1 - s) / kStages);
-    if (!mbar_wait(smem_u32(&tail->full[s]), (last / kStages) & 1)) atomicOr(a.err, B2_DEV_TIMEOUT);
+    if (!mbar_wait(smem_u32(&tail->full[s]), (last / kStages) & 1, kDrainLimitNs))
+      atomicOr(a.err, B2_DEV_TIMEOUT);
   }
 }
 
@@ -1153,7 +1198,7 @@ __device__ __forceinline__ void step_epilogue(const StepArgs &a, StepTail *tail,
     red[warp][1][0] = m1;
     red[warp][1][1] = l1;
   }
-  consumers_sync(tail, lane, ephase, a.err);
+  consumers_sync(tail, lane, ephase, a.err, a.wait_ns);
   const int tid = threadIdx.x;  // 0..127
   const int h = tid >> 6, d = tid & 63;
   float M = -1.0e30f;
@@ -1184,7 +1229,7 @@ __device__ __forceinline__ void step_epilogue(const StepArgs &a, StepTail *tail,
 __device__ __forceinline__ void publish(const StepArgs &a, StepTail *tail, int lane, uint32_t &pubs, int b,
                                         int kvh, int split, int nsplit) {
   const int slot = pubs % kPubSlots;
-  if (pubs >= kPubSlots && !mbar_wait(smem_u32(&tail->pfree[slot]), ((pubs / kPubSlots) - 1) & 1)) {
+  if (pubs >= kPubSlots && !mbar_wait(smem_u32(&tail->pfree[slot]), ((pubs / kPubSlots) - 1) & 1, a.wait_ns)) {
     if (lane == 0) atomicOr(a.err, B2_DEV_TIMEOUT);
   }
   if (threadIdx.x == 0) tail->pubinfo[slot] = make_int4(b, kvh, split, nsplit);
@@ -1201,7 +1246,7 @@ __device__ __forceinline__ void publish(const StepArgs &a, StepTail *tail, int l
 __device__ __forceinline__ void step_merger(const StepArgs &a, StepTail *tail, int lane) {
   for (uint32_t k = 0;; ++k) {
     const int slot = k % kPubSlots;
-    if (!mbar_wait(smem_u32(&tail->pub[slot]), (k / kPubSlots) & 1)) {
+    if (!mbar_wait(smem_u32(&tail->pub[slot]), (k / kPubSlots) & 1, a.wait_ns)) {
       if (lane == 0) atomicOr(a.err, B2_DEV_TIMEOUT);
       return;
     }
@@ -1287,7 +1332,14 @@ __device__ __forceinline__ void step_consumer(const StepArgs &a, StepTail *tail,
   for (int it = 0;; ++it) {
     const int s = it % kStages;
     const uint32_t ph = (it / kStages) & 1;
-    if (!mbar_wait(smem_u32(&tail->full[s]), ph)) {
+    if ((a.mode & B2_TEST_STALL) && it == 0 && warp == 0 && blockIdx.x == 0 &&
+        !mbar_wait(smem_u32(&tail->stall), 0, a.wait_ns)) {
+      // test mode: this warp waits on a barrier that nothing completes, gives
+      // up after the wait limit and leaves like a warp that timed out
+      if (lane == 0) atomicOr(a.err, B2_DEV_TIMEOUT);
+      break;
+    }
+    if (!mbar_wait(smem_u32(&tail->full[s]), ph, a.wait_ns)) {
       if (lane == 0) atomicOr(a.err, B2_DEV_TIMEOUT);
       break;
     }
@@ -1403,6 +1455,7 @@ __global__ void __launch_bounds__(kStepThreads, 3)
       mbar_init(smem_u32(&tail->empty[s]), kConsumerWarps);
     }
     mbar_init(smem_u32(&tail->ebar), kConsumerWarps);
+    mbar_init(smem_u32(&tail->stall), 1);
 #pragma unroll
     for (int s = 0; s < kPubSlots; ++s) {
       mbar_init(smem_u32(&tail->pub[s]), kConsumerWarps * 32);
@@ -1498,6 +1551,7 @@ struct PrefillArgs {
   // units, sum) and part_o [nsplit][batch][tokens][16][64] (unnormalised)
   int bps, nsplit;
   float *part_ml, *part_o;
+  uint64_t wait_ns;  // limit of a wait on another warp
 };
 
 // Split-KV prefill: the partial state of (split, sequence b, token row, head)
@@ -1712,7 +1766,7 @@ __global__ void __launch_bounds__(kPfThreads, 2)
       for (int j = 0; j < nblk; ++j) {
         const int s = j % kPfStages;
         const uint32_t ph = (j / kPfStages) & 1;
-        if (j >= kPfStages && !mbar_wait(smem_u32(&emptyb[s]), ph ^ 1)) {
+        if (j >= kPfStages && !mbar_wait(smem_u32(&emptyb[s]), ph ^ 1, a.wait_ns)) {
           atomicOr(a.err, B2_DEV_TIMEOUT);
           tail->abort = 1;
           break;
@@ -1732,7 +1786,8 @@ __global__ void __launch_bounds__(kPfThreads, 2)
       // wait (bounded) until every issued copy has landed before leaving
       for (int s = 0; s < kPfStages && s < issued; ++s) {
         const int last = s + kPfStages * ((issued - 1 - s) / kPfStages);
-        if (!mbar_wait(smem_u32(&fullb[s]), (last / kPfStages) & 1)) atomicOr(a.err, B2_DEV_TIMEOUT);
+        if (!mbar_wait(smem_u32(&fullb[s]), (last / kPfStages) & 1, kDrainLimitNs))
+          atomicOr(a.err, B2_DEV_TIMEOUT);
       }
     }
   } else if (warp == 5) {
@@ -1740,8 +1795,8 @@ __global__ void __launch_bounds__(kPfThreads, 2)
     if (lane == 0) {
       auto issue_s = [&](int j) -> bool {
         const int s = j % kPfStages;
-        if (!mbar_wait(smem_u32(&tail->kfull[s]), (j / kPfStages) & 1)) return false;
-        if (j >= 2 && !mbar_wait(smem_u32(&tail->sfree[j & 1]), ((j >> 1) - 1) & 1)) return false;
+        if (!mbar_wait(smem_u32(&tail->kfull[s]), (j / kPfStages) & 1, a.wait_ns)) return false;
+        if (j >= 2 && !mbar_wait(smem_u32(&tail->sfree[j & 1]), ((j >> 1) - 1) & 1, a.wait_ns)) return false;
         tmem_fence_after();
         const uint32_t kt = smem_u32(kring + s * kTileBytes);
 #pragma unroll
@@ -1755,8 +1810,8 @@ __global__ void __launch_bounds__(kPfThreads, 2)
       bool ok = issue_s(0) && (nblk < 2 || issue_s(1));
       for (int j = 0; ok && j < nblk; ++j) {
         const int s = j % kPfStages;
-        if (!mbar_wait(smem_u32(&tail->pready[j & 1]), (j >> 1) & 1) || tail->abort ||
-            !mbar_wait(smem_u32(&tail->vfull[s]), (j / kPfStages) & 1)) {
+        if (!mbar_wait(smem_u32(&tail->pready[j & 1]), (j >> 1) & 1, a.wait_ns) || tail->abort ||
+            !mbar_wait(smem_u32(&tail->vfull[s]), (j / kPfStages) & 1, a.wait_ns)) {
           ok = false;
           break;
         }
@@ -1782,7 +1837,7 @@ __global__ void __launch_bounds__(kPfThreads, 2)
       // wait on pvbar could not: it is exact only while pvbar is within one
       // phase of the completion waited for, and here it may lag by two.
       umma_commit(smem_u32(&tail->obar));
-      if (!mbar_wait(smem_u32(&tail->obar), 0)) atomicOr(a.err, B2_DEV_TIMEOUT);
+      if (!mbar_wait(smem_u32(&tail->obar), 0, kDrainLimitNs)) atomicOr(a.err, B2_DEV_TIMEOUT);
     }
   } else {
     // ---------------- softmax warps: thread = query row = TMEM lane
@@ -1795,7 +1850,7 @@ __global__ void __launch_bounds__(kPfThreads, 2)
     // Waits decided for the whole warp (the TMEM loads and stores below are
     // warp-collective): false if any lane timed out or the CTA is aborting.
     auto warp_wait = [&](uint32_t bar, uint32_t parity) -> bool {
-      const bool got = mbar_wait(bar, parity);
+      const bool got = mbar_wait(bar, parity, a.wait_ns);
       return !__any_sync(0xffffffffu, !got || tail->abort);
     };
     // A warp whose 32 rows are all past the chunk (tiles of fewer than 33
@@ -1991,6 +2046,14 @@ int make_pool_map(CUtensorMap *map, const void *pool, int num_blocks) {
   return B2_OK;
 }
 
+// Wait limits of the launches (b2_set_wait_limits), read at every launch.
+std::atomic<uint64_t> g_wait_ns{kWaitLimitNs};
+std::atomic<uint64_t> g_poll_ns{kXWaitNs};
+constexpr int64_t kMaxWaitLimitNs = 60000000000ll;
+
+uint64_t wait_limit() { return g_wait_ns.load(std::memory_order_relaxed); }
+uint64_t poll_limit() { return g_poll_ns.load(std::memory_order_relaxed); }
+
 int launch_status(const char *what) {
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(B2_ERR_CUDA, "%s launch failed: %s", what, cudaGetErrorString(e));
@@ -2044,6 +2107,20 @@ int b2_record_error(int code, const char *message) { return fail(code, "%s", mes
 int b2_clear_error() { return ok(); }
 
 extern "C" int b2_version(void) { return 100; }
+
+extern "C" int b2_set_wait_limits(int64_t wait_ns, int64_t poll_ns) {
+  if (wait_ns > kMaxWaitLimitNs || poll_ns > kMaxWaitLimitNs)
+    return fail(B2_ERR_ARG, "wait limits must be <= %lld ns", (long long)kMaxWaitLimitNs);
+  g_wait_ns.store(wait_ns > 0 ? static_cast<uint64_t>(wait_ns) : kWaitLimitNs);
+  g_poll_ns.store(poll_ns > 0 ? static_cast<uint64_t>(poll_ns) : kXWaitNs);
+  return ok();
+}
+
+extern "C" int b2_get_wait_limits(int64_t *wait_ns, int64_t *poll_ns) {
+  if (wait_ns) *wait_ns = static_cast<int64_t>(wait_limit());
+  if (poll_ns) *poll_ns = static_cast<int64_t>(poll_limit());
+  return ok();
+}
 
 extern "C" int b2_last_error(char *buf, int len) {
   const int n = static_cast<int>(strlen(g_err));
@@ -2118,7 +2195,7 @@ extern "C" int b2_decode_attn(const uint16_t *q, const uint16_t *k_pool, const u
   if (rc) return rc;
   if (!decode_smem_ready()) return fail(B2_ERR_CUDA, "cannot set the decode kernel's shared memory size");
   DecodeArgs a{q, block_tables, max_blocks_per_seq, seq_lens, num_blocks, blocks_per_split, num_splits,
-               scale * 1.4426950408889634f, part_ml, part_o, dev_err};
+               scale * 1.4426950408889634f, part_ml, part_o, dev_err, wait_limit()};
   const dim3 grid(num_splits, kHkv, batch);
   paged_decode_kernel<<<grid, kDecodeThreads, kDecodeSmem, static_cast<cudaStream_t>(stream)>>>(mk, mv, a);
   return launch_status("paged_decode_kernel");
@@ -2162,7 +2239,8 @@ int decode_step_impl(const uint16_t *qkv, int64_t row_stride, const uint16_t *ga
   if (x && (!out || state_o || state_ml)) return fail(B2_ERR_ARG, "an exchange writes out and no state");
   if (!out && !state_o) return fail(B2_ERR_ARG, "one of out or state_o is required");
   if ((state_o == nullptr) != (state_ml == nullptr)) return fail(B2_ERR_ARG, "state_ml and state_o go together");
-  if (mode & ~(B2_NORM_QK | B2_ROPE_QK | B2_STORE_KV)) return fail(B2_ERR_ARG, "unknown mode bits 0x%x", mode);
+  if (mode & ~(B2_NORM_QK | B2_ROPE_QK | B2_STORE_KV | B2_TEST_STALL))
+    return fail(B2_ERR_ARG, "unknown mode bits 0x%x", mode);
   if (row_stride < kQkvWidth || row_stride % 8 != 0)
     return fail(B2_ERR_ARG, "row_stride must be >= %d and a multiple of 8", kQkvWidth);
   if (!aligned16(qkv) || (out && !aligned16(out)) || (q_out && !aligned16(q_out)) || !aligned16(k_pool) ||
@@ -2198,7 +2276,7 @@ int decode_step_impl(const uint16_t *qkv, int64_t row_stride, const uint16_t *ga
              block_tables, max_blocks_per_seq, k_pool, v_pool, num_blocks, batch, blocks_per_split,
              static_cast<int>(splits), static_cast<int>(total), direct_out, merge_here,
              scale * 1.4426950408889634f, mode, x ? nullptr : out, q_out, state_ml, state_o, part_ml, part_o,
-             counters, dev_err};
+             counters, dev_err, wait_limit()};
   int64_t ctas = static_cast<int64_t>(sm_count()) * 3;
   if (max_ctas > 0 && max_ctas < ctas) ctas = max_ctas;
   if (ctas > total) ctas = total;
@@ -2278,7 +2356,7 @@ extern "C" int b2_decode_step_exchange(const uint16_t *qkv, int64_t row_stride, 
   if (world < 1 || world > kXMaxWorld) return fail(B2_ERR_ARG, "world must be in [1, %d]", kXMaxWorld);
   if (rank < 0 || rank >= world) return fail(B2_ERR_ARG, "rank must be in [0, world)");
   if (!areas || !dev_err) return fail(B2_ERR_ARG, "null pointer argument");
-  XchgArgs x{nullptr, nullptr, batch, world, rank, out, dev_err, {}};
+  XchgArgs x{nullptr, nullptr, batch, world, rank, out, dev_err, {}, poll_limit()};
   for (int r = 0; r < world; ++r) {
     if (!areas[r] || (reinterpret_cast<uintptr_t>(areas[r]) & 15))
       return fail(B2_ERR_ARG, "exchange area %d is null or not 16-byte aligned", r);
@@ -2372,7 +2450,7 @@ extern "C" int b2_prefill_attn(const uint16_t *q, const uint16_t *k_pool, const 
   if (rc) return rc;
   if (!prefill_smem_ready()) return fail(B2_ERR_CUDA, "cannot set the prefill kernel's shared memory size");
   PrefillArgs a{q, block_tables, max_blocks_per_seq, past_lens, chunk_lens, tokens, num_blocks,
-                scale * 1.4426950408889634f, out, dev_err};
+                scale * 1.4426950408889634f, out, dev_err, 0, 0, nullptr, nullptr, wait_limit()};
   const dim3 grid((tokens + 63) / 64, kHkv, batch);
   prefill_attn_kernel<<<grid, kPfThreads, kPfSmem, static_cast<cudaStream_t>(stream)>>>(mk, mv, a);
   return launch_status("prefill_attn_kernel");
@@ -2409,7 +2487,7 @@ extern "C" int b2_prefill_attn_split(const uint16_t *q, const uint16_t *k_pool, 
   if (!prefill_smem_ready()) return fail(B2_ERR_CUDA, "cannot set the prefill kernel's shared memory size");
   PrefillArgs a{q, block_tables, max_blocks_per_seq, past_lens, chunk_lens, tokens, num_blocks,
                 scale * 1.4426950408889634f, out, dev_err, blocks_per_split, static_cast<int>(nsplit),
-                part_ml, part_o};
+                part_ml, part_o, wait_limit()};
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   const dim3 grid((tokens + 63) / 64, kHkv, static_cast<unsigned>(batch * nsplit));
   prefill_attn_kernel<<<grid, kPfThreads, kPfSmem, st>>>(mk, mv, a);
@@ -2621,7 +2699,7 @@ extern "C" int b2_exchange_merge(const float *state_ml, const float *state_o, in
   if (world < 1 || world > kXMaxWorld) return fail(B2_ERR_ARG, "world must be in [1, %d]", kXMaxWorld);
   if (rank < 0 || rank >= world) return fail(B2_ERR_ARG, "rank must be in [0, world)");
   if (!state_ml || !state_o || !areas || !out || !dev_err) return fail(B2_ERR_ARG, "null pointer argument");
-  XchgArgs a{state_ml, state_o, batch, world, rank, out, dev_err, {}};
+  XchgArgs a{state_ml, state_o, batch, world, rank, out, dev_err, {}, poll_limit()};
   for (int r = 0; r < world; ++r) {
     if (!areas[r] || (reinterpret_cast<uintptr_t>(areas[r]) & 15))
       return fail(B2_ERR_ARG, "exchange area %d is null or not 16-byte aligned", r);
@@ -2703,6 +2781,8 @@ extern "C" int b2_decode_attn_noalloc(const uint16_t *q, const uint16_t *k_pool,
                 "b2_decode_attn_noalloc: batch * ceil(max_blocks_per_seq / blocks_per_split) = %lld exceeds "
                 "the static scratch limit B2_NOALLOC_MAX_PARTS = %d; raise blocks_per_split or split the batch",
                 (long long)(splits * batch), B2_NOALLOC_MAX_PARTS);
+  if (splits * blocks_per_split * kBlock > 0x7fffffff)
+    return fail(B2_ERR_ARG, "b2_decode_attn_noalloc: splits x blocks_per_split x 64 must fit an int32 token count");
   if (num_blocks <= 0 || static_cast<int64_t>(num_blocks) * kHkv * kBlock >= (int64_t(1) << 31))
     return fail(B2_ERR_ARG, "num_blocks must be in [1, 2^22) (got %d)", num_blocks);
   if (!aligned16(q) || !aligned16(k_pool) || !aligned16(v_pool))
@@ -2721,7 +2801,7 @@ extern "C" int b2_decode_attn_noalloc(const uint16_t *q, const uint16_t *k_pool,
   if (!decode_smem_ready()) return fail(B2_ERR_CUDA, "cannot set the decode kernel's shared memory size");
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   DecodeArgs a{q, block_tables, max_blocks_per_seq, seq_lens, num_blocks, blocks_per_split,
-               static_cast<int>(splits), scale * 1.4426950408889634f, part_ml, part_o, dev_err};
+               static_cast<int>(splits), scale * 1.4426950408889634f, part_ml, part_o, dev_err, wait_limit()};
   paged_decode_kernel<<<dim3(static_cast<unsigned>(splits), kHkv, batch), kDecodeThreads, kDecodeSmem, s>>>(mk, mv, a);
   rc = launch_status("paged_decode_kernel (noalloc)");
   if (rc) return rc;

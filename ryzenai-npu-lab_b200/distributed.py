@@ -92,6 +92,14 @@ def agree(failure: str | None, group=None) -> list[str]:
     return [f"rank {r}: {o}" for r, o in enumerate(outcomes) if o]
 
 
+def agree_device_errors(word: int, group=None) -> list[str]:
+    """Every rank's device error word, on every rank (one all_gather_object):
+    the ranks whose kernels flagged an error, with the decoded bits.  An empty
+    list on every rank when none did, so all ranks take the same branch."""
+    text = "; ".join(_lib.decode_dev_err(word)) if word else None
+    return agree(text, group)
+
+
 def open_peer_areas(entries: list, rank: int, open_fn, close_fn, group=None) -> tuple[list, list]:
     """Map every other rank's exchange area; `entries[r]` is what open_fn needs
     for rank r, and open_fn returns the mapped pointer.  The ranks agree on
@@ -174,7 +182,12 @@ class PeerExchange:
         _lib.check(rc, "b2_exchange_merge")
 
     def reset(self) -> None:
-        """Zero the area (after a device error; every rank, then a barrier)."""
+        """Zero the area after a device error (every rank together).  The first
+        barrier makes sure no rank's exchange kernel is still writing tagged
+        words into this area when it is cleared; the second, that no rank
+        starts its next exchange before every area is clear."""
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
         self.area.zero_()
         torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)
@@ -339,11 +352,16 @@ class LongContextDecode:
             self.peer = None
 
     def check(self) -> None:
+        """Synchronise on the device error word.  With several ranks the words
+        are agreed first (every rank calls check() together), so that all
+        ranks raise together and can then reset_exchange() together."""
         word = int(self.dev_err.item())
-        if word:
+        failed = agree_device_errors(word, self.group) if self.world > 1 else (
+            [f"rank 0: {'; '.join(_lib.decode_dev_err(word))}"] if word else [])
+        if failed:
             self.dev_err.zero_()
             self.counters.zero_()
-            raise RuntimeError("long-context decode device error: " + "; ".join(_lib.decode_dev_err(word)) +
+            raise RuntimeError("long-context decode device error: " + "; ".join(failed) +
                                ("; call reset_exchange() on every rank" if self.peer is not None else ""))
 
     def reset_exchange(self) -> None:

@@ -160,19 +160,49 @@ def test_rope_tables_must_be_64_wide_without_gpu():
                          gamma_q=None, gamma_k=None, cos=cos, sin=sin, dev_err=err, mode=mode)
 
 
-def test_integration_stub_matches_the_library_signatures():
-    """The ctypes stub in INTEGRATION.md (what a maintainer would paste into
-    the reference's code) declares the same argument types as _lib.py."""
+def test_reference_binding_matches_the_library_signatures():
+    """The standalone ctypes stub a maintainer adds to the reference's loop
+    (reference_binding.py) declares the same argument types as _lib.py, and
+    binds the loaded library without a GPU."""
     lib = load_pkg("_lib")
-    code = {ctypes.c_void_p: "p", ctypes.c_int64: "i64", ctypes.c_int32: "i32", ctypes.c_float: "f32"}
-    text = (ROOT / "INTEGRATION.md").read_text()
-    stubs = re.findall(r"lib\.(b2_\w+)\.argtypes = \[([^\]]*)\]", text, flags=re.S)
-    assert {"b2_append_rope", "b2_decode_attn", "b2_combine", "b2_decode_step"} <= {n for n, _ in stubs}
-    for name, args in stubs:
-        if name == "b2_last_error":
-            continue
-        doc = [a.strip() for a in args.replace("\n", " ").split(",") if a.strip()]
-        assert doc == [code[t] for t in lib.SIGNATURES[name][1]], name
+    rb = load_pkg("reference_binding")
+    assert {"b2_append_rope", "b2_decode_attn", "b2_combine", "b2_decode_step"} <= set(rb.ARGTYPES)
+    for name, args in rb.ARGTYPES.items():
+        assert list(args) == list(lib.SIGNATURES[name][1]), name
+    cdll = rb.bind(str(lib.LIB_PATH))
+    assert cdll.b2_decode_step_counters(4) == 2 + 8 * 4
+    assert cdll.b2_combine(None, None, 0, None, 1, 1, None, None, None, None) == lib.B2_ERR_ARG
+    assert "num_parts" in rb.last_error(cdll)
+
+
+def test_wait_limits_without_gpu():
+    """b2_set_wait_limits: defaults 2 s / 5 s, <= 0 restores them, > 60 s refused."""
+    lib = load_pkg("_lib")
+    c = lib.load()
+    w, q = ctypes.c_int64(), ctypes.c_int64()
+    assert c.b2_get_wait_limits(ctypes.byref(w), ctypes.byref(q)) == lib.B2_OK
+    assert (w.value, q.value) == (2_000_000_000, 5_000_000_000)
+    assert c.b2_set_wait_limits(1_000_000, 3_000_000) == lib.B2_OK
+    c.b2_get_wait_limits(ctypes.byref(w), ctypes.byref(q))
+    assert (w.value, q.value) == (1_000_000, 3_000_000)
+    assert c.b2_set_wait_limits(61_000_000_000, 0) == lib.B2_ERR_ARG
+    assert "60" in lib.last_error()
+    assert c.b2_set_wait_limits(0, -1) == lib.B2_OK
+    c.b2_get_wait_limits(ctypes.byref(w), ctypes.byref(q))
+    assert (w.value, q.value) == (2_000_000_000, 5_000_000_000)
+
+
+def test_noalloc_refuses_token_count_overflow_without_gpu():
+    """b2_decode_attn_noalloc refuses a split geometry whose token count
+    (splits x blocks_per_split x 64) leaves int32, before any launch."""
+    lib = load_pkg("_lib")
+    c = lib.load()
+    buf = ctypes.create_string_buffer(64)
+    big = (1 << 25) - 1
+    rc = c.b2_decode_attn_noalloc(buf, buf, buf, 1, buf, big, buf, 1, big // 2 + 1, ctypes.c_float(0.125),
+                                  buf, buf, None)
+    assert rc == lib.B2_ERR_ARG
+    assert "int32" in lib.last_error()
 
 
 def test_last_error_is_per_thread_without_gpu():
@@ -211,3 +241,17 @@ def test_last_error_is_per_thread_without_gpu():
         t.join(30)
     assert seen["a"][0] and "ffn" in seen["a"][1] and "null pointer" not in seen["a"][1], seen
     assert seen["b"][0] and "ffn" not in seen["b"][1], seen
+
+
+def test_stall_bit_is_refused_outside_the_decode_step_without_gpu():
+    """B2_TEST_STALL (a test of the failure path) belongs to b2_decode_step
+    only: the append entry points refuse it before any launch."""
+    lib = load_pkg("_lib")
+    c = lib.load()
+    buf = ctypes.create_string_buffer(64 * 1024)
+    rc = c.b2_append_rope(buf, 2048, None, None, ctypes.c_float(1e-5), None, None, 0, buf, None, 0, None, None, 0,
+                          None, 1, lib.B2_TEST_STALL, buf, None)
+    assert rc == lib.B2_ERR_ARG and "mode" in lib.last_error()
+    rc = c.b2_prefill_append(buf, 2048, None, None, ctypes.c_float(1e-5), None, None, 0, buf, None, 1, None, 0,
+                             None, None, 0, None, 1, lib.B2_TEST_STALL, buf, None)
+    assert rc == lib.B2_ERR_ARG and "mode" in lib.last_error()

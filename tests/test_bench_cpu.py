@@ -22,17 +22,50 @@ def test_reference_arm_prints_one_json_line():
     assert d["e2e"]["value"] == d["value"] and d["e2e"]["h2d_bytes_per_step"] == 0
     assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["cores"] >= 1
     assert "workload" in d["config"]
+    assert d["cpu_baseline"]["mean_context"] == d["config"]["context_mean"]
 
 
-def test_every_rank_gets_the_one_gpu_batch():
+def test_strong_scaling_shards_the_one_batch():
+    """Default (strong): the one seeded 64-sequence batch is split over the
+    ranks, 64/32/16/8 per GPU, every sequence on exactly one rank, balanced
+    by cached tokens."""
     sys.path.insert(0, str(ROOT))
     import bench
-    a = types.SimpleNamespace(seed=3, min_len=128, max_len=8192, batch=64)
+    a = types.SimpleNamespace(seed=3, min_len=128, max_len=8192, batch=64, scaling="strong")
     base = sorted(bench.seq_lengths(a, 0, 1))
     assert len(base) == 64
     for world in (2, 4, 8):
+        shards = [bench.seq_lengths(a, rank, world) for rank in range(world)]
+        assert sorted(sum(shards, [])) == base
+        assert all(len(sh) == 64 // world for sh in shards)
+        tokens = [sum(sh) for sh in shards]
+        assert max(tokens) - min(tokens) <= max(base)
+        assert bench.global_tokens_per_step(a, world) == 64
+
+
+def test_weak_scaling_gives_every_rank_the_one_gpu_batch():
+    sys.path.insert(0, str(ROOT))
+    import bench
+    a = types.SimpleNamespace(seed=3, min_len=128, max_len=8192, batch=64, scaling="weak")
+    base = sorted(bench.seq_lengths(a, 0, 1))
+    for world in (2, 4, 8):
         for rank in range(world):
             assert sorted(bench.seq_lengths(a, rank, world)) == base
+        assert bench.global_tokens_per_step(a, world) == 64 * world
+
+
+def test_cpu_baseline_sample_is_the_whole_workload():
+    """The CPU baseline loops over all 64 sequences, so its mean context is
+    the workload's (not a longer or shorter subset)."""
+    sys.path.insert(0, str(ROOT))
+    import bench
+    a = types.SimpleNamespace(seed=3, min_len=128, max_len=8192, batch=64, scaling="strong")
+    lengths = bench.base_lengths(a)
+    rate, info = bench.cpu_reference_rate(lengths, 0.0)
+    assert rate > 0 and info["sequences"] == 64
+    assert info["mean_context"] == round(sum(lengths) / 64, 1)
+    assert bench.config_block(types.SimpleNamespace(**vars(a), gpus=1), lengths, 12)["context_mean"] == \
+        info["mean_context"]
 
 
 def test_reference_arm_other_ranks_exit_quietly():
@@ -57,6 +90,6 @@ def test_algorithmic_bytes_follow_the_formula():
     step, decode = bench.step_bytes([0, 63, 64])
     assert step == (2048 * 4 + 4) + (2048 * 67 + 4) + (2048 * 68 + 8)
     assert decode == (2048 * 1 + 2048 + 4) + (2048 * 64 + 2048 + 4) + (2048 * 65 + 2048 + 8)
-    a = types.SimpleNamespace(seed=3, min_len=128, max_len=8192, batch=64)
+    a = types.SimpleNamespace(seed=3, min_len=128, max_len=8192, batch=64, scaling="strong")
     step, _ = bench.step_bytes(bench.seq_lengths(a, 0, 1))
     assert 0.45e9 < step < 0.65e9          # ~546 MB per layer-step for 64 sequences of mean ~4 K

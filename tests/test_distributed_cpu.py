@@ -302,3 +302,68 @@ def test_peer_exchange_handle_failure_is_everyones_gloo():
     res = _run_peer_exchange(2, fail_handle_rank=1)
     for r in range(2):
         assert res[r][0] == "ValueError" and "rank 1: b2_ipc_handle: fake failure" in res[r][1]
+
+
+def _device_error_worker(rank, world, port, words, result):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        lib_mod = load_pkg("_lib")
+        dist_mod = load_pkg("distributed")
+        failed = dist_mod.agree_device_errors(words[rank])
+        out = ["raised" if failed else "clean", failed]
+        if failed:
+            # the recovery every rank then runs together: PeerExchange.reset()
+            # (fake IPC library; the barriers must pair up on every rank)
+            fake = _FakeIpcLib(rank, False)
+            lib_mod.load = lambda: fake
+            torch.cuda.get_device_properties = lambda dev: type("P", (), {"uuid": f"GPU-{rank}"})()
+            torch.cuda.synchronize = lambda dev=None: None
+            px = dist_mod.PeerExchange(1, device="cpu")
+            px.area.fill_(7)
+            px.reset()
+            out.append(int(px.area.abs().sum()))
+            px.close()
+        dist.barrier()
+        result[rank] = out
+    finally:
+        dist.destroy_process_group()
+
+
+def test_device_errors_agreed_by_every_rank_gloo():
+    """A bounded wait that ran out on one rank only (its dev_err word set, the
+    other's clear): every rank learns of it and raises, then all reset the
+    exchange areas together without waiting for one another in vain."""
+    lib = load_pkg("_lib")
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as mgr:
+        result = mgr.dict()
+        port = _free_port()
+        words = [0, lib.B2_DEV_TIMEOUT]
+        procs = [ctx.Process(target=_device_error_worker, args=(r, 2, port, words, result)) for r in range(2)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(120)
+            assert p.exitcode == 0
+        res = dict(result)
+    for r in range(2):
+        assert res[r][0] == "raised", res
+        assert res[r][1] == ["rank 1: a bounded device wait ran out"], res
+        assert res[r][2] == 0      # the area is zero after reset()
+
+
+def test_device_errors_clean_on_every_rank_gloo():
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as mgr:
+        result = mgr.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_device_error_worker, args=(r, 2, port, [0, 0], result)) for r in range(2)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(120)
+            assert p.exitcode == 0
+        res = dict(result)
+    assert res[0] == ["clean", []] and res[1] == ["clean", []]

@@ -127,3 +127,56 @@ def test_prefill_oracle_matches_hf(path):
                                          w["q_gamma"], w["k_gamma"])
     assert np.array_equal(orc.bits(ctx), f["context"])
     assert k_all.shape == (8, past + t, 64)
+
+
+def sum_squares64_kernel_order(x: np.ndarray) -> np.ndarray:
+    """The order in which the decode and append kernels add the 64 rounded
+    squares of a head vector (csrc/b2_attn.cu, sum_squares64), restated in
+    numpy float32 with no fused multiply-add: v_k = squares 8k..8k+7,
+    a_k = v_k + v_{k+4}, p = ((a_0 + a_1) + a_2) + a_3 lane-wise, then the 8
+    lanes of p added left to right."""
+    f32 = np.float32
+    sq = (x.astype(f32) * x.astype(f32)).astype(f32)
+    v = [sq[:, 8 * k: 8 * k + 8] for k in range(8)]
+    a = [(v[k] + v[k + 4]).astype(f32) for k in range(4)]
+    p = (((a[0] + a[1]).astype(f32) + a[2]).astype(f32) + a[3]).astype(f32)
+    s = p[:, 0].copy()
+    for lane in range(1, 8):
+        s = (s + p[:, lane]).astype(f32)
+    return s
+
+
+@pytest.mark.parametrize("scale", [1e-3, 0.6, 1.0, 37.0])
+def test_kernel_sum_order_is_torch_mean_order(scale):
+    """torch's CPU x.pow(2).mean(-1) of a contiguous 64-float row (the
+    variance of Lfm2RMSNorm, modeling_lfm2.py:59-64) equals the kernels'
+    summation order divided by 64, bit for bit, on 100 000 bf16 rows.  This
+    pins the order the append kernels reproduce for a bit-exact KV append."""
+    g = torch.Generator().manual_seed(int(scale * 1000))
+    x = (torch.randn(100_000, 64, generator=g) * scale).to(torch.bfloat16).float()
+    ref = x.pow(2).mean(-1).numpy()
+    got = sum_squares64_kernel_order(x.numpy()) / np.float32(64)
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
+def test_kernel_sum_order_on_golden_heads():
+    """The same on every q/k head vector of the transformers fixtures."""
+    for path in CASES:
+        f = _load(path)
+        x = np.concatenate([orc.from_bits(f["q_raw"]).reshape(16, 64).float().numpy(),
+                            orc.from_bits(f["k_raw"]).reshape(8, 64).float().numpy()])
+        ref = torch.from_numpy(x).pow(2).mean(-1).numpy()
+        got = sum_squares64_kernel_order(x) / np.float32(64)
+        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), path.stem
+
+
+def test_package_rope_table_matches_hf():
+    """The product's RoPE table (rope.rope_table, what every kernel reads)
+    against transformers' Lfm2RotaryEmbedding at the fixture's positions,
+    up to 131 136 (the long-context config's range)."""
+    from conftest import load_pkg
+    f = _load(GOLDEN / "lfm2_rope.npz")
+    pos = np.asarray(f["positions"], dtype=np.int64)
+    cos, sin = load_pkg("rope").rope_table(int(pos.max()) + 1, device="cpu")
+    assert np.array_equal(orc.bits(cos[pos]), f["cos"])
+    assert np.array_equal(orc.bits(sin[pos]), f["sin"])

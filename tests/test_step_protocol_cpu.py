@@ -3,8 +3,8 @@
 step_merger), checked under random schedules.
 
 Roles: the producer warp fills a ring of 4 stages (a stage = one block's K
-and V tiles plus its StageMeta) item after item and ends with a marker on
-the next stage; four consumer warps take every stage, run an epilogue at the
+and V tiles plus its StageMeta) item after item, ends with a marker on the
+next stage and waits for its last copy on every other stage; four consumer warps take every stage, run an epilogue at the
 last block of an item (a barrier of the four warps, `ebar`, around a
 reduction array double-buffered by epilogue parity) and, for items of a
 sequence split over several CTAs, publish the item to the merger warp
@@ -80,6 +80,12 @@ class StepCTA:
         self.stage[s] = "end"
         self.stage_readers[s] = set(range(WARPS))
         self.bar[f"full{s}"].arrive()                         # the end marker: a plain arrival
+        marker = s
+        # drain: the last copy issued on every other stage has landed before
+        # the producer leaves (the marker's stage: released above)
+        for st in range(min(STAGES, issued)):
+            if st != marker:
+                yield ("wait", f"full{st}", (issued - 1 - st) // STAGES)
 
     def consumer(self, w):
         ephase, epilogues, pubs = 0, 0, 0
