@@ -88,6 +88,9 @@ def parse():
     p.add_argument("--scaling", choices=["strong", "weak"], default="strong",
                    help="c3 with N GPUs: shard the one 64-sequence batch (strong) or give every GPU a copy (weak)")
     p.add_argument("--no-sweep", action="store_true", help="c3: skip the vs-context points")
+    p.add_argument("--shard", type=str, default="",
+                   help="c3 on one GPU: run only rank R's shard of an N-GPU job, given as R/N "
+                        "(its sequences and work, to study one rank of the scaling runs)")
     return p.parse_args()
 
 
@@ -468,7 +471,13 @@ def run_b200(args):
         import datetime
         torch.distributed.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
         pg = torch.distributed.group.WORLD
-    wl = build_workload(args, rank, dev, world)
+    if args.shard:
+        if world != 1:
+            raise SystemExit("--shard runs one rank's shard in a single process")
+        srank, sworld = (int(x) for x in args.shard.split("/"))
+        wl = build_workload(args, srank, dev, sworld)
+    else:
+        wl = build_workload(args, rank, dev, world)
     runner = wl["runner"]
     K, W, ring = args.steps, args.warmup, wl["ring"]
     stream = torch.cuda.Stream(dev)
@@ -605,6 +614,9 @@ def run_b200(args):
     kv_tokens = sum(n + 1 for n in lengths)
     step_gbs = sbytes / (ms_step / 1e3) / 1e9
     all_lengths = base_lengths(args) * (world if args.scaling == "weak" else 1)
+    if args.shard:
+        tokens = len(lengths)   # only this shard's sequences were decoded
+        value = tokens * K / (ms / 1e3)
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
         "warmup": W, "ms_per_step": ms_step, "higher_is_better": True, "scaling": args.scaling,
@@ -620,11 +632,15 @@ def run_b200(args):
         "e2e": {"value": tokens * e2e_steps / (e2e_ms / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": nb * (2048 * 2 + (4 if runner.fused else 8)),
                 "d2h_bytes_per_step": nb * HQ * D * 2, "steps": e2e_steps},
-        "gpu_launches": (1 if runner.fused else 3) * K,
+        # the fused step, plus the combine kernel when a sequence has more than 16 splits
+        "gpu_launches": ((1 + (runner.num_splits > 16)) if runner.fused else 3) * K,
     }
-    if rank == 0 and world == 1 and not args.no_sweep:
+    if args.shard:
+        line["config"]["shard"] = args.shard
+        line["config"]["workload"] += f"; ONLY shard {args.shard} of it on this GPU (one rank's part)"
+    if rank == 0 and world == 1 and not args.no_sweep and not args.shard:
         line["contexts"] = context_sweep(args, dev)
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.shard:
         rate, info = cpu_reference_rate(base_lengths(args), args.cpu_seconds)
         line["cpu_baseline"] = {"value": rate, "unit": "tokens/s", "cores": torch.get_num_threads(),
                                 "kind": "port", "sample": "reference CPU path (transformers Lfm2Attention "

@@ -27,7 +27,10 @@ extern "C" {
  * sum = bf16(x + residual) (skipped when residual is NULL: sum = x), then
  * norm_out = bf16(gamma * bf16(sum * rsqrt(mean(sum^2) + eps))), per row of
  * `width` values (width % 8 == 0, width <= 4096).  sum_out (may alias
- * residual or x) receives sum when not NULL.  Replaces the reference's
+ * residual or x) receives sum when not NULL.  For width % 32 == 0 the result
+ * is bit-identical to the reference's CPU path (torch's Lfm2RMSNorm): the
+ * squares are summed in torch's CPU reduction order and rsqrt is 1 / sqrt
+ * with IEEE-rounded sqrt and divide.  Replaces the reference's
  * RMSNorm kernels (experiments/kernels/lfm25_rms_norm.cc:21-40,
  * experiments/kernels/x8/x8_math.h:126-148) and the residual adds between
  * them.

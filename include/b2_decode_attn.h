@@ -198,9 +198,11 @@ int b2_combine(const float *part_ml, const float *part_o, int32_t num_parts,
  * one split is written to out directly, the others leave partial states in
  * part_ml/part_o and the last split of a (sequence, kv head) to finish
  * merges them (a dedicated warp per CTA counts the arrivals and merges, off
- * the path of the warps that stream the cache).  With more than 16 splits
- * per sequence the merge is left to the parallel combine kernel, which this
- * call launches after the decode kernel as a programmatic dependent.
+ * the path of the warps that stream the cache; one split per lane of that
+ * warp, so all splits' loads are in flight together).  With more than 16
+ * splits per sequence the merge is left to the parallel combine kernel,
+ * which this call launches after the decode kernel as a programmatic
+ * dependent.
  *
  * seq_lens     NULL: attend over past_lens[b] + 1 tokens (the usual decode
  *              step).  Otherwise tokens attended per sequence; with
@@ -214,7 +216,8 @@ int b2_combine(const float *part_ml, const float *part_o, int32_t num_parts,
  * counters     int32 [b2_decode_step_counters(batch)] (= 2 + 8 * batch); must be zero
  *              before the first call; every call that completes leaves it
  *              zero again (after a device error, zero it again).
- * part_ml/o    as b2_decode_attn with num_splits = ceil(max_blocks / bps).
+ * part_ml/o    as b2_decode_attn with num_splits = ceil(max_blocks / bps);
+ *              16-byte aligned (as are state_ml / state_o).
  * blocks_per_split  1 .. 64.
  * q_out        optional bf16 [batch][16][64] normalised + rotated q.
  * Calls sharing `counters` must not overlap on the GPU.

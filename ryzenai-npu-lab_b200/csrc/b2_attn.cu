@@ -824,7 +824,7 @@ constexpr int kProducerWarp = kConsumerWarps;
 constexpr int kMergerWarp = kConsumerWarps + 1;
 constexpr int kStepThreads = (kConsumerWarps + 2) * 32;
 constexpr int kPubSlots = 4;  // items published to the merger warp, in flight
-constexpr int kMergeInKernelSplits = 16;
+constexpr int kMergeInKernelSplits = 16;  // at most 32: one split per merger lane
 constexpr int kStepMaxBlocksPerSplit = 64;  // two block-table entries per producer lane
 
 struct __align__(16) StepTail {
@@ -1240,9 +1240,13 @@ __device__ __forceinline__ void publish(const StepArgs &a, StepTail *tail, int l
 }
 
 // Merger warp: for every published item, count its arrival for (sequence,
-// kv head); the last split to arrive merges all splits of the sequence
-// (lane owns dims 2*lane, 2*lane+1 of both query heads) into the bf16
-// context, or into the fp32 state when the caller asked for states.
+// kv head); the last split to arrive merges all splits of the sequence (at
+// most kMergeInKernelSplits) into the bf16 context, or into the fp32 state
+// when the caller asked for states.  The merge keeps every split's loads in
+// flight together (it runs at the tail of the launch for the last sequences):
+// lane sp loads split sp's (max, sum) of both heads, the warp reduces the
+// maximum and the rescaled sums with shuffles, then each lane accumulates its
+// two dims of both heads over the splits, loading eight splits per round.
 __device__ __forceinline__ void step_merger(const StepArgs &a, StepTail *tail, int lane) {
   for (uint32_t k = 0;; ++k) {
     const int slot = k % kPubSlots;
@@ -1266,31 +1270,53 @@ __device__ __forceinline__ void step_merger(const StepArgs &a, StepTail *tail, i
     __syncwarp();
     if (!last) continue;
     const int64_t base = (int64_t)b * a.num_splits * kHq + 2 * kvh;  // (b, split 0, head 2kvh)
+    // (max, sum) of heads 2kvh and 2kvh+1 of split `lane`: 4 adjacent floats
+    float4 ml = make_float4(-1.0e30f, 0.f, -1.0e30f, 0.f);
+    if (lane < nsplit) ml = __ldcg(reinterpret_cast<const float4 *>(a.part_ml + (base + (int64_t)lane * kHq) * 2));
+    float M0 = ml.x, M1 = ml.z;
 #pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      const float *ml = a.part_ml + (base + hh) * 2;
-      const float *po = a.part_o + (base + hh) * kDim + 2 * lane;
-      float M = -1.0e30f, L = 0.f, O0 = 0.f, O1 = 0.f;
-      for (int sp = 0; sp < nsplit; ++sp) {
-        const float ms = __ldcg(ml + sp * kHq * 2), ls = __ldcg(ml + sp * kHq * 2 + 1);
-        const float2 o = __ldcg(reinterpret_cast<const float2 *>(po + (int64_t)sp * kHq * kDim));
-        const float nm = fmaxf(M, ms);
-        const float c1 = ex2(M - nm), c2 = ex2(ms - nm);
-        L = L * c1 + ls * c2;
-        O0 = O0 * c1 + o.x * c2;
-        O1 = O1 * c1 + o.y * c2;
-        M = nm;
-      }
-      const int64_t oi = ((int64_t)b * kHq + 2 * kvh + hh) * kDim + 2 * lane;
-      if (a.direct_out) {
-        *reinterpret_cast<uint32_t *>(a.out + oi) = bf16_bits(O0 / L) | (bf16_bits(O1 / L) << 16);
-      } else {
-        *reinterpret_cast<float2 *>(a.state_o + oi) = make_float2(O0, O1);
-        if (lane == 0) {
-          a.state_ml[((int64_t)b * kHq + 2 * kvh + hh) * 2] = M;
-          a.state_ml[((int64_t)b * kHq + 2 * kvh + hh) * 2 + 1] = L;
+    for (int off = 16; off > 0; off >>= 1) {
+      M0 = fmaxf(M0, __shfl_xor_sync(0xffffffffu, M0, off));
+      M1 = fmaxf(M1, __shfl_xor_sync(0xffffffffu, M1, off));
+    }
+    const float c0 = ex2(ml.x - M0), c1 = ex2(ml.z - M1);  // lanes past nsplit carry l = 0
+    float L0 = ml.y * c0, L1 = ml.w * c1;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      L0 += __shfl_xor_sync(0xffffffffu, L0, off);
+      L1 += __shfl_xor_sync(0xffffffffu, L1, off);
+    }
+    float2 O0 = make_float2(0.f, 0.f), O1 = make_float2(0.f, 0.f);
+    for (int s0 = 0; s0 < nsplit; s0 += 8) {
+      float2 v0[8], v1[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        v0[e] = v1[e] = make_float2(0.f, 0.f);
+        if (s0 + e < nsplit) {
+          const float *po = a.part_o + (base + (int64_t)(s0 + e) * kHq) * kDim + 2 * lane;
+          v0[e] = __ldcg(reinterpret_cast<const float2 *>(po));
+          v1[e] = __ldcg(reinterpret_cast<const float2 *>(po + kDim));
         }
       }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float w0 = __shfl_sync(0xffffffffu, c0, (s0 + e) & 31);
+        const float w1 = __shfl_sync(0xffffffffu, c1, (s0 + e) & 31);
+        O0.x = fmaf(w0, v0[e].x, O0.x);
+        O0.y = fmaf(w0, v0[e].y, O0.y);
+        O1.x = fmaf(w1, v1[e].x, O1.x);
+        O1.y = fmaf(w1, v1[e].y, O1.y);
+      }
+    }
+    const int64_t oi = ((int64_t)b * kHq + 2 * kvh) * kDim + 2 * lane;
+    if (a.direct_out) {
+      *reinterpret_cast<uint32_t *>(a.out + oi) = bf16_bits(O0.x / L0) | (bf16_bits(O0.y / L0) << 16);
+      *reinterpret_cast<uint32_t *>(a.out + oi + kDim) = bf16_bits(O1.x / L1) | (bf16_bits(O1.y / L1) << 16);
+    } else {
+      *reinterpret_cast<float2 *>(a.state_o + oi) = O0;
+      *reinterpret_cast<float2 *>(a.state_o + oi + kDim) = O1;
+      if (lane == 0)
+        *reinterpret_cast<float4 *>(a.state_ml + ((int64_t)b * kHq + 2 * kvh) * 2) = make_float4(M0, L0, M1, L1);
     }
     if (lane == 0) atomicExch(cnt, 0);
   }
@@ -2258,6 +2284,9 @@ int decode_step_impl(const uint16_t *qkv, int64_t row_stride, const uint16_t *ga
   if (blocks_per_split < 1 || blocks_per_split > kStepMaxBlocksPerSplit)
     return fail(B2_ERR_ARG, "blocks_per_split must be in [1, %d] (got %d)", kStepMaxBlocksPerSplit, blocks_per_split);
   if (!(scale > 0.f)) return fail(B2_ERR_ARG, "scale must be positive");
+  if (!aligned16(part_ml) || !aligned16(part_o) || (state_ml && !aligned16(state_ml)) ||
+      (state_o && !aligned16(state_o)))
+    return fail(B2_ERR_ARG, "part_ml, part_o, state_ml and state_o must be 16-byte aligned");
   const int64_t splits = (static_cast<int64_t>(max_blocks_per_seq) + blocks_per_split - 1) / blocks_per_split;
   const int64_t total = splits * batch * kHkv;
   if (total >= (int64_t(1) << 31)) return fail(B2_ERR_ARG, "too many work items");

@@ -50,14 +50,65 @@ __device__ __forceinline__ uint4 pack8(const float f[8]) {
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
+// Sum of the squares of one row, bit-identical to torch's CPU
+// x.pow(2).mean(-1) * width for a contiguous row of `width` floats (a multiple
+// of 32, at most 4096): ATen's vectorised inner sum over 8-float vectors v_m
+// (elements 8m..8m+7), read as rows of 4 vectors (row i = v_4i..v_4i+3)
+// summed into 4 lane-wise accumulators in a cascade of 16-row groups:
+//   S_gk = v_{4(16g)+k} + ... + v_{4(16g+15)+k}   (left to right from 0)
+//   A_k  = S_0k + S_1k + ...                      (left to right)
+//   P_k  = (rows past the last full group, left to right from 0) + A_k
+//   p    = ((P_0 + P_1) + P_2) + P_3, then its 8 lanes left to right.
+// sq holds the row's rounded squares; every thread of the CTA calls this.
+__device__ float torch_order_sum(const float *sq, int width, float *chains) {
+  const int rows = width / 32;
+  const int groups = rows / 16, tail = rows % 16;
+  const int nchains = (groups + (tail > 0)) * 32;  // (group, k, lane)
+  for (int c = threadIdx.x; c < nchains; c += blockDim.x) {
+    const int g = c >> 5, k = (c >> 3) & 3, l = c & 7;
+    const int r0 = 16 * g, r1 = g < groups ? r0 + 16 : r0 + tail;
+    float acc = sq[(4 * r0 + k) * 8 + l];
+    for (int i = r0 + 1; i < r1; ++i) acc = __fadd_rn(acc, sq[(4 * i + k) * 8 + l]);
+    chains[c] = acc;
+  }
+  __syncthreads();
+  float total = 0.f;
+  if (threadIdx.x < 32) {
+    const int k = threadIdx.x >> 3, l = threadIdx.x & 7;
+    float a = chains[threadIdx.x];
+    for (int g = 1; g < groups; ++g) a = __fadd_rn(a, chains[g * 32 + threadIdx.x]);
+    const float P = tail > 0 ? (groups > 0 ? __fadd_rn(chains[groups * 32 + threadIdx.x], a)
+                                           : chains[threadIdx.x])
+                             : a;
+    // p_l = ((P_0l + P_1l) + P_2l) + P_3l on lanes l = 0..7 (lane 8k + l holds P_kl)
+    const float p1 = __shfl_sync(0xffffffffu, P, 8 + l);
+    const float p2 = __shfl_sync(0xffffffffu, P, 16 + l);
+    const float p3 = __shfl_sync(0xffffffffu, P, 24 + l);
+    const float pl = __fadd_rn(__fadd_rn(__fadd_rn(P, p1), p2), p3);
+    total = __shfl_sync(0xffffffffu, pl, 0);
+#pragma unroll
+    for (int j = 1; j < 8; ++j) total = __fadd_rn(total, __shfl_sync(0xffffffffu, pl, j));
+    (void)k;
+    if (threadIdx.x == 0) chains[0] = total;
+  }
+  __syncthreads();
+  return chains[0];
+}
+
 // sum_out may alias x or residual: every thread reads its own chunks before
 // the barrier and writes only those chunks after it.
+// Lfm2RMSNorm: gamma * bf16(x * rsqrt(mean(x^2) + eps)) with the mean summed
+// in torch's CPU order (widths that are a multiple of 32) and rsqrt as
+// 1 / sqrt with IEEE-rounded sqrt and divide, as torch's CPU rsqrt computes it.
 __global__ void __launch_bounds__(kNormThreads)
     add_rmsnorm_kernel(const uint16_t *x, const uint16_t *residual, const uint16_t *__restrict__ gamma,
                        float eps, uint16_t *sum_out, uint16_t *__restrict__ norm_out, int width) {
+  __shared__ float sq[kNormThreads * 8 * kNormMaxChunks];
+  __shared__ float chains[kNormThreads * 8 * kNormMaxChunks / 32 / 16 * 32 + 32];
   __shared__ float red[kNormThreads / 32];
   const int64_t row = blockIdx.x;
   const int chunks = width / 8;
+  const bool torch_order = width % 32 == 0;
   float v[kNormMaxChunks][8];
   float ss = 0.f;
 #pragma unroll
@@ -72,17 +123,27 @@ __global__ void __launch_bounds__(kNormThreads)
         for (int e = 0; e < 8; ++e) v[k][e] = rnd(v[k][e] + r[e]);  // bf16 tensor add
       }
 #pragma unroll
-      for (int e = 0; e < 8; ++e) ss = fmaf(v[k][e], v[k][e], ss);
+      for (int e = 0; e < 8; ++e) {
+        const float q = __fmul_rn(v[k][e], v[k][e]);
+        if (torch_order) sq[c * 8 + e] = q;
+        else ss += q;
+      }
     }
   }
+  float tot;
+  if (torch_order) {
+    __syncthreads();
+    tot = torch_order_sum(sq, width, chains);
+  } else {
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-  __syncthreads();
-  float tot = 0.f;
+    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    tot = 0.f;
 #pragma unroll
-  for (int w = 0; w < kNormThreads / 32; ++w) tot += red[w];
-  const float inv = rsqrtf(tot / static_cast<float>(width) + eps);
+    for (int w = 0; w < kNormThreads / 32; ++w) tot += red[w];
+  }
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(width)), eps)));
 #pragma unroll
   for (int k = 0; k < kNormMaxChunks; ++k) {
     const int c = threadIdx.x + k * kNormThreads;
@@ -91,7 +152,7 @@ __global__ void __launch_bounds__(kNormThreads)
       float g[8], o[8];
       unpack8(reinterpret_cast<const uint4 *>(gamma)[c], g);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) o[e] = g[e] * rnd(v[k][e] * inv);
+      for (int e = 0; e < 8; ++e) o[e] = __fmul_rn(g[e], rnd(__fmul_rn(v[k][e], inv)));
       reinterpret_cast<uint4 *>(norm_out + row * width)[c] = pack8(o);
     }
   }
@@ -108,7 +169,7 @@ __global__ void swiglu_kernel(const uint16_t *__restrict__ gu, uint16_t *__restr
   unpack8(reinterpret_cast<const uint4 *>(gu + r * 2 * ffn)[c], g);
   unpack8(reinterpret_cast<const uint4 *>(gu + r * 2 * ffn + ffn)[c], u);
 #pragma unroll
-  for (int e = 0; e < 8; ++e) o[e] = rnd(g[e] / (1.0f + __expf(-g[e]))) * u[e];
+  for (int e = 0; e < 8; ++e) o[e] = __fmul_rn(rnd(__fdiv_rn(g[e], 1.0f + expf(-g[e]))), u[e]);
   reinterpret_cast<uint4 *>(out + r * ffn)[c] = pack8(o);
 }
 

@@ -11,6 +11,7 @@ available, so the inputs are the seeded generators of oracle/lfm2_attention.py;
 a sha256 of every regenerated input is stored to pin the generators.
 
 Run from the repository root:  python tests/golden/make_golden.py
+(`--only greedy` / `--only greedy_free` regenerates only that greedy fixture).
 Nothing at test time imports transformers; tests read the .npz files.
 """
 from __future__ import annotations
@@ -161,14 +162,22 @@ def greedy_case() -> dict:
     """The reference's CPU greedy loop (experiments/010_cpu_greedy.py:43-63):
     Lfm2ForCausalLM in BF16, one token per forward with a DynamicCache, argmax.
     Records, for every step, the input ids and the top-8 logits (values and
-    indices) so that a GPU runner can be checked teacher-forced."""
+    indices) so that a GPU runner can be checked teacher-forced.  The same
+    inputs are also run with transformers' eager attention (the reference's
+    other CPU attention path) and its logits at those top-8 ids recorded, to
+    show how far the reference's own implementations differ."""
     from transformers import Lfm2ForCausalLM
-    cfg = config("sdpa")
-    cfg.tie_word_embeddings = True
-    model = Lfm2ForCausalLM(cfg).to(BF16).eval()
     sd = orc.lfm2_model_weights(GREEDY_SEED)
-    model.load_state_dict(sd, strict=True)
-    model.tie_weights()
+
+    def model_for(impl):
+        cfg = config(impl)
+        cfg.tie_word_embeddings = True
+        model = Lfm2ForCausalLM(cfg).to(BF16).eval()
+        model.load_state_dict(sd, strict=True)
+        model.tie_weights()
+        return model, cfg
+
+    model, cfg = model_for("sdpa")
     g = torch.Generator().manual_seed(GREEDY_SEED + 1)
     prompt = torch.randint(0, cfg.vocab_size, (GREEDY_BATCH, GREEDY_PROMPT), generator=g)
     cache = DynamicCache(config=cfg)
@@ -183,14 +192,79 @@ def greedy_case() -> dict:
             topv.append(v)
             topi.append(i)
             nxt = logits.argmax(-1)
-    return {"inputs": torch.stack(inputs, 1).numpy(), "top_values": torch.stack(topv, 1).numpy(),
-            "top_indices": torch.stack(topi, 1).numpy(), "prompt_len": np.int64(GREEDY_PROMPT),
-            "weight_seed": np.int64(GREEDY_SEED),
+    inputs, topi = torch.stack(inputs, 1), torch.stack(topi, 1)
+    eager, ecfg = model_for("eager")
+    cache = DynamicCache(config=ecfg)
+    eager_v = []
+    with torch.no_grad():
+        for t in range(inputs.shape[1]):
+            logits = eager(inputs[:, t:t + 1], past_key_values=cache, use_cache=True).logits[:, -1].float()
+            eager_v.append(torch.gather(logits, 1, topi[:, t]))
+    return {"inputs": inputs.numpy(), "top_values": torch.stack(topv, 1).numpy(),
+            "top_indices": topi.numpy(), "eager_top_values": torch.stack(eager_v, 1).numpy(),
+            "prompt_len": np.int64(GREEDY_PROMPT), "weight_seed": np.int64(GREEDY_SEED),
+            "model_weights_sha256": sha(*[sd[k] for k in sorted(sd) if k != "lm_head.weight"])}
+
+
+FREE_SEED = 7
+FREE_PROMPTS, FREE_PROMPT_LEN, FREE_NEW, FREE_TOPK = 16, 32, 64, 4
+EOS_ID = 7   # experiments/010_cpu_greedy.py:19
+
+
+def greedy_free_case() -> dict:
+    """Free-running greedy generation with the reference's CPU loop, prompt by
+    prompt exactly as experiments/010_cpu_greedy.py:46-63 runs it (batch 1,
+    the prompt fed one token per forward with a DynamicCache, then argmax fed
+    back until FREE_NEW tokens or EOS): the C5 model shape (random init,
+    seeded), 16 prompts of 32 random ids, 64 new tokens each.  Records the
+    generated ids and, at every generated step, the top-FREE_TOPK logits
+    (the bf16 values as float32, and their ids), so a divergence can be
+    judged against the reference's own top-2 margin at that step."""
+    from transformers import Lfm2ForCausalLM
+    cfg = config("sdpa")
+    cfg.tie_word_embeddings = True
+    model = Lfm2ForCausalLM(cfg).to(BF16).eval()
+    sd = orc.lfm2_model_weights(FREE_SEED)
+    model.load_state_dict(sd, strict=True)
+    model.tie_weights()
+    g = torch.Generator().manual_seed(FREE_SEED + 1)
+    prompts = torch.randint(0, cfg.vocab_size, (FREE_PROMPTS, FREE_PROMPT_LEN), generator=g)
+    gen = np.full((FREE_PROMPTS, FREE_NEW), -1, dtype=np.int64)
+    topv = np.zeros((FREE_PROMPTS, FREE_NEW, FREE_TOPK), dtype=np.float32)
+    topi = np.zeros((FREE_PROMPTS, FREE_NEW, FREE_TOPK), dtype=np.int64)
+    with torch.inference_mode():
+        for s in range(FREE_PROMPTS):
+            past = DynamicCache(config=cfg)
+            for token in prompts[s].tolist():
+                out = model(torch.tensor([[token]]), past_key_values=past, use_cache=True)
+            for t in range(FREE_NEW):
+                logits = out.logits[0, -1]
+                v, i = logits.float().topk(FREE_TOPK)
+                topv[s, t], topi[s, t] = v.numpy(), i.numpy()
+                nxt = int(logits.argmax())
+                gen[s, t] = nxt
+                if nxt == EOS_ID or t == FREE_NEW - 1:
+                    break
+                out = model(torch.tensor([[nxt]]), past_key_values=past, use_cache=True)
+    return {"prompts": prompts.numpy(), "generated": gen, "top_values": topv, "top_indices": topi,
+            "weight_seed": np.int64(FREE_SEED), "eos_id": np.int64(EOS_ID),
             "model_weights_sha256": sha(*[sd[k] for k in sorted(sd) if k != "lm_head.weight"])}
 
 
 def main() -> None:
     torch.manual_seed(0)
+    if sys.argv[1:] == ["--only", "greedy"]:
+        weights = orc.attention_weights(WEIGHT_SEED)
+        meta = {"transformers": transformers.__version__, "torch": torch.__version__,
+                "weights_sha256": sha(*[weights[k] for k in sorted(weights)])}
+        np.savez_compressed(OUT / "lfm2_greedy.npz", **greedy_case(), **meta)
+        print("wrote lfm2_greedy.npz")
+        return
+    if sys.argv[1:] == ["--only", "greedy_free"]:
+        meta = {"transformers": transformers.__version__, "torch": torch.__version__}
+        np.savez_compressed(OUT / "lfm2_greedy_free.npz", **greedy_free_case(), **meta)
+        print("wrote lfm2_greedy_free.npz")
+        return
     weights = orc.attention_weights(WEIGHT_SEED)
     meta = {"transformers": transformers.__version__, "torch": torch.__version__,
             "weights_sha256": sha(*[weights[k] for k in sorted(weights)])}
@@ -214,6 +288,8 @@ def main() -> None:
         np.savez_compressed(OUT / f"lfm2_prefill_P{past}_T{t}.npz", **prefill_case(past, t, weights), **meta,
                             weight_seed=np.int64(WEIGHT_SEED))
     np.savez_compressed(OUT / "lfm2_greedy.npz", **greedy_case(), **meta)
+    np.savez_compressed(OUT / "lfm2_greedy_free.npz", **greedy_free_case(),
+                        **{k: meta[k] for k in ("transformers", "torch")})
     print("wrote", sorted(p.name for p in OUT.glob("*.npz")))
 
 

@@ -1,9 +1,11 @@
 """The layer kernels around the attention path (include/b2_block.h) against
-the same operations written in torch on the GPU, in the order of the model
-definition (transformers modeling_lfm2.py: Lfm2RMSNorm 59-64, Lfm2MLP
-135-152, Lfm2ShortConv.slow_forward 356-387, the decoder layer's residual
-adds 413-442).  bf16 results within one bf16 ulp, at least 99 % bit-exact
-(the GPU reductions and exp add in other orders than torch's); the
+the same operations written in torch, in the order of the model definition
+(transformers modeling_lfm2.py: Lfm2RMSNorm 59-64, Lfm2MLP 135-152,
+Lfm2ShortConv.slow_forward 356-387, the decoder layer's residual adds
+413-442).  The RMSNorm is bit-exact against torch on the CPU (the
+reference's path) for widths that are a multiple of 32 (its mean is summed
+in torch's CPU order); other bf16 results within one bf16 ulp and at least
+99 % bit-exact (exp and GPU reductions in other orders than torch's); the
 convolution state bit-exact."""
 import numpy as np
 import pytest
@@ -42,7 +44,12 @@ def test_add_rmsnorm(cuda, rows, width, with_residual):
     blk.add_rmsnorm(x, res, gamma, 1e-5, out=out, sum_out=sum_out)
     torch.cuda.synchronize()
     assert torch.equal(sum_out, s_ref)
-    _close(out, _rms_ref(s_ref, gamma, 1e-5), "rmsnorm")
+    ref = _rms_ref(s_ref.cpu(), gamma.cpu(), 1e-5)
+    if width % 32 == 0:
+        d = ulp_diff(out, ref)
+        assert (d == 0).all(), f"rmsnorm: {(d != 0).sum()} of {d.size} elements differ from torch CPU"
+    else:
+        _close(out, ref, "rmsnorm")
 
 
 def test_add_rmsnorm_in_place_on_the_residual(cuda):
@@ -56,7 +63,7 @@ def test_add_rmsnorm_in_place_on_the_residual(cuda):
     blk.add_rmsnorm(x, h, gamma, 1e-5, out=out, sum_out=h)
     torch.cuda.synchronize()
     assert torch.equal(h, s_ref)
-    _close(out, _rms_ref(s_ref, gamma, 1e-5), "rmsnorm in place")
+    assert torch.equal(out.cpu(), _rms_ref(s_ref.cpu(), gamma.cpu(), 1e-5)), "rmsnorm in place"
 
 
 @pytest.mark.parametrize("rows,ffn", [(1, 2560), (256, 2560), (3, 8)])

@@ -1,13 +1,19 @@
 """Whole-model decode (config C5 shape) through the paged attention path,
-checked teacher-forced against the reference's CPU greedy loop
-(transformers Lfm2ForCausalLM in BF16, one token per forward:
-experiments/010_cpu_greedy.py:43-63; fixture tests/golden/lfm2_greedy.npz).
+against the reference's CPU greedy loop (transformers Lfm2ForCausalLM in
+BF16, one token per forward: experiments/010_cpu_greedy.py:43-63).
 
-The reference's own criterion (experiments/010_x8_engine.md:65-69) is that
-greedy ids agree except at exact bf16 top-2 ties.  The GPU's GEMMs add in a
-different order than the CPU's, so a logit may move by about one bf16 ulp;
-a differing argmax is accepted only where the reference's top candidates lie
-within 2 ulps of each other, and the chosen id must be one of them.
+The reference's own criterion compares the generated id sequences token for
+token (experiments/010_compare.py:33-51) and explains a divergence by the CPU
+logits at that step: an exact bf16 top-2 tie, or top-2 logits one bf16 step
+apart (experiments/010_x8_engine.md:59-69).  Logits are not bit-exact across
+implementations: the reference's own two CPU attention paths (sdpa and
+eager) differ by up to 2 bf16 ulps at the top candidates
+(tests/test_oracle.py::test_reference_cpu_paths_differ_by_a_few_ulps), and
+the GPU's GEMMs and split softmax (fp32, other orders) land within 3 ulps of
+the sdpa path.  So every logit at the reference's top-8 must be within
+TIE_ULPS = 3 ulps of the reference's, every greedy choice must equal the
+reference's except where the reference's top candidates lie within those
+3 ulps, and then it must be one of them.
 """
 import hashlib
 import pathlib
@@ -21,6 +27,14 @@ from oracle import lfm2_attention as orc
 
 pytestmark = pytest.mark.gpu
 GOLDEN = pathlib.Path(__file__).resolve().parent / "golden" / "lfm2_greedy.npz"
+FREE = pathlib.Path(__file__).resolve().parent / "golden" / "lfm2_greedy_free.npz"
+
+
+TIE_ULPS = 3
+
+
+def bf16_ulp(x: float) -> float:
+    return 2.0 ** (np.floor(np.log2(abs(x))) - 7)
 
 
 def _weights(f):
@@ -36,6 +50,10 @@ def _weights(f):
 @pytest.mark.parametrize("fused_glue", [True, False], ids=["kernels", "torch_glue"])
 @pytest.mark.parametrize("use_graph", [True, False], ids=["graph", "eager"])
 def test_greedy_teacher_forced_matches_reference(cuda, use_graph, fused_glue):
+    """Teacher-forced (the reference's inputs at every step): the logits at the
+    reference's top-8 within TIE_ULPS bf16 ulps of the reference's; the argmax
+    equals the reference's except where its top logits are within TIE_ULPS
+    ulps of each other, and then it is one of those."""
     f = dict(np.load(GOLDEN))
     runner_mod = load_pkg("lfm2_runner")
     inputs = f["inputs"]                      # [B, T]
@@ -43,26 +61,57 @@ def test_greedy_teacher_forced_matches_reference(cuda, use_graph, fused_glue):
     b, steps = inputs.shape
     runner = runner_mod.LFM2DecodeRunner(_weights(f), max_batch=b, max_context=64, device=cuda,
                                          use_graph=use_graph, fused_glue=fused_glue)
-    exact = mismatches = 0
-    worst = 0.0
+    ulps, flips = [], []
     for t in range(steps):
         nxt = runner.step(torch.from_numpy(inputs[:, t])).cpu().numpy()
         logits = runner.logits.float().cpu().numpy()
         for s in range(b):
             ref_ids, ref_vals = top_i[s, t], top_v[s, t]
-            worst = max(worst, float(np.abs(logits[s, ref_ids] - ref_vals).max()))
-            if nxt[s] == ref_ids[0]:
-                exact += 1
-                continue
-            ulp = 2.0 ** (np.floor(np.log2(abs(ref_vals[0]))) - 7)
-            near = ref_ids[ref_vals >= ref_vals[0] - 2 * ulp]
-            assert nxt[s] in near, f"step {t} seq {s}: got {nxt[s]}, reference top {ref_ids[:3]} {ref_vals[:3]}"
-            mismatches += 1
+            ulps.extend(np.abs(logits[s, ref_ids] - ref_vals) / np.array([bf16_ulp(v) for v in ref_vals]))
+            if nxt[s] != ref_ids[0]:
+                flips.append((t, s, int(nxt[s]), ref_ids[:3].tolist(), ref_vals[:3].tolist()))
     runner.check()
-    assert worst <= 0.0625, f"logits differ by {worst} at the reference's top-8"
-    assert exact >= 0.8 * b * steps, f"only {exact} of {b * steps} argmax exact"
+    hist = np.bincount(np.minimum(np.round(ulps).astype(int), 8))
+    print(f"logit differences at the reference's top-8, in bf16 ulps (0..8+): {hist.tolist()}; flips {flips}")
+    assert len(hist) <= TIE_ULPS + 1, f"logits beyond {TIE_ULPS} ulps of the reference: {hist.tolist()}"
+    for t, s, got, ids, vals in flips:
+        near = [i for i, v in zip(ids, vals) if v >= vals[0] - TIE_ULPS * bf16_ulp(vals[0])]
+        assert got in near, f"step {t} seq {s}: got {got}, reference top {ids} {vals}"
     k, v = runner.kv(0, 0, steps - 1)
     assert k.shape == (8, steps, 64) and torch.isfinite(k.float()).all() and torch.isfinite(v.float()).all()
+
+
+def test_greedy_free_running_matches_reference(cuda):
+    """Free-running greedy generation, as the reference's 010_compare.py runs
+    it: 16 prompts of 32 random ids (C5 model shape), 64 new tokens each, the
+    GPU feeding back its own choices.  Each prompt's generated ids equal the
+    reference's up to the first divergence, and a divergence is accepted only
+    at a step where the GPU's choice is among the reference's candidates
+    within TIE_ULPS bf16 ulps of its top logit (the comparison of that prompt
+    ends there, as the two generations then continue from different tokens)."""
+    f = dict(np.load(FREE))
+    runner_mod = load_pkg("lfm2_runner")
+    prompts, ref = f["prompts"], f["generated"]
+    top_v, top_i = f["top_values"], f["top_indices"]
+    n, new = ref.shape
+    runner = runner_mod.LFM2DecodeRunner(_weights(f), max_batch=n, max_context=prompts.shape[1] + new + 1,
+                                         device=cuda)
+    got = runner.generate(torch.from_numpy(prompts), new).cpu().numpy()
+    runner.check()
+    compared, report = 0, []
+    for s in range(n):
+        diff = np.nonzero(got[s] != ref[s])[0]
+        first = int(diff[0]) if diff.size else new
+        compared += first
+        if first == new:
+            continue
+        v, i = top_v[s, first], top_i[s, first]
+        report.append((s, first, int(got[s, first]), int(i[0]), int(i[1]), float(v[0] - v[1])))
+        near = i[v >= v[0] - TIE_ULPS * bf16_ulp(v[0])]
+        assert got[s, first] in near, \
+            f"prompt {s} diverges at token {first}: got {got[s, first]}, reference top {i[:3]} {v[:3]}"
+    print(f"greedy free-running: {compared} of {n * new} tokens identical before any divergence; "
+          f"divergences (prompt, token, got, ref top-1, top-2, margin): {report}")
 
 
 def test_generate_and_reset(cuda):

@@ -180,3 +180,17 @@ def test_package_rope_table_matches_hf():
     cos, sin = load_pkg("rope").rope_table(int(pos.max()) + 1, device="cpu")
     assert np.array_equal(orc.bits(cos[pos]), f["cos"])
     assert np.array_equal(orc.bits(sin[pos]), f["sin"])
+
+
+def test_reference_cpu_paths_differ_by_a_few_ulps():
+    """The reference's own two CPU attention paths (transformers sdpa, which
+    produced the greedy fixture, and eager) on the same teacher-forced inputs
+    of the C5-shaped model: their logits at the sdpa top-8 differ by up to
+    2 bf16 ulps (GEMM and softmax roundings in another order), and the
+    greedy choice can differ where the top candidates are that close.  This
+    is the noise floor against which the GPU runner's greedy parity is read."""
+    f = _load(GOLDEN / "lfm2_greedy.npz")
+    v, e = f["top_values"], f["eager_top_values"]
+    ulp = 2.0 ** (np.floor(np.log2(np.abs(v))) - 7)
+    d = np.round(np.abs(e - v) / ulp).astype(int)
+    assert d.max() == 2 and (d > 0).mean() > 0.3
