@@ -110,9 +110,13 @@ def choose_blocks_per_split(batch: int, work_blocks: int, sms: int = B200_SMS, f
     batch (one head).  Three-kernel path: about 8 CTAs of real work per SM
     (3 are resident at a time; the rest balance the tail).  Fused persistent
     kernel: about 6 items per resident CTA (items stream back to back, so they
-    can be smaller; the end-of-launch tail is one item).  Measured on the C3
-    workload: the fused kernel is within 1 % of its best for 8-16 blocks.
-    With many sequences of at most 32 blocks, one split per sequence.
+    can be smaller; the end-of-launch tail is one item), at least 6 blocks.
+    Measured on the C3 workload: the fused kernel is within 1 % of its best for
+    8-16 blocks; on its shards (8 / 16 / 32 sequences) the best are 6 / 6 / 8
+    blocks.  With many sequences of at most 32 blocks, one split per sequence.
+    The split grows to ceil(longest / 16) blocks when that still leaves about
+    3 items per resident CTA, so that a sequence has at most 16 splits and the
+    kernel's merger warp merges them without a combine launch.
     With a few sequences (a long context split over the CTAs) the items are
     all alike: about two per SM in one wave, every CTA streaming the same
     number of blocks (up to 64), finish together; measured on one 131 072-token
@@ -128,7 +132,14 @@ def choose_blocks_per_split(batch: int, work_blocks: int, sms: int = B200_SMS, f
             per_seq = math.ceil(work_blocks / max(1, batch))
             splits = max(1, (sms * 2) // (max(1, batch) * HKV))
             return int(max(1, min(64, math.ceil(per_seq / splits))))
-        return int(min(32, max(4, math.ceil(work_blocks * HKV / (sms * 3 * 6)))))
+        bps = int(min(32, max(6, math.ceil(work_blocks * HKV / (sms * 3 * 6)))))
+        # at most 16 splits per sequence (merged by the kernel's merger warp, no
+        # combine launch) when that still leaves ~3 items per resident CTA
+        merge_bps = math.ceil(per_seq_max / 16)
+        items = HKV * (work_blocks / merge_bps + batch)
+        if bps < merge_bps <= 64 and items >= 3 * (3 * sms):
+            bps = int(merge_bps)
+        return bps
     target = 8 * sms
     return int(min(64, max(2, math.ceil(work_blocks * HKV / target))))
 

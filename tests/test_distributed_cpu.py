@@ -154,6 +154,11 @@ def test_split_size_heuristic():
     assert attn.choose_blocks_per_split(1, 4097, fused=True) == 64      # capped: several equal waves
     # many sequences: ~6 items per resident CTA, 4..32 blocks
     assert attn.choose_blocks_per_split(64, 3715, fused=True) == 12
+    # the 64-sequence batch sharded over 2/4/8 GPUs (longest 129 blocks): the
+    # measured best split sizes; at 32 sequences at most 16 splits (merged in
+    # the kernel) with ~3 items per resident CTA
+    for batch, work, want in ((32, 1860, 9), (16, 930, 6), (8, 470, 6)):
+        assert attn.choose_blocks_per_split(batch, work, fused=True, max_blocks_per_seq=129) == want
     assert 4 <= attn.choose_blocks_per_split(512, 512 * 60, fused=True) <= 32
     # three-kernel path: ~8 CTAs of work per SM
     assert 2 <= attn.choose_blocks_per_split(64, 3715) <= 64
