@@ -1006,6 +1006,8 @@ def run_prefill(args):
         "config": {"workload": f"batched prompt: 64 sequences with cached L ~ U[128, 8192] each receiving "
                                f"{T} new tokens through one attention layer (chunk append + tcgen05 "
                                f"attention, causal within the chunk)", "chunk": T,
+                   "prefill_blocks_per_split": (attn.prefill_blocks_per_split(b, T, tables.shape[1])
+                                                if args.prefill_bps < 0 else args.prefill_bps),
                    "global_batch": b, "parallelism": "replicas"},
         "hbm_gbs_per_gpu": gbs, "tflops": flops / (ms / 1e3) / 1e12,
         "roofline": {"bound": "hbm", "kernel": "append_rope_kernel + prefill_attn_kernel", "achieved": gbs,
