@@ -170,6 +170,12 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
+// Expect `bytes` more of the current phase's transfer without arriving: the
+// phase completes once the bytes have landed and the arrival comes later.
+__device__ __forceinline__ void mbar_expect_tx_only(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
                : "memory");
@@ -882,12 +888,29 @@ __device__ __forceinline__ void consumers_sync(StepTail *tail, int lane, uint32_
 // Lengths of sequence b: past (RoPE position and, with B2_STORE_KV, the
 // append slot) and seq_len (tokens attended).  False for lengths the block
 // table cannot hold, or an append slot that is not the last attended token.
-__device__ __forceinline__ bool step_lengths(const StepArgs &a, int b, int &past, int &seq_len) {
-  past = __ldg(a.past_lens + b);
-  seq_len = a.seq_lens ? __ldg(a.seq_lens + b) : past + 1;
+__device__ __forceinline__ bool lengths_ok(const StepArgs &a, int past, int seq_len) {
   bool ok = past >= 0 && seq_len >= 0 && seq_len <= a.max_blocks * kBlock;
   if (a.mode & B2_STORE_KV) ok = ok && seq_len == past + 1;
   return ok;
+}
+
+__device__ __forceinline__ bool step_lengths(const StepArgs &a, int b, int &past, int &seq_len) {
+  past = __ldg(a.past_lens + b);
+  seq_len = a.seq_lens ? __ldg(a.seq_lens + b) : past + 1;
+  return lengths_ok(a, past, seq_len);
+}
+
+// Empty result of sequence e (nothing to attend): a zero context, or the
+// state (-inf, 0, 0).  One warp.
+__device__ __forceinline__ void write_empty_result(const StepArgs &a, int e, int lane) {
+  for (int i = lane; i < kHq * kDim; i += 32) {
+    if (a.direct_out) a.out[(int64_t)e * kHq * kDim + i] = 0;
+    else if (a.state_o) a.state_o[(int64_t)e * kHq * kDim + i] = 0.f;
+  }
+  if (!a.direct_out && a.state_ml && lane < kHq) {
+    a.state_ml[((int64_t)e * kHq + lane) * 2] = -1.0e30f;
+    a.state_ml[((int64_t)e * kHq + lane) * 2 + 1] = 0.f;
+  }
 }
 
 // One work item as the producer sees it, with its loads already issued.
@@ -952,16 +975,31 @@ __device__ __forceinline__ void step_producer(const StepArgs &a, StepTail *tail,
   const bool compact = a.batch <= kMaxCompactBatch;
   int total = a.total_items;
   if (compact) {
-    // prefix[b + 1] = sum of splits of sequences 0..b (inclusive warp scan per 32)
+    // prefix[b + 1] = sum of splits of sequences 0..b.  Every lane loads the
+    // lengths of its sequences (b = 32 k + lane) first, so that all the loads
+    // are in flight together (one round trip for any batch), then the 32-wide
+    // chunks are scanned in turn; CTA 0 also writes the empty results of the
+    // sequences with nothing to attend (they get no work item).
+    constexpr int kChunks = kMaxCompactBatch / 32;
+    int pl[kChunks], sl[kChunks];
+#pragma unroll
+    for (int k = 0; k < kChunks; ++k) {
+      const int b = 32 * k + lane;
+      pl[k] = b < a.batch ? __ldg(a.past_lens + b) : 0;
+      sl[k] = b < a.batch ? (a.seq_lens ? __ldg(a.seq_lens + b) : pl[k] + 1) : 0;
+    }
     int running = 0;
-    for (int base = 0; base < a.batch; base += 32) {
-      const int b = base + lane;
+#pragma unroll
+    for (int k = 0; k < kChunks; ++k) {
+      if (32 * k >= a.batch) break;
+      const int b = 32 * k + lane;
       int ns = 0;
+      bool empty = false;
       if (b < a.batch) {
-        int past, seq_len;
-        if (step_lengths(a, b, past, seq_len)) {
-          const int nblk = (seq_len + kBlock - 1) / kBlock;
+        if (lengths_ok(a, pl[k], sl[k])) {
+          const int nblk = (sl[k] + kBlock - 1) / kBlock;
           ns = (nblk + a.blocks_per_split - 1) / a.blocks_per_split;
+          empty = sl[k] == 0;
         } else if (blockIdx.x == 0) {
           atomicOr(a.err, B2_DEV_BAD_LENGTH);
         }
@@ -974,14 +1012,21 @@ __device__ __forceinline__ void step_producer(const StepArgs &a, StepTail *tail,
       }
       if (b < a.batch) tail->prefix[b + 1] = running + incl;
       running += __shfl_sync(0xffffffffu, incl, 31);
+      if (blockIdx.x == 0) {
+        unsigned mask = __ballot_sync(0xffffffffu, empty);
+        while (mask) {
+          const int e = 32 * k + __ffs(mask) - 1;
+          mask &= mask - 1;
+          write_empty_result(a, e, lane);
+        }
+      }
     }
     if (lane == 0) tail->prefix[0] = 0;
     __syncwarp();
     total = running * kHkv;
-  }
-  if (blockIdx.x == 0) {
+  } else if (blockIdx.x == 0) {
     // Sequences with nothing to attend (seq_lens[b] == 0) get no work item:
-    // write their empty result here (zero context, or the state (-inf, 0, 0)).
+    // write their empty result here.
     for (int b0 = 0; b0 < a.batch; b0 += 32) {
       const int b = b0 + lane;
       int past = 0, seq_len = 1;
@@ -990,14 +1035,7 @@ __device__ __forceinline__ void step_producer(const StepArgs &a, StepTail *tail,
       while (mask) {
         const int e = b0 + __ffs(mask) - 1;
         mask &= mask - 1;
-        for (int i = lane; i < kHq * kDim; i += 32) {
-          if (a.direct_out) a.out[(int64_t)e * kHq * kDim + i] = 0;
-          else if (a.state_o) a.state_o[(int64_t)e * kHq * kDim + i] = 0.f;
-        }
-        if (!a.direct_out && a.state_ml && lane < kHq) {
-          a.state_ml[((int64_t)e * kHq + lane) * 2] = -1.0e30f;
-          a.state_ml[((int64_t)e * kHq + lane) * 2 + 1] = 0.f;
-        }
+        write_empty_result(a, e, lane);
       }
     }
   }
@@ -1030,52 +1068,53 @@ __device__ __forceinline__ void step_producer(const StepArgs &a, StepTail *tail,
     if (lane == 0) w_next = atomicAdd(work_ctr, 1) + static_cast<int>(gridDim.x);
     const bool stores = cur.split == cur.nsplit - 1 && (a.mode & B2_STORE_KV);
     const int new_idx = stores ? cur.past / kBlock - cur.blk0 : -1;  // block receiving the new token
-
-    float x[8];
-    unpack8(cur.raw, x);
-    const bool rope_ok = cur.past < a.rope_rows;
-    if ((a.mode & B2_ROPE_QK) && !rope_ok && lane == 0 && cur.split == 0 && cur.kvh == 0)
-      atomicOr(a.err, B2_DEV_BAD_POSITION);
-    const bool rope = grp < 3 && (a.mode & B2_ROPE_QK) && rope_ok;
-    norm_rope8(x, j, norm, rope, grp < 2 ? a.gamma_q : a.gamma_k, a.eps,
-               rope ? a.cos + (int64_t)cur.past * kDim : nullptr,
-               rope ? a.sin + (int64_t)cur.past * kDim : nullptr);
-    const uint4 packed = pack8(x);
-    if (cur.split == 0 && grp < 2 && a.q_out)
-      *reinterpret_cast<uint4 *>(a.q_out + ((int64_t)cur.b * kHq + 2 * cur.kvh + grp) * kDim + j * 8) = packed;
-    if (stores) {
-      // The new token's row lies in this item's last block: write it, then
-      // fence so the TMA (async proxy) read of that tile sees the store.
-      const int idx = new_idx;  // < n <= 64, the same in every lane
-      const int blk = idx < 32 ? __shfl_sync(0xffffffffu, cur.my_blk, idx)
-                               : __ldg(a.block_tables + (int64_t)cur.b * a.max_blocks + cur.blk0 + idx);
-      if (blk < 0 || blk >= a.num_blocks) {
-        if (lane == 0) atomicOr(a.err, B2_DEV_BAD_BLOCK);
-      } else if (grp >= 2) {
-        uint16_t *pool = grp == 2 ? a.k_pool : a.v_pool;
-        *reinterpret_cast<uint4 *>(
-            pool + (((int64_t)blk * kHkv + cur.kvh) * kBlock + cur.past % kBlock) * kDim + j * 8) = packed;
-        asm volatile("fence.proxy.async.global;" ::: "memory");
+    // The q/k work of the item: norm + RoPE of its q, k (and the appended k/v
+    // rows with a fence, so the TMA read of that tile sees them).
+    uint4 packed = make_uint4(0u, 0u, 0u, 0u);
+    auto qk_work = [&]() {
+      float x[8];
+      unpack8(cur.raw, x);
+      const bool rope_ok = cur.past < a.rope_rows;
+      if ((a.mode & B2_ROPE_QK) && !rope_ok && lane == 0 && cur.split == 0 && cur.kvh == 0)
+        atomicOr(a.err, B2_DEV_BAD_POSITION);
+      const bool rope = grp < 3 && (a.mode & B2_ROPE_QK) && rope_ok;
+      norm_rope8(x, j, norm, rope, grp < 2 ? a.gamma_q : a.gamma_k, a.eps,
+                 rope ? a.cos + (int64_t)cur.past * kDim : nullptr,
+                 rope ? a.sin + (int64_t)cur.past * kDim : nullptr);
+      packed = pack8(x);
+      if (cur.split == 0 && grp < 2 && a.q_out)
+        *reinterpret_cast<uint4 *>(a.q_out + ((int64_t)cur.b * kHq + 2 * cur.kvh + grp) * kDim + j * 8) = packed;
+      if (stores) {
+        // The new token's row lies in this item's last block: write it, then
+        // fence so the TMA (async proxy) read of that tile sees the store.
+        const int idx = new_idx;  // < n <= 64, the same in every lane
+        const int nb = idx < 32 ? __shfl_sync(0xffffffffu, cur.my_blk, idx)
+                                : __ldg(a.block_tables + (int64_t)cur.b * a.max_blocks + cur.blk0 + idx);
+        if (nb < 0 || nb >= a.num_blocks) {
+          if (lane == 0) atomicOr(a.err, B2_DEV_BAD_BLOCK);
+        } else if (grp >= 2) {
+          uint16_t *pool = grp == 2 ? a.k_pool : a.v_pool;
+          *reinterpret_cast<uint4 *>(
+              pool + (((int64_t)nb * kHkv + cur.kvh) * kBlock + cur.past % kBlock) * kDim + j * 8) = packed;
+          asm volatile("fence.proxy.async.global;" ::: "memory");
+        }
       }
-    }
-    __syncwarp();
+    };
+    // The item's blocks go out in order, block jj into stage `issued`: wait
+    // (bounded) for the stage to be free, write its meta, copy K and V.
     int blk_hi = 0;  // block table entry blk0 + 32 + lane, read at jj == 32
-    for (int jj = 0; jj < cur.n; ++jj, ++issued) {
-      const int s = issued % kStages;
-      const uint32_t ph = (issued / kStages) & 1;
+    auto stage_free = [&](int s, uint32_t ph) -> bool {
       int wait_ok = 1;
       if (issued >= kStages && lane == 0) wait_ok = mbar_wait(smem_u32(&tail->empty[s]), ph ^ 1, a.wait_ns);
       wait_ok = __shfl_sync(0xffffffffu, wait_ok, 0);
-      if (!wait_ok) {
-        if (lane == 0) atomicOr(a.err, B2_DEV_TIMEOUT);
-        ok = false;
-        break;
-      }
+      if (!wait_ok && lane == 0) atomicOr(a.err, B2_DEV_TIMEOUT);
+      return wait_ok != 0;
+    };
+    auto write_meta = [&](int jj, int s) -> int {
       if (jj == 32)
         blk_hi = lane + 32 < cur.n ? __ldg(a.block_tables + (int64_t)cur.b * a.max_blocks + cur.blk0 + 32 + lane) : 0;
       int blk = __shfl_sync(0xffffffffu, jj < 32 ? cur.my_blk : blk_hi, jj & 31);
       StageMeta &m = tail->meta[s];
-      if (jj == 0 && grp < 2) *reinterpret_cast<uint4 *>(m.q + grp * kDim + j * 8) = packed;
       if (lane == 0) {
         if (blk < 0 || blk >= a.num_blocks) {
           atomicOr(a.err, B2_DEV_BAD_BLOCK);
@@ -1089,19 +1128,68 @@ __device__ __forceinline__ void step_producer(const StepArgs &a, StepTail *tail,
         m.flags = (jj == 0 ? kFlagFirst : 0) | (jj == cur.n - 1 ? kFlagLast : 0) |
                   (cur.nsplit == 1 && a.direct_out ? kFlagFinal : 0);
       }
+      return (blk * kHkv + cur.kvh) * kBlock;  // the tile's first row in the pool tensor map
+    };
+    // The first block.  While the ring fills (the start of the launch: the
+    // stage is certainly free) its copies go out before the q/k work and the
+    // stage's arrival waits until q is in its meta; later the q/k work runs
+    // first, overlapping the wait for a free stage, as the copies could not
+    // start earlier anyway.  A first block that receives the new token is
+    // copied after the store and its fence in either case.
+    const bool early = issued < kStages;
+    const bool first_later = new_idx == 0;
+    {
+      const int s = issued % kStages;
+      const uint32_t full = smem_u32(&tail->full[s]);
+      uint8_t *dst = tiles + s * kStageBytes;
+      int row = 0;
+      if (early) {
+        row = write_meta(0, s);
+        if (lane == 0) {
+          mbar_expect_tx_only(full, kStageBytes);
+          if (!first_later) {
+            tma_load_2d(smem_u32(dst), tm_k, 0, row, full, policy);
+            tma_load_2d(smem_u32(dst + kTileBytes), tm_v, 0, row, full, policy);
+          }
+        }
+      }
+      qk_work();
+      if (!early) {
+        if (!stage_free(s, (issued / kStages) & 1)) {
+          ok = false;
+          break;
+        }
+        row = write_meta(0, s);
+      }
+      if (grp < 2) *reinterpret_cast<uint4 *>(tail->meta[s].q + grp * kDim + j * 8) = packed;
+      __syncwarp();
+      if (lane == 0) {
+        if (!early) mbar_expect_tx(full, kStageBytes);  // arrival + expected bytes
+        if (!early || first_later) {
+          tma_load_2d(smem_u32(dst), tm_k, 0, row, full, policy);
+          tma_load_2d(smem_u32(dst + kTileBytes), tm_v, 0, row, full, policy);
+        }
+        if (early) mbar_arrive(full);  // q and the meta are in place (release)
+      }
+      ++issued;
+      // the first copy of this item is queued: load the next item now
+      w_next = __shfl_sync(0xffffffffu, w_next, 0);
+      nxt = producer_load(a, tail, compact, total, w_next, lane);
+    }
+    for (int jj = 1; jj < cur.n; ++jj, ++issued) {
+      const int s = issued % kStages;
+      if (!stage_free(s, (issued / kStages) & 1)) {
+        ok = false;
+        break;
+      }
+      const int row = write_meta(jj, s);
       __syncwarp();
       if (lane == 0) {
         const uint32_t full = smem_u32(&tail->full[s]);
-        const int row = (blk * kHkv + cur.kvh) * kBlock;
         uint8_t *dst = tiles + s * kStageBytes;
         mbar_expect_tx(full, kStageBytes);
         tma_load_2d(smem_u32(dst), tm_k, 0, row, full, policy);
         tma_load_2d(smem_u32(dst + kTileBytes), tm_v, 0, row, full, policy);
-      }
-      if (jj == 0) {
-        // the first copy of this item is queued: load the next item now
-        w_next = __shfl_sync(0xffffffffu, w_next, 0);
-        nxt = producer_load(a, tail, compact, total, w_next, lane);
       }
     }
     if (!ok) break;

@@ -4,7 +4,10 @@ step_merger), checked under random schedules.
 
 Roles: the producer warp fills a ring of 4 stages (a stage = one block's K
 and V tiles plus its StageMeta) item after item, ends with a marker on the
-next stage and waits for its last copy on every other stage; four consumer warps take every stage, run an epilogue at the
+next stage and waits for its last copy on every other stage.  An item's
+first block is issued with an expected transfer but no arrival; the
+producer arrives on that stage only after the item's q is in the stage's
+meta, so the phase completes when both the copy has landed and q is there; four consumer warps take every stage, run an epilogue at the
 last block of an item (a barrier of the four warps, `ebar`, around a
 reduction array double-buffered by epilogue parity) and, for items of a
 sequence split over several CTAs, publish the item to the merger warp
@@ -41,9 +44,12 @@ class Barrier:
 
 
 class StepCTA:
-    def __init__(self, items, seed):
-        """items: list of (blocks, publishes) in the order the producer takes them."""
+    def __init__(self, items, seed, early_arrive=False):
+        """items: list of (blocks, publishes) in the order the producer takes them.
+        early_arrive: the first block's arrival comes with its copy (a wrong
+        protocol, for the negative control)."""
         self.rng = random.Random(seed)
+        self.early_arrive = early_arrive
         self.items = items
         self.bar = {}
         for s in range(STAGES):
@@ -61,6 +67,8 @@ class StepCTA:
         self.slot_unread = [False] * SLOTS
         self.merged = []
         self.tma = []
+        self.first = {}                       # stage -> [copy landed, producer arrived] of a first block
+        self.q_ready = [True] * STAGES        # the stage's meta holds its item's q (first blocks)
 
     def producer(self):
         issued = 0
@@ -71,7 +79,19 @@ class StepCTA:
                     yield ("wait", f"empty{s}", issued // STAGES - 1)
                 assert not self.stage_readers[s], f"stage {s} refilled while warps still read it"
                 self.stage[s] = None                          # meta written, copy in flight
+                if jj == 0:
+                    self.q_ready[s] = False
+                    if not self.early_arrive:
+                        self.first[s] = [False, False]        # expect_tx only: no arrival yet
                 self.tma.append((s, (it, jj)))
+                if jj == 0:
+                    yield ("work", None, None)                # the q/k work, with the copy in flight
+                    self.q_ready[s] = True                    # q into the stage's meta, then arrive
+                    if not self.early_arrive:
+                        self.first[s][1] = True
+                        if self.first[s][0]:
+                            del self.first[s]
+                            self.bar[f"full{s}"].arrive()
                 issued += 1
         s = issued % STAGES
         if issued >= STAGES:
@@ -95,6 +115,7 @@ class StepCTA:
             yield ("wait", f"full{s}", k // STAGES)
             got = self.stage[s]
             assert got is not None, f"warp {w} read stage {s} before its copy landed"
+            assert self.q_ready[s], f"warp {w} read stage {s} before its q was in the meta"
             if got == "end":
                 self.stage_readers[s].discard(w)
                 break
@@ -154,7 +175,8 @@ class StepCTA:
         pending = dict.fromkeys(roles)
         for _ in range(10 ** 6):
             choices = [("role", n) for n, g in roles.items()
-                       if g is not None and (pending[n] is None or self.bar[pending[n][1]].done > pending[n][2])]
+                       if g is not None and (pending[n] is None or pending[n][0] == "work"
+                                             or self.bar[pending[n][1]].done > pending[n][2])]
             choices += [("tma", i) for i in range(len(self.tma))]
             if not choices:
                 live = [n for n, g in roles.items() if g is not None]
@@ -165,16 +187,23 @@ class StepCTA:
                 s, what = self.tma.pop(arg)
                 self.stage[s] = what
                 self.stage_readers[s] = set(range(WARPS))
-                self.bar[f"full{s}"].arrive()
+                if s in self.first:                            # a first block: the arrival completes it
+                    self.first[s][0] = True
+                    if self.first[s][1]:
+                        del self.first[s]
+                        self.bar[f"full{s}"].arrive()
+                else:
+                    self.bar[f"full{s}"].arrive()
                 continue
             p = pending[arg]
-            if p is not None:
+            if p is not None and p[0] == "wait":
                 d = self.bar[p[1]].done
                 assert d <= p[2] + 1, f"{arg}: wait for completion {p[2]} of {p[1]} with {d} done: lapped"
             try:
                 nxt = next(roles[arg])
-                d = self.bar[nxt[1]].done
-                assert d >= nxt[2], f"{arg}: wait for completion {nxt[2]} of {nxt[1]} with {d} done: passes early"
+                if nxt[0] == "wait":
+                    d = self.bar[nxt[1]].done
+                    assert d >= nxt[2], f"{arg}: wait for completion {nxt[2]} of {nxt[1]} with {d} done: passes early"
                 pending[arg] = nxt
             except StopIteration:
                 roles[arg], pending[arg] = None, None
@@ -186,3 +215,17 @@ def test_step_barriers_hold_under_random_schedules(seed):
     rng = random.Random(seed)
     items = [(rng.randint(1, 6), rng.random() < 0.6) for _ in range(rng.randint(0, 12))]
     StepCTA(items, seed).run()
+
+
+def test_an_arrival_before_q_is_caught():
+    """Negative control: if the first block's phase completed with its copy
+    alone (q written afterwards), a consumer could read the meta before q;
+    the model reports it under some schedule."""
+    caught = 0
+    for seed in range(200):
+        try:
+            StepCTA([(2, False), (1, True), (3, False)], seed, early_arrive=True).run()
+        except AssertionError as e:
+            assert "before its q" in str(e), e
+            caught += 1
+    assert caught > 0
