@@ -888,6 +888,15 @@ __device__ __forceinline__ void consumers_sync(StepTail *tail, int lane, uint32_
 // Lengths of sequence b: past (RoPE position and, with B2_STORE_KV, the
 // append slot) and seq_len (tokens attended).  False for lengths the block
 // table cannot hold, or an append slot that is not the last attended token.
+// A 4-byte load from read-only memory, issued where it stands: the compiler
+// may not move it next to its first use, so a run of these is in flight
+// together.
+__device__ __forceinline__ int ld_nc_now(const int *p) {
+  int v;
+  asm volatile("ld.global.nc.b32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+
 __device__ __forceinline__ bool lengths_ok(const StepArgs &a, int past, int seq_len) {
   bool ok = past >= 0 && seq_len >= 0 && seq_len <= a.max_blocks * kBlock;
   if (a.mode & B2_STORE_KV) ok = ok && seq_len == past + 1;
@@ -972,21 +981,27 @@ __device__ __forceinline__ void step_producer(const StepArgs &a, StepTail *tail,
   int32_t *work_ctr = a.counters;
   const uint64_t policy = evict_first_policy();
   const int grp = lane >> 3, j = lane & 7;
-  const bool compact = a.batch <= kMaxCompactBatch;
+  // With one split per sequence the dense enumeration has no split past a
+  // sequence's end, so the compact one (and its prefix scan) is not needed.
+  const bool compact = a.batch <= kMaxCompactBatch && a.num_splits > 1;
   int total = a.total_items;
+  constexpr int kChunks = kMaxCompactBatch / 32;  // 32-sequence chunks of the largest compact batch
   if (compact) {
     // prefix[b + 1] = sum of splits of sequences 0..b.  Every lane loads the
     // lengths of its sequences (b = 32 k + lane) first, so that all the loads
     // are in flight together (one round trip for any batch), then the 32-wide
     // chunks are scanned in turn; CTA 0 also writes the empty results of the
-    // sequences with nothing to attend (they get no work item).
-    constexpr int kChunks = kMaxCompactBatch / 32;
+    // sequences with nothing to attend (they get no work item).  (Measured: a
+    // lane-owned run per lane and one scan of the run totals was ~1 us slower
+    // for batches of 8-64.)
     int pl[kChunks], sl[kChunks];
 #pragma unroll
     for (int k = 0; k < kChunks; ++k) {
-      const int b = 32 * k + lane;
-      pl[k] = b < a.batch ? __ldg(a.past_lens + b) : 0;
-      sl[k] = b < a.batch ? (a.seq_lens ? __ldg(a.seq_lens + b) : pl[k] + 1) : 0;
+      if (32 * k < a.batch) {
+        const int b = min(32 * k + lane, a.batch - 1);
+        pl[k] = ld_nc_now(a.past_lens + b);
+        sl[k] = a.seq_lens ? ld_nc_now(a.seq_lens + b) : 0;
+      }
     }
     int running = 0;
 #pragma unroll
@@ -996,6 +1011,7 @@ __device__ __forceinline__ void step_producer(const StepArgs &a, StepTail *tail,
       int ns = 0;
       bool empty = false;
       if (b < a.batch) {
+        if (!a.seq_lens) sl[k] = pl[k] + 1;
         if (lengths_ok(a, pl[k], sl[k])) {
           const int nblk = (sl[k] + kBlock - 1) / kBlock;
           ns = (nblk + a.blocks_per_split - 1) / a.blocks_per_split;
@@ -1026,16 +1042,26 @@ __device__ __forceinline__ void step_producer(const StepArgs &a, StepTail *tail,
     total = running * kHkv;
   } else if (blockIdx.x == 0) {
     // Sequences with nothing to attend (seq_lens[b] == 0) get no work item:
-    // write their empty result here.
-    for (int b0 = 0; b0 < a.batch; b0 += 32) {
-      const int b = b0 + lane;
-      int past = 0, seq_len = 1;
-      const bool empty = b < a.batch && step_lengths(a, b, past, seq_len) && seq_len == 0;
-      unsigned mask = __ballot_sync(0xffffffffu, empty);
-      while (mask) {
-        const int e = b0 + __ffs(mask) - 1;
-        mask &= mask - 1;
-        write_empty_result(a, e, lane);
+    // write their empty result here.  The lengths of 32 * kChunks sequences
+    // are loaded before any is examined.
+    for (int c0 = 0; c0 < a.batch; c0 += 32 * kChunks) {
+      int pl[kChunks], sl[kChunks];
+#pragma unroll
+      for (int k = 0; k < kChunks; ++k) {
+        const int b = min(c0 + 32 * k + lane, a.batch - 1);
+        pl[k] = ld_nc_now(a.past_lens + b);
+        sl[k] = a.seq_lens ? ld_nc_now(a.seq_lens + b) : pl[k] + 1;
+      }
+#pragma unroll
+      for (int k = 0; k < kChunks; ++k) {
+        const int b = c0 + 32 * k + lane;
+        const bool empty = b < a.batch && lengths_ok(a, pl[k], sl[k]) && sl[k] == 0;
+        unsigned mask = __ballot_sync(0xffffffffu, empty);
+        while (mask) {
+          const int e = c0 + 32 * k + __ffs(mask) - 1;
+          mask &= mask - 1;
+          write_empty_result(a, e, lane);
+        }
       }
     }
   }

@@ -267,6 +267,60 @@ def test_fused_step_large_batch_dense_items(cuda, bps):
         check_close(outs[1][i], ctx, f"seq {i} len {lengths[i] + 1} bps {bps}")
 
 
+@pytest.mark.parametrize("state", [False, True], ids=["context", "state"])
+@pytest.mark.parametrize("bps", [1, 8])
+def test_fused_step_empty_sequences(cuda, bps, state):
+    """Attention without the append (seq_lens given) where some sequences have
+    nothing to attend: their context is zero, or their fp32 state (-1e30, 0,
+    0); the others match the oracle's (m, l, o) over their first seq_lens
+    tokens with q at position past_lens.  The table is 5 blocks wide: bps 8
+    is one split per sequence (the dense walk of the work, no prefix scan),
+    bps 1 five splits (the compact walk through the prefix scan)."""
+    attn = _attn()
+    rope = load_pkg("rope")
+    w = orc.attention_weights(0)
+    lengths = [0, 5, 0, 64, 300, 0, 1, 129] * 5
+    b = len(lengths)
+    cache, hist = build_batch(lengths, cuda, seed=12, capacity=320)
+    assert cache.max_blocks == 5
+    raw = rand_qkv(b, 77)
+    past = torch.tensor([n + 3 for n in lengths], dtype=torch.int32, device=cuda)   # q's RoPE position
+    seq = torch.tensor(lengths, dtype=torch.int32, device=cuda)
+    splits = attn.num_splits_for(cache.max_blocks, bps)
+    kp, vp = cache.pool(0)
+    cos, sin = rope.rope_table(400, device=cuda)
+    out = torch.full((b, 16, 64), 7.0, dtype=torch.bfloat16, device=cuda)
+    sml = torch.full((b, 16, 2), 7.0, device=cuda)
+    so = torch.full((b, 16, 64), 7.0, device=cuda)
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    counters = torch.zeros(2 + 8 * b, dtype=torch.int32, device=cuda)
+    attn.decode_step(raw.to(cuda), past, k_pool=kp, v_pool=vp, block_tables=cache.block_tables(),
+                     blocks_per_split=bps, out=None if state else out,
+                     part_ml=torch.empty(b, splits, 16, 2, device=cuda),
+                     part_o=torch.empty(b, splits, 16, 64, device=cuda), counters=counters, dev_err=err,
+                     gamma_q=w["q_gamma"].to(cuda), gamma_k=w["k_gamma"].to(cuda), cos=cos, sin=sin,
+                     seq_lens=seq, state_ml=sml if state else None, state_o=so if state else None,
+                     mode=_lib().B2_NORM_QK | _lib().B2_ROPE_QK)
+    torch.cuda.synchronize()
+    assert err.item() == 0 and int(counters.abs().sum().item()) == 0
+    for i, n in enumerate(lengths):
+        q_raw, k_raw, _ = orc.split_qkv(raw[i:i + 1])
+        c, s = orc.rope_cos_sin([n + 3])
+        q, _ = orc.norm_rope_qk(q_raw, k_raw, w["q_gamma"], w["k_gamma"], c, s)
+        m, l, o = orc.partial_state(q[0], hist[i][0], hist[i][1])
+        if state:
+            if n == 0:
+                assert (sml[i, :, 0] == -1.0e30).all() and (sml[i, :, 1] == 0).all() and (so[i] == 0).all()
+                continue
+            # (m, l, o) equal the oracle's up to a common factor (the kernel's m is in log2 units)
+            assert torch.isfinite(sml[i]).all() and (sml[i, :, 1] > 0).all()
+            check_close(so[i].cpu() / sml[i, :, 1].cpu()[:, None], o / l[:, None], f"seq {i} len {n}: state")
+        elif n == 0:
+            assert (out[i] == 0).all(), f"seq {i}: empty context not zero"
+        else:
+            check_close(out[i], o / l[:, None], f"seq {i} len {n}")
+
+
 def test_fused_multi_step_decode_vs_oracle(cuda):
     """Eight consecutive decode steps crossing a block edge, each attending
     over the tokens appended by the previous steps."""

@@ -3,9 +3,13 @@ producer_load, step_producer, step_merger) distributes its work and merges
 splits across CTAs, checked under random interleavings of the CTAs.
 
 Work items are (sequence b, split, kv head).  Batches of up to 512 sequences
+with more than one split per sequence (block-table width > blocks per split)
 enumerate only real items through a prefix sum of splits per sequence
-(compact); larger batches walk the dense (split, sequence, head) space and
-skip splits past a sequence's end.  CTA i takes item i first, then items
+(compact); the others walk the dense (split, sequence, head) space and skip
+splits past a sequence's end (with one split per sequence there are none).
+The prefix sum is formed as the producer warp forms it: 32-sequence chunks
+in turn, each by a warp scan (shfl_up by 1, 2, 4, 8, 16) plus the running
+total of the chunks before it.  CTA i takes item i first, then items
 counter + gridDim from a global counter.  When a sequence has more than one
 split, the merger warp of the CTA that finishes a split counts the arrival
 for (b, kv head); the last of nsplit arrivals merges all splits and resets the
@@ -30,14 +34,32 @@ def nsplits(seq_len: int, bps: int) -> int:
     return math.ceil(math.ceil(seq_len / 64) / bps)
 
 
+def chunk_prefix(splits: list[int]) -> list[int]:
+    """step_producer's prefix: prefix[b] = splits of sequences 0..b-1, from a
+    Hillis-Steele warp scan of each 32-sequence chunk (lane = b % 32) and the
+    running total of the chunks before it (the scan's lane 31)."""
+    batch = len(splits)
+    prefix = [0] * (batch + 1)
+    running = 0
+    for c0 in range(0, batch, 32):
+        incl = [splits[c0 + lane] if c0 + lane < batch else 0 for lane in range(32)]
+        off = 1
+        while off < 32:
+            incl = [incl[i] + (incl[i - off] if i >= off else 0) for i in range(32)]
+            off *= 2
+        for lane in range(32):
+            if c0 + lane < batch:
+                prefix[c0 + lane + 1] = running + incl[lane]
+        running += incl[31]
+    return prefix
+
+
 def enumerate_items(lens: list[int], bps: int, max_blocks: int):
     """producer_load's decoding of work index w (returns total and a decoder)."""
     batch = len(lens)
-    compact = batch <= MAX_COMPACT
+    compact = batch <= MAX_COMPACT and math.ceil(max_blocks / bps) > 1
     if compact:
-        prefix = [0]
-        for n in lens:
-            prefix.append(prefix[-1] + nsplits(n, bps))
+        prefix = chunk_prefix([nsplits(n, bps) for n in lens])
         total = prefix[-1] * HKV
     else:
         total = math.ceil(max_blocks / bps) * batch * HKV
@@ -151,3 +173,30 @@ def test_equal_waves_leave_no_cta_idle(total, max_ctas):
     waves = math.ceil(total / ctas)
     assert 1 <= ctas <= total and ctas * (waves - 1) < total <= ctas * waves
     assert ctas <= (max_ctas if max_ctas > 0 else 444)
+
+
+@pytest.mark.parametrize("batch", [1, 2, 8, 31, 32, 33, 64, 100, 255, 256, 257, 511, 512])
+def test_chunk_scans_form_the_prefix_sum(batch):
+    rng = random.Random(batch)
+    splits = [rng.choice([0, 1, 2, 7, 64]) for _ in range(batch)]
+    want = [0]
+    for n in splits:
+        want.append(want[-1] + n)
+    assert chunk_prefix(splits) == want
+    assert (batch + 31) // 32 <= MAX_COMPACT // 32   # the kernel's per-lane length arrays hold the chunks
+
+
+@pytest.mark.parametrize("seed", range(6))
+def test_one_split_per_sequence_uses_the_dense_walk(seed):
+    """bps >= the table width: the dense walk is taken (no prefix scan) and,
+    with no split past any sequence's end, visits exactly the real items."""
+    rng = random.Random(200 + seed)
+    batch = rng.choice([1, 17, 256, 512])
+    lens = [rng.randint(1, 288) for _ in range(batch)]
+    max_blocks = max(math.ceil(n / 64) for n in lens)
+    bps = max_blocks + rng.randint(0, 2)
+    total, _ = enumerate_items(lens, bps, max_blocks)
+    assert total == batch * HKV
+    total, ctas, processed, merges, arrivals = simulate(lens, bps, max_blocks, 148, seed)
+    assert sorted(processed) == sorted((b, 0, h) for b in range(batch) for h in range(HKV))
+    assert merges == []
