@@ -1,9 +1,10 @@
 /*
  * C ABI of the LFM2.5 layer kernels around the attention hot path
- * (libb2attn.so), used by the whole-token decode runner: the residual add
- * fused with the RMSNorm that follows it, the SwiGLU gate of the feed-forward
- * block, and one decode step of the gated short convolution.  The GEMMs of
- * the layer stay library GEMMs (cuBLAS through the caller).
+ * (libb2attn.so), used by the whole-token decode runner: the layer's
+ * projection GEMMs on the tensor cores (with the SwiGLU gate fused into the
+ * stacked w1 / w3 product), the residual add fused with the RMSNorm that
+ * follows it, the SwiGLU gate on its own, one decode step of the gated short
+ * convolution, and the greedy argmax.
  *
  * Conventions as in b2_decode_attn.h: bf16 values as uint16_t bit patterns,
  * row-major, device pointers owned by the caller, a cudaStream_t as void *,
@@ -22,6 +23,42 @@
 #ifdef __cplusplus
 extern "C" {
 #endif
+
+/* b2_gemm epilogues */
+enum {
+  B2_GEMM_PLAIN = 0,  /* d = bf16(a . w^T) */
+  B2_GEMM_SWIGLU = 1  /* w = [w1; w3] (2n rows): d = bf16(bf16(silu(bf16(a . w1^T))) * bf16(a . w3^T)) */
+};
+
+/*
+ * d[m, n] = a[m, k] . w[n, k]^T (torch's Linear: y = x W^T) with bf16
+ * operands, fp32 accumulation on the tensor cores (tcgen05, TMEM
+ * accumulators) and a bf16 result rounded to nearest even; with
+ * B2_GEMM_SWIGLU, w holds the w1 rows and then the w3 rows (2n rows) and d
+ * receives the SwiGLU gate of the two products at the rounding points of
+ * b2_swiglu.  Row-major operands with row strides lda, ldw, ldd (elements):
+ * k % 64 == 0, lda and ldw >= k, ldd >= n, all three multiples of 8, the
+ * pointers 16-byte aligned.  tile_n (output columns per CTA: a multiple of
+ * 16 dividing n, <= 128, <= 64 with SwiGLU) and splits (K split over a
+ * cluster of that many CTAs: 1, 2, 4 or 8, dividing k / 64) are chosen by
+ * b2_gemm_plan when passed as 0.  Split-K partials are summed in a fixed
+ * order, so results are deterministic.  The kernel is launched with
+ * programmatic stream serialization: it starts fetching w before the
+ * previous kernel in the stream has finished and reads a only after it.
+ * A wait that gives up (b2_set_wait_limits) ORs B2_DEV_TIMEOUT into dev_err.
+ * Replaces the reference's bf16 GEMV (experiments/lfm25_bf16_gemv_kernel.py:19-60:
+ * fp32 accumulation, bf16 output; experiments/kernels/x8/x8_core.cc:166-177)
+ * for a batch of rows.
+ */
+int b2_gemm(const uint16_t *a, int64_t lda, const uint16_t *w, int64_t ldw, uint16_t *d, int64_t ldd,
+            int32_t m, int32_t n, int32_t k, int32_t mode, int32_t tile_n, int32_t splits, int32_t *dev_err,
+            void *stream);
+
+/*
+ * The tiling b2_gemm would use for an m x n x k product: tile_n and splits
+ * in/out (0 = choose), ctas (may be NULL) the launch's CTA count.
+ */
+int b2_gemm_plan(int32_t m, int32_t n, int32_t k, int32_t mode, int32_t *tile_n, int32_t *splits, int32_t *ctas);
 
 /*
  * sum = bf16(x + residual) (skipped when residual is NULL: sum = x), then

@@ -30,6 +30,9 @@ B2_TEST_STALL = 0x100         # b2_decode_step test mode: one warp's wait runs o
 B2_NOALLOC_MAX_PARTS = 1024   # batch * num_splits limit of b2_decode_attn_noalloc
 B2_XCHG_MAX_WORLD = 8         # ranks of b2_exchange_merge
 
+B2_GEMM_PLAIN = 0             # b2_gemm epilogues
+B2_GEMM_SWIGLU = 1
+
 DEV_ERR_NAMES = {
     B2_DEV_BAD_BLOCK: "block table entry outside the pool",
     B2_DEV_BAD_LENGTH: "length or position outside the block table",
@@ -137,6 +140,15 @@ SIGNATURES = {
     "b2_swiglu": (ctypes.c_int, [_p, _p, _i32, _i32, _p]),
     "b2_shortconv_step": (ctypes.c_int, [_p, _p, _p, _p, _i32, _i32, _p]),
     "b2_argmax_rows": (ctypes.c_int, [_p, _i32, _i32, _p, _p]),
+    "b2_gemm": (ctypes.c_int, [
+        _p, _i64, _p, _i64,  # a, lda, w, ldw
+        _p, _i64,            # d, ldd
+        _i32, _i32, _i32,    # m, n, k
+        _i32, _i32, _i32,    # mode, tile_n, splits
+        _p, _p,              # dev_err, stream
+    ]),
+    "b2_gemm_plan": (ctypes.c_int, [_i32, _i32, _i32, _i32, ctypes.POINTER(ctypes.c_int32),
+                                    ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_int32)]),
     "b2_merge_states": (ctypes.c_int, [
         _p, _i32, _i32,      # states, num_parts, batch
         _p, _p, _p, _p,      # out, state_ml, state_o, stream

@@ -15,7 +15,7 @@ PKG = pathlib.Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libb2attn.so"
-SOURCES = [CSRC / "b2_attn.cu", CSRC / "b2_block.cu"]
+SOURCES = [CSRC / "b2_attn.cu", CSRC / "b2_block.cu", CSRC / "b2_gemm.cu"]
 HEADERS = [ROOT / "include" / "b2_decode_attn.h", ROOT / "include" / "b2_block.h", CSRC / "b2_internal.h"]
 
 NVCC_FLAGS = [

@@ -2244,6 +2244,7 @@ int sm_count() {
 // ------------------------------------------------------------------ C ABI
 
 int b2_record_error(int code, const char *message) { return fail(code, "%s", message); }
+uint64_t b2_wait_limit_ns() { return wait_limit(); }
 int b2_clear_error() { return ok(); }
 
 extern "C" int b2_version(void) { return 100; }

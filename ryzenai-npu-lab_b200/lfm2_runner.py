@@ -9,10 +9,13 @@ and the head) is one CUDA-graph replay.
 
 The attention layers' hot path — q/k RMSNorm + RoPE + paged KV append +
 split-KV attention — runs in libb2attn.so's fused decode step.  Around it
-(fused_glue=True, the default) the layer's residual adds + RMSNorms, the
-SwiGLU gate and the short-convolution step are libb2attn.so kernels too
-(b2_add_rmsnorm, b2_swiglu, b2_shortconv_step), between cuBLAS GEMMs (w1 and
-w3 stacked into one); fused_glue=False runs that glue as plain torch ops.
+(fused_glue=True, the default) the layer's projections are libb2attn.so's
+tensor-core GEMM (b2_gemm; w1 and w3 stacked into one product with the
+SwiGLU gate as its epilogue), and the residual adds + RMSNorms and the
+short-convolution step are libb2attn.so kernels too (b2_add_rmsnorm,
+b2_shortconv_step); own_gemm=False runs the projections as cuBLAS GEMMs
+(torch.matmul) with b2_swiglu after the stacked w1/w3 product, and
+fused_glue=False runs all of the glue as plain torch ops.
 Both follow the model definition the reference's CPU path uses
 (transformers modeling_lfm2.py: Lfm2RMSNorm 59-64, Lfm2MLP 135-152,
 Lfm2ShortConv.slow_forward 356-387, Lfm2DecoderLayer.forward 413-442,
@@ -28,7 +31,7 @@ from dataclasses import dataclass, field
 
 import torch
 
-from . import block
+from . import _lib, block
 from .attention import PagedDecodeAttention
 from .paged_cache import PagedKVCache, blocks_for
 
@@ -69,7 +72,7 @@ class LFM2DecodeRunner:
 
     def __init__(self, state_dict: dict, config: LFM2Config = LFM2Config(), *, max_batch: int,
                  max_context: int, device: torch.device | str = "cuda", use_graph: bool = True,
-                 blocks_per_split: int | None = None, fused_glue: bool = True):
+                 blocks_per_split: int | None = None, fused_glue: bool = True, own_gemm: bool = True):
         self.cfg = config
         self.device = torch.device(device)
         self.max_batch = max_batch
@@ -126,6 +129,8 @@ class LFM2DecodeRunner:
         self.use_graph = use_graph and self.device.type == "cuda"
         self._graph = None
         self.fused_glue = fused_glue
+        self.own_gemm = fused_glue and own_gemm
+        self.gemm_err = torch.zeros(1, dtype=torch.int32, device=dev)
         if fused_glue:
             ffn = self.layers[0]["w1"].shape[0]
             hd = config.hidden
@@ -146,11 +151,18 @@ class LFM2DecodeRunner:
         else:
             self._token_torch()
 
+    def _mm(self, a: torch.Tensor, w: torch.Tensor, out: torch.Tensor) -> None:
+        """out = a @ w.T: b2_gemm, or cuBLAS with own_gemm=False."""
+        if self.own_gemm:
+            block.gemm(a, w, out=out, dev_err=self.gemm_err)
+        else:
+            torch.matmul(a, w.t(), out=out)
+
     def _token_fused(self) -> None:
         """The token with the layer glue in libb2attn.so: per layer two GEMMs
         around the mixer (attention step or short-convolution step), then
-        residual + RMSNorm, the stacked w1/w3 GEMM, SwiGLU, w2 GEMM; each
-        residual add is fused into the RMSNorm that follows it."""
+        residual + RMSNorm, the stacked w1/w3 GEMM with the SwiGLU gate, the w2
+        GEMM; each residual add is fused into the RMSNorm that follows it."""
         cfg, b = self.cfg, self.max_batch
         h, x, o = self.h, self.x, self.o
         torch.index_select(self.embed, 0, self.ids, out=h)
@@ -159,20 +171,23 @@ class LFM2DecodeRunner:
         n = len(self.layers)
         for i, lw in enumerate(self.layers):
             if lw["kind"] == "attention":
-                torch.matmul(x, lw["qkv"].t(), out=self.qkv)                     # [B, 2048]: q | k | v
+                self._mm(x, lw["qkv"], self.qkv)                                    # [B, 2048]: q | k | v
                 ctx = self.attn[lw["att"]].step(lw["att"], self.qkv, self.past, self.seq, self.tables)
-                torch.matmul(ctx.reshape(b, cfg.heads * cfg.head_dim), lw["out"].t(), out=o)
+                self._mm(ctx.reshape(b, cfg.heads * cfg.head_dim), lw["out"], o)
             else:
-                torch.matmul(x, lw["in"].t(), out=self.bcx)                      # [B, 3 * hidden]: B | C | x
+                self._mm(x, lw["in"], self.bcx)                                     # [B, 3 * hidden]: B | C | x
                 block.shortconv_step(self.bcx, self.conv_state[lw["conv_id"]], lw["conv"], out=self.y)
-                torch.matmul(self.y, lw["out"].t(), out=o)
+                self._mm(self.y, lw["out"], o)
             block.add_rmsnorm(o, h, lw["ffn_norm"], cfg.eps, out=x, sum_out=h)  # h += mixer; x = ffn_norm(h)
-            torch.matmul(x, lw["w13"].t(), out=self.gu)
-            block.swiglu(self.gu, out=self.m)
-            torch.matmul(self.m, lw["w2"].t(), out=o)
+            if self.own_gemm:
+                block.gemm(x, lw["w13"], out=self.m, dev_err=self.gemm_err, swiglu=True)
+            else:
+                torch.matmul(x, lw["w13"].t(), out=self.gu)
+                block.swiglu(self.gu, out=self.m)
+            self._mm(self.m, lw["w2"], o)
             nxt = self.layers[i + 1]["op_norm"] if i + 1 < n else self.final_norm
             block.add_rmsnorm(o, h, nxt, cfg.eps, out=x, sum_out=h)             # h += ffn; x = next norm(h)
-        torch.matmul(x, self.head.t(), out=self.logits)
+        self._mm(x, self.head, self.logits)
         block.argmax_rows(self.logits, out=self.next_ids)
         self.past.add_(1)
 
@@ -273,3 +288,7 @@ class LFM2DecodeRunner:
     def check(self) -> None:
         for a in self.attn:
             a.check()
+        word = int(self.gemm_err.item())
+        if word:
+            self.gemm_err.zero_()
+            raise RuntimeError("b2_gemm device error: " + "; ".join(_lib.decode_dev_err(word)))

@@ -47,9 +47,9 @@ def _weights(f):
     return sd
 
 
-@pytest.mark.parametrize("fused_glue", [True, False], ids=["kernels", "torch_glue"])
+@pytest.mark.parametrize("glue", ["kernels", "kernels_cublas", "torch_glue"])
 @pytest.mark.parametrize("use_graph", [True, False], ids=["graph", "eager"])
-def test_greedy_teacher_forced_matches_reference(cuda, use_graph, fused_glue):
+def test_greedy_teacher_forced_matches_reference(cuda, use_graph, glue):
     """Teacher-forced (the reference's inputs at every step): the logits at the
     reference's top-8 within TIE_ULPS bf16 ulps of the reference's; the argmax
     equals the reference's except where its top logits are within TIE_ULPS
@@ -60,7 +60,8 @@ def test_greedy_teacher_forced_matches_reference(cuda, use_graph, fused_glue):
     top_v, top_i = f["top_values"], f["top_indices"]
     b, steps = inputs.shape
     runner = runner_mod.LFM2DecodeRunner(_weights(f), max_batch=b, max_context=64, device=cuda,
-                                         use_graph=use_graph, fused_glue=fused_glue)
+                                         use_graph=use_graph, fused_glue=glue != "torch_glue",
+                                         own_gemm=glue == "kernels")
     ulps, flips = [], []
     for t in range(steps):
         nxt = runner.step(torch.from_numpy(inputs[:, t])).cpu().numpy()
@@ -128,16 +129,19 @@ def test_generate_and_reset(cuda):
         runner.step(torch.zeros(3, dtype=torch.long))
 
 
-def test_kernel_glue_matches_torch_glue(cuda):
-    """The same model, token by token, with the layer glue in libb2attn.so and
-    as torch ops: logits within a few bf16 ulps of their scale."""
+@pytest.mark.parametrize("own_gemm", [True, False], ids=["b2_gemm", "cublas"])
+def test_kernel_glue_matches_torch_glue(cuda, own_gemm):
+    """The same model, token by token, with the layer glue (and the
+    projections, with b2_gemm) in libb2attn.so and as torch ops: logits within
+    a few bf16 ulps of their scale."""
     runner_mod = load_pkg("lfm2_runner")
     f = dict(np.load(GOLDEN))
     sd = _weights(f)
     ids = torch.from_numpy(f["inputs"])
     runs = []
     for fused in (True, False):
-        r = runner_mod.LFM2DecodeRunner(sd, max_batch=ids.shape[0], max_context=40, device=cuda, fused_glue=fused)
+        r = runner_mod.LFM2DecodeRunner(sd, max_batch=ids.shape[0], max_context=40, device=cuda, fused_glue=fused,
+                                        own_gemm=own_gemm)
         logits = []
         for t in range(12):
             r.step(ids[:, t])
