@@ -83,8 +83,8 @@ def parse():
     p.add_argument("--context", type=int, default=131072, help="c4: cached tokens of the sequence")
     p.add_argument("--torch-glue", action="store_true",
                    help="c5: run the layer glue (norms, SwiGLU, short conv) as torch ops")
-    p.add_argument("--cublas-gemm", action="store_true",
-                   help="c5: the layer projections as cuBLAS GEMMs instead of b2_gemm")
+    p.add_argument("--b2-gemm", action="store_true",
+                   help="c5: the layer projections on b2_gemm (tcgen05) instead of cuBLAS")
     p.add_argument("--exchange", choices=["auto", "p2p", "collective"], default="auto",
                    help="c4: how the ranks' partial states are merged")
     p.add_argument("--scaling", choices=["strong", "weak"], default="strong",
@@ -901,7 +901,8 @@ def run_c5(args):
     batch, prompt_len, new = 256, 32, 256
     sd = orc.lfm2_model_weights(args.seed)
     runner = runner_mod.LFM2DecodeRunner(sd, max_batch=batch, max_context=prompt_len + new + 1, device=dev,
-                                         fused_glue=not args.torch_glue, own_gemm=not args.cublas_gemm)
+                                         fused_glue=not args.torch_glue,
+                                         own_gemm=args.b2_gemm and not args.torch_glue)
     del sd
     g = torch.Generator().manual_seed(args.seed * 1000 + rank)
     prompts = torch.randint(0, 65536, (batch, prompt_len), generator=g)
@@ -925,8 +926,8 @@ def run_c5(args):
         "config": {"workload": "C5 end-to-end greedy decode, LFM2.5-230M-shaped random-init model, "
                                "256 prompts x 32 ids, 256 new tokens, paged KV, CUDA graph per token",
                    "layer_glue": "torch ops" if args.torch_glue else "libb2attn kernels",
-                   "projections": "cuBLAS (torch.matmul)" if args.torch_glue or args.cublas_gemm
-                   else "b2_gemm (tcgen05, SwiGLU fused into w1/w3)",
+                   "projections": "b2_gemm (tcgen05, SwiGLU fused into w1/w3)" if args.b2_gemm and not args.torch_glue
+                   else "cuBLAS (torch.matmul)",
                    "global_batch": batch * world, "prompt": prompt_len, "new_tokens": new,
                    "parallelism": f"replicas x{world}"},
         "generated_shape": list(out.shape), "clocks": clocks.summary(),

@@ -25,6 +25,12 @@ constexpr int kNormMaxChunks = 4;  // 8-value chunks per thread: width <= 128 * 
 
 __device__ __forceinline__ float bf2f(uint32_t bits16) { return __uint_as_float(bits16 << 16); }
 
+// Let a kernel launched after this one with programmatic stream serialization
+// (b2_gemm) start its own set-up and its weight copies now; it reads this
+// kernel's output only after griddepcontrol.wait, which waits for this grid
+// to complete.
+__device__ __forceinline__ void allow_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ uint32_t f2bf(float x) {
   return static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(x)));
 }
@@ -106,6 +112,7 @@ __global__ void __launch_bounds__(kNormThreads)
   __shared__ float sq[kNormThreads * 8 * kNormMaxChunks];
   __shared__ float chains[kNormThreads * 8 * kNormMaxChunks / 32 / 16 * 32 + 32];
   __shared__ float red[kNormThreads / 32];
+  allow_dependents();
   const int64_t row = blockIdx.x;
   const int chunks = width / 8;
   const bool torch_order = width % 32 == 0;
@@ -160,6 +167,7 @@ __global__ void __launch_bounds__(kNormThreads)
 
 // silu(g) = g / (1 + e^-g) in fp32, rounded to bf16 as the bf16 silu tensor is
 __global__ void swiglu_kernel(const uint16_t *__restrict__ gu, uint16_t *__restrict__ out, int rows, int ffn) {
+  allow_dependents();
   const int chunks = ffn / 8;
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= static_cast<int64_t>(rows) * chunks) return;
@@ -177,6 +185,7 @@ __global__ void swiglu_kernel(const uint16_t *__restrict__ gu, uint16_t *__restr
 __global__ void shortconv_step_kernel(const uint16_t *__restrict__ bcx, uint16_t *__restrict__ state,
                                       const uint16_t *__restrict__ w, uint16_t *__restrict__ out, int rows,
                                       int hidden) {
+  allow_dependents();
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t r = blockIdx.y;
   if (c >= hidden) return;
@@ -209,6 +218,7 @@ __global__ void __launch_bounds__(kArgmaxThreads)
     argmax_rows_kernel(const uint16_t *__restrict__ logits, int cols, int64_t *__restrict__ out) {
   __shared__ float sv[kArgmaxThreads / 32];
   __shared__ int si[kArgmaxThreads / 32];
+  allow_dependents();
   const int64_t row = blockIdx.x;
   const uint4 *p = reinterpret_cast<const uint4 *>(logits + row * cols);
   float bv = -INFINITY;

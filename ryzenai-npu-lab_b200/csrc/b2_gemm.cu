@@ -12,11 +12,14 @@
 // into the TMEM accumulator and frees each stage with tcgen05.commit.  The
 // weights do not depend on the previous kernel, so the first stages' W copies
 // are issued before griddepcontrol.wait (programmatic dependent launch): they
-// overlap the tail of the kernel that produces A.  Split-K runs the K slices
-// of one tile as a thread-block cluster: every CTA stages its fp32 partial tile
-// in its own shared memory, and CTA r of the cluster sums rows [r * 128 /
-// splits, ...) of all partials over distributed shared memory in a fixed
-// order (deterministic), applies the epilogue and stores bf16 rows.  No TMA
+// overlap the tail of the kernel that produces A (the layer kernels of
+// b2_block.cu allow it from their first instruction).  Without a K split each
+// thread converts its TMEM row and stores it.  Split-K runs the K slices of
+// one tile as a thread-block cluster: every CTA stages its fp32 partial tile
+// in its own shared memory and sends rows [r * 128 / splits, ...) to cluster
+// CTA r with a bulk shared-to-shared copy (point to point, completing on the
+// receiver's mbarrier); CTA r sums the slices of its rows in K-slice order
+// (deterministic), applies the epilogue and stores bf16 rows.  No TMA
 // multicast: every CTA loads its own tiles.
 //
 // The decode layer's projections are weight-streaming products (m = batch);
@@ -46,10 +49,11 @@ constexpr int kThreads = 128;  // 4 warps: producer lane, MMA lane, then all fou
 constexpr int kTileM = 128;    // UMMA M (one TMEM lane per tile row)
 constexpr int kChunkK = 64;    // K elements per stage: one 128-byte swizzle row
 constexpr uint32_t kATileBytes = kTileM * kChunkK * 2;  // 16 KiB
-constexpr int kMaxStages = 8;
+constexpr int kMaxStages = 16;
 constexpr int kMaxSplits = 8;      // portable cluster size
 constexpr int kMaxAccCols = 128;   // accumulator columns (tile_n, or 2 x tile_n for SwiGLU)
-constexpr int kSmemBudget = 112 * 1024;  // two CTAs per SM
+constexpr int kSmemBudget = 112 * 1024;      // two CTAs per SM
+constexpr int kSmemBudgetOne = 200 * 1024;   // one CTA per SM (grids of at most one CTA per SM)
 constexpr uint64_t kDrainNs = 2000000000ull;
 
 struct GemmArgs {
@@ -65,6 +69,7 @@ struct GemmBars {
   uint64_t full[kMaxStages];
   uint64_t empty[kMaxStages];
   uint64_t done;
+  uint64_t recv;  // split K: the other K slices' rows of this CTA have landed
   uint32_t tmem;
 };
 
@@ -156,14 +161,15 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t r[16]) {
+__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t r[16]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
         "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
@@ -171,28 +177,30 @@ __device__ __forceinline__ uint32_t cluster_rank() {
   return r;
 }
 
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 }
 
-// float4 at a shared::cta address of cluster CTA `rank`
-__device__ __forceinline__ float4 ld_peer4(uint32_t addr, uint32_t rank) {
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+
+// shared::cluster address of the same shared-memory offset in cluster CTA `rank`
+__device__ __forceinline__ uint32_t peer_addr(uint32_t addr, uint32_t rank) {
   uint32_t remote;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(addr), "r"(rank));
-  float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(remote)
-               : "memory");
-  return v;
+  return remote;
 }
 
-__device__ __forceinline__ float4 ld_own4(uint32_t addr) {
-  float4 v;
-  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr)
+// Bulk copy of `bytes` (a multiple of 16) from this CTA's shared memory into
+// another cluster CTA's, completing on that CTA's mbarrier (point to point).
+__device__ __forceinline__ void push_to_peer(uint32_t dst_cluster, uint32_t src, uint32_t bytes,
+                                             uint32_t bar_cluster) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   dst_cluster),
+               "r"(src), "r"(bytes), "r"(bar_cluster)
                : "memory");
-  return v;
 }
+
+__device__ __forceinline__ float4 ld_smem4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
 
 // fp32 -> bf16 -> fp32, round to nearest even (torch's rounding)
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
@@ -218,7 +226,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int cols = acc_cols(g.tile_n, g.mode);
   const uint32_t sbytes = stage_bytes(cols);
   const int ring = g.stages * static_cast<int>(sbytes);
-  GemmBars *bars = reinterpret_cast<GemmBars *>(smem + (ring > part_bytes(cols) ? ring : part_bytes(cols)));
+  // [ring (reused for this CTA's fp32 partial tile) | split K: receive area,
+  // the same [128][cols + 4] layout, rows r * R.. from K slice r | barriers]
+  const int body = ring > part_bytes(cols) ? ring : part_bytes(cols);
+  float *recv = reinterpret_cast<float *>(smem + body);
+  GemmBars *bars = reinterpret_cast<GemmBars *>(smem + body + (g.splits > 1 ? part_bytes(cols) : 0));
+  const int rows_per_split = kTileM / g.splits;
+  const uint32_t slice_bytes = static_cast<uint32_t>(rows_per_split * (cols + 4) * 4);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t split = g.splits > 1 ? cluster_rank() : 0;
   const int m0 = static_cast<int>(blockIdx.x / g.splits) * kTileM;
@@ -227,11 +241,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t ncols = tmem_cols(cols);
 
   if (threadIdx.x == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_w)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_a)) : "memory");
     for (int s = 0; s < g.stages; ++s) {
       mbar_init(smem_u32(&bars->full[s]), 1);
       mbar_init(smem_u32(&bars->empty[s]), 1);
     }
     mbar_init(smem_u32(&bars->done), 1);
+    if (g.splits > 1) {
+      mbar_init(smem_u32(&bars->recv), 1);
+      // the other splits' slices of this CTA's rows, pushed by their CTAs
+      mbar_arrive_expect_tx(smem_u32(&bars->recv), static_cast<uint32_t>(g.splits - 1) * slice_bytes);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -243,6 +264,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = bars->tmem;
+  // phase 1 of the cluster barrier: this CTA's receive barrier is set up (the
+  // wait comes just before the first push, long after every CTA arrived)
+  if (g.splits > 1) cluster_arrive_relaxed();
 
   if (warp == 0 && lane == 0) {
     // producer: the first stages' weight tiles go out before the wait for the
@@ -303,64 +327,137 @@ __global__ void __launch_bounds__(kThreads, 1)
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
-  // epilogue: TMEM lane = tile row = threadIdx.x; the fp32 partial tile goes
-  // to this CTA's shared memory (the ring is idle once the products are done)
+  // epilogue: TMEM lane = tile row = threadIdx.x
   if (!mbar_wait(smem_u32(&bars->done), 0, kDrainNs)) atomicOr(g.err, B2_DEV_TIMEOUT);
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+  const int grow = m0 + static_cast<int>(threadIdx.x);
+
+  if (g.splits == 1) {
+    // one K slice: each thread converts its own row and stores it, 16
+    // columns (32 bytes) at a time; no shared memory, no barrier
+    uint16_t *drow = g.d + static_cast<int64_t>(grow) * g.ldd + n0;
+    for (int c0 = 0; c0 < g.tile_n; c0 += 16) {
+      uint32_t r[16], ru[16];
+      tmem_ld16_nowait(taddr + c0, r);
+      if (swiglu) tmem_ld16_nowait(taddr + g.tile_n + c0, ru);
+      tmem_wait_ld();
+      uint32_t w[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        float lo = __uint_as_float(r[2 * q]), hi = __uint_as_float(r[2 * q + 1]);
+        if (swiglu) {
+          lo = swiglu1(lo, __uint_as_float(ru[2 * q]));
+          hi = swiglu1(hi, __uint_as_float(ru[2 * q + 1]));
+        }
+        w[q] = bf16_pair(lo, hi);
+      }
+      if (grow < g.m) {
+        reinterpret_cast<uint4 *>(drow + c0)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        reinterpret_cast<uint4 *>(drow + c0)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+      }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 1) {
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols));
+    }
+    return;
+  }
+
+  // split K: the fp32 partial tile goes to this CTA's shared memory (the ring
+  // is idle once the products are done), padded rows of cols + 4 floats
   float *part = reinterpret_cast<float *>(smem);
   const int pstride = cols + 4;
   {
-    const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
     float4 *row = reinterpret_cast<float4 *>(part + threadIdx.x * pstride);
-    for (int c0 = 0; c0 < cols; c0 += 16) {
-      uint32_t r[16];
-      tmem_ld16(taddr + c0, r);
+    for (int c0 = 0; c0 < cols; c0 += 32) {
+      uint32_t r[32];
+      tmem_ld16_nowait(taddr + c0, r);
+      if (c0 + 16 < cols) tmem_ld16_nowait(taddr + c0 + 16, r + 16);
+      tmem_wait_ld();
 #pragma unroll
-      for (int q = 0; q < 4; ++q)
-        row[c0 / 4 + q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
-                                      __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
+      for (int q = 0; q < 8; ++q)
+        if (c0 + 4 * q < cols)
+          row[c0 / 4 + q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                                        __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
     }
   }
+  // the partial tile is read next by the bulk-copy (async) proxy
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-  if (g.splits > 1) cluster_sync(); else __syncthreads();
+  __syncthreads();
   if (warp == 1) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols));
   }
+  cluster_wait();  // phase 1: every CTA's receive barrier is initialised
+  const int rows = rows_per_split;
+  if (threadIdx.x == 0) {
+    // rows [q * R, q * R + R) of this partial go to CTA q, into its slot `split`
+    for (int q = 0; q < g.splits; ++q) {
+      if (q == static_cast<int>(split)) continue;
+      push_to_peer(peer_addr(smem_u32(recv + split * rows * pstride), q), smem_u32(part + q * rows * pstride),
+                   slice_bytes, peer_addr(smem_u32(&bars->recv), q));
+    }
+  }
+  if (!mbar_wait(smem_u32(&bars->recv), 0, g.wait_ns)) atomicOr(g.err, B2_DEV_TIMEOUT);
+  // phase 2: all pushes into this CTA have landed; when every CTA has arrived,
+  // every push out of this CTA has been read and its partial may go
+  cluster_arrive_relaxed();
 
-  // rows [split * R, split * R + R) of the tile: the splits' partials summed in
-  // cluster-rank order, then the epilogue; 4 output columns per thread and step
-  const int rows = kTileM / g.splits;
-  const int quads = g.tile_n / 4;
-  for (int i = threadIdx.x; i < rows * quads; i += kThreads) {
-    const int r = static_cast<int>(split) * rows + i / quads;
-    const int c4 = i - (i / quads) * quads;
-    const uint32_t off = smem_u32(part + r * pstride + 4 * c4);
-    const uint32_t off_u = off + 4u * g.tile_n;
-    float4 s = g.splits > 1 ? ld_peer4(off, 0) : ld_own4(off);
-    float4 u = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (swiglu) u = g.splits > 1 ? ld_peer4(off_u, 0) : ld_own4(off_u);
-    for (int q = 1; q < g.splits; ++q) {
-      const float4 v = ld_peer4(off, q);
-      s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
-      if (swiglu) {
-        const float4 w = ld_peer4(off_u, q);
-        u.x += w.x; u.y += w.y; u.z += w.z; u.w += w.w;
+  // rows [split * R, split * R + R) of the tile: the slices summed in K-slice
+  // order (this CTA's own slice from its partial tile), then the epilogue.
+  // Thread t keeps column quad t % quads and takes rows t / quads + j *
+  // (128 / quads): four rows per round, their loads of a slice issued together.
+  const int quads = g.tile_n / 4;                  // a power of two (tile_n is 16, 32, 64 or 128)
+  const int qshift = __ffs(quads) - 1;
+  const int step = kThreads >> qshift;             // rows per pass of the CTA
+  const int c = 4 * (static_cast<int>(threadIdx.x) & (quads - 1));
+  const int lr0 = static_cast<int>(threadIdx.x) >> qshift;
+  for (int base = lr0; base < rows; base += 4 * step) {
+    float4 sm[4], u[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) sm[e] = u[e] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int q = 0; q < g.splits; ++q) {
+      const float *slice = q == static_cast<int>(split) ? part + split * rows * pstride : recv + q * rows * pstride;
+      float4 v[4], w[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int lr = base + e * step;
+        if (lr < rows) {
+          v[e] = ld_smem4(slice + lr * pstride + c);
+          if (swiglu) w[e] = ld_smem4(slice + lr * pstride + g.tile_n + c);
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        if (base + e * step < rows) {
+          sm[e].x += v[e].x; sm[e].y += v[e].y; sm[e].z += v[e].z; sm[e].w += v[e].w;
+          if (swiglu) { u[e].x += w[e].x; u[e].y += w[e].y; u[e].z += w[e].z; u[e].w += w[e].w; }
+        }
       }
     }
-    if (swiglu) {
-      s.x = swiglu1(s.x, u.x);
-      s.y = swiglu1(s.y, u.y);
-      s.z = swiglu1(s.z, u.z);
-      s.w = swiglu1(s.w, u.w);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int lr = base + e * step;
+      if (lr >= rows) break;
+      float4 o = sm[e];
+      if (swiglu) {
+        o.x = swiglu1(o.x, u[e].x);
+        o.y = swiglu1(o.y, u[e].y);
+        o.z = swiglu1(o.z, u[e].z);
+        o.w = swiglu1(o.w, u[e].w);
+      }
+      const int gr = m0 + static_cast<int>(split) * rows + lr;
+      if (gr < g.m)
+        *reinterpret_cast<uint2 *>(g.d + static_cast<int64_t>(gr) * g.ldd + n0 + c) =
+            make_uint2(bf16_pair(o.x, o.y), bf16_pair(o.z, o.w));
     }
-    const int gr = m0 + r;
-    if (gr < g.m)
-      *reinterpret_cast<uint2 *>(g.d + static_cast<int64_t>(gr) * g.ldd + n0 + 4 * c4) =
-          make_uint2(bf16_pair(s.x, s.y), bf16_pair(s.z, s.w));
   }
   __syncwarp();
-  if (g.splits > 1) cluster_sync();  // the other CTAs read this CTA's partial until here
+  cluster_wait();  // phase 2
 }
 
 // ------------------------------------------------------------------ host side
@@ -405,7 +502,7 @@ bool smem_ready() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return false;
   if (!done[dev]) {
-    if (cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget + 2048) !=
+    if (cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudgetOne + 2048) !=
         cudaSuccess)
       return false;
     done[dev] = true;
@@ -419,46 +516,56 @@ struct Plan {
 
 // Tile width, K splits and ring depth for an m x n x k product.  Wider tiles
 // read A fewer times (A is re-read once per column tile); K splits keep about
-// one CTA per SM busy when the tiles are few.
+// one CTA per SM busy when the tiles are few.  A grid that leaves every CTA an
+// SM of its own gets a deeper ring (the loop is bound by in-flight bytes /
+// latency); split K also needs a receive area for the other slices' rows.
 bool plan_gemm(int m, int n, int k, int mode, int tile_n, int splits, int sms, Plan *p) {
   const int mt = (m + kTileM - 1) / kTileM;
   const int kch = k / kChunkK;
   const int max_tile = mode == B2_GEMM_SWIGLU ? kMaxAccCols / 2 : kMaxAccCols;
   if (tile_n <= 0) {
     tile_n = 0;
-    const int cands[4] = {128, 64, 32, 16};
+    // 128 columns when that alone fills the GPU twice (the vocabulary head);
+    // else 32 (measured on the decode layer's shapes at m = 256: 32 beat 64
+    // in four of five, with split K filling the SMs), else what divides n
+    const int cands[4] = {128, 32, 64, 16};
     for (int t : cands) {
       if (t > max_tile || n % t) continue;
-      if (tile_n == 0) tile_n = t;  // the widest that divides n
-      if (t == 128 && static_cast<int64_t>(mt) * (n / t) >= 2 * sms) { tile_n = t; break; }
-      if (t <= 64) { tile_n = t; break; }
+      if (t == 128 && static_cast<int64_t>(mt) * (n / t) < 2 * sms) continue;
+      tile_n = t;
+      break;
     }
     if (tile_n == 0) return false;
   }
   if (tile_n % 16 || tile_n > max_tile || n % tile_n) return false;
   const int64_t tiles = static_cast<int64_t>(mt) * (n / tile_n);
-  if (splits <= 0) {
-    splits = 1;
-    while (splits * 2 <= kMaxSplits && tiles * splits * 2 <= (3 * sms) / 2 && kch % (splits * 2) == 0 &&
-           kch / (splits * 2) >= 2)
-      splits *= 2;
-  }
-  if (splits < 1 || splits > kMaxSplits || (splits & (splits - 1)) || kch % splits) return false;
   const int cols = acc_cols(tile_n, mode);
-  const int chunks = kch / splits;
-  int stages = (kSmemBudget - static_cast<int>(sizeof(GemmBars))) / static_cast<int>(stage_bytes(cols));
-  if (stages > kMaxStages) stages = kMaxStages;
-  if (stages > chunks) stages = chunks;
-  if (stages < 1) return false;
-  const int ring = stages * static_cast<int>(stage_bytes(cols));
-  const int body = ring > part_bytes(cols) ? ring : part_bytes(cols);
-  p->tile_n = tile_n;
-  p->splits = splits;
-  p->chunks = chunks;
-  p->stages = stages;
-  p->smem = body + static_cast<int>(sizeof(GemmBars)) + 1024;
-  p->ctas = static_cast<int>(tiles * splits);
-  return p->smem <= kSmemBudget + 2048;
+  auto fit = [&](int sp, Plan *out) {
+    if (sp < 1 || sp > kMaxSplits || (sp & (sp - 1)) || kch % sp) return false;
+    const int chunks = kch / sp;
+    const int budget = tiles * sp <= sms ? kSmemBudgetOne : kSmemBudget;
+    const int recv = sp > 1 ? part_bytes(cols) : 0;
+    int stages = (budget - recv - static_cast<int>(sizeof(GemmBars))) / static_cast<int>(stage_bytes(cols));
+    if (stages > kMaxStages) stages = kMaxStages;
+    if (stages > chunks) stages = chunks;
+    if (stages < 1) return false;
+    const int ring = stages * static_cast<int>(stage_bytes(cols));
+    const int body = ring > part_bytes(cols) ? ring : part_bytes(cols);
+    out->tile_n = tile_n;
+    out->splits = sp;
+    out->chunks = chunks;
+    out->stages = stages;
+    out->smem = body + recv + static_cast<int>(sizeof(GemmBars)) + 1024;
+    out->ctas = static_cast<int>(tiles * sp);
+    return out->smem <= budget + 2048;
+  };
+  if (splits > 0) return fit(splits, p);
+  int sp = 1;
+  while (sp * 2 <= kMaxSplits && tiles * sp * 2 <= 2 * sms && kch % (sp * 2) == 0 && kch / (sp * 2) >= 2)
+    sp *= 2;
+  for (; sp >= 1; sp /= 2)
+    if (fit(sp, p)) return true;
+  return false;
 }
 
 int launch_error(const char *what) {

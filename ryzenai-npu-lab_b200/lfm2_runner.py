@@ -9,13 +9,15 @@ and the head) is one CUDA-graph replay.
 
 The attention layers' hot path — q/k RMSNorm + RoPE + paged KV append +
 split-KV attention — runs in libb2attn.so's fused decode step.  Around it
-(fused_glue=True, the default) the layer's projections are libb2attn.so's
-tensor-core GEMM (b2_gemm; w1 and w3 stacked into one product with the
-SwiGLU gate as its epilogue), and the residual adds + RMSNorms and the
-short-convolution step are libb2attn.so kernels too (b2_add_rmsnorm,
-b2_shortconv_step); own_gemm=False runs the projections as cuBLAS GEMMs
-(torch.matmul) with b2_swiglu after the stacked w1/w3 product, and
-fused_glue=False runs all of the glue as plain torch ops.
+(fused_glue=True, the default) the residual adds + RMSNorms, the SwiGLU gate
+and the short-convolution step are libb2attn.so kernels too (b2_add_rmsnorm,
+b2_swiglu, b2_shortconv_step); fused_glue=False runs that glue as plain
+torch ops.  The projections are cuBLAS GEMMs (torch.matmul, w1 and w3
+stacked into one) by default; own_gemm=True runs them on libb2attn.so's
+tensor-core GEMM (b2_gemm, with the SwiGLU gate as the epilogue of the
+stacked w1/w3 product), which at batch 256 is 1.2-1.7x slower than cuBLAS per
+projection.  With fused_glue=False and own_gemm=True the torch glue runs
+around b2_gemm products, the w1/w3 product tiled as in the fused epilogue.
 Both follow the model definition the reference's CPU path uses
 (transformers modeling_lfm2.py: Lfm2RMSNorm 59-64, Lfm2MLP 135-152,
 Lfm2ShortConv.slow_forward 356-387, Lfm2DecoderLayer.forward 413-442,
@@ -72,7 +74,7 @@ class LFM2DecodeRunner:
 
     def __init__(self, state_dict: dict, config: LFM2Config = LFM2Config(), *, max_batch: int,
                  max_context: int, device: torch.device | str = "cuda", use_graph: bool = True,
-                 blocks_per_split: int | None = None, fused_glue: bool = True, own_gemm: bool = True):
+                 blocks_per_split: int | None = None, fused_glue: bool = True, own_gemm: bool = False):
         self.cfg = config
         self.device = torch.device(device)
         self.max_batch = max_batch
@@ -129,7 +131,7 @@ class LFM2DecodeRunner:
         self.use_graph = use_graph and self.device.type == "cuda"
         self._graph = None
         self.fused_glue = fused_glue
-        self.own_gemm = fused_glue and own_gemm
+        self.own_gemm = own_gemm
         self.gemm_err = torch.zeros(1, dtype=torch.int32, device=dev)
         if fused_glue:
             ffn = self.layers[0]["w1"].shape[0]
@@ -191,31 +193,49 @@ class LFM2DecodeRunner:
         block.argmax_rows(self.logits, out=self.next_ids)
         self.past.add_(1)
 
+    def _proj(self, a: torch.Tensor, w: torch.Tensor, **tiling) -> torch.Tensor:
+        """a @ w.T into a new tensor: b2_gemm, or cuBLAS with own_gemm=False."""
+        if not self.own_gemm:
+            return a @ w.t()
+        out = torch.empty(a.shape[0], w.shape[0], dtype=a.dtype, device=a.device)
+        return block.gemm(a, w, out=out, dev_err=self.gemm_err, **tiling)
+
     def _token_torch(self) -> None:
         """The token with the layer glue as torch ops."""
         cfg = self.cfg
         b = self.max_batch
+        ffn = self.layers[0]["w1"].shape[0]
+        # the w1/w3 product as the fused SwiGLU epilogue tiles it (same fp32 sums)
+        t, sp, _ = block.gemm_plan(b, ffn, cfg.hidden, _lib.B2_GEMM_SWIGLU) if self.own_gemm else (0, 0, 0)
         h = self.embed[self.ids]                                   # [B, hidden]
         torch.add(self.past, 1, out=self.seq)
         for lw in self.layers:
             x = rms_norm(h, lw["op_norm"], cfg.eps)
             if lw["kind"] == "attention":
-                qkv = x @ lw["qkv"].t()                             # [B, 2048]: q | k | v
+                qkv = self._proj(x, lw["qkv"])                      # [B, 2048]: q | k | v
                 ctx = self.attn[lw["att"]].step(lw["att"], qkv, self.past, self.seq, self.tables)
-                o = ctx.reshape(b, cfg.heads * cfg.head_dim) @ lw["out"].t()
+                o = self._proj(ctx.reshape(b, cfg.heads * cfg.head_dim), lw["out"])
             else:
-                bcx = x @ lw["in"].t()                              # [B, 3 * hidden]: B | C | x
+                bcx = self._proj(x, lw["in"])                       # [B, 3 * hidden]: B | C | x
                 bg, cg, xg = bcx.split(cfg.hidden, dim=-1)
                 bx = bg * xg
                 st = self.conv_state[lw["conv_id"]]
                 st.copy_(torch.cat([st[..., 1:], bx[..., None]], dim=-1))
                 conv = torch.sum(st * lw["conv"], dim=-1)
-                o = (cg * conv) @ lw["out"].t()
+                o = self._proj(cg * conv, lw["out"])
             h = o + h
             hn = rms_norm(h, lw["ffn_norm"], cfg.eps)
-            h = h + (torch.nn.functional.silu(hn @ lw["w1"].t()) * (hn @ lw["w3"].t())) @ lw["w2"].t()
+            if self.own_gemm:
+                gu = self._proj(hn, lw["w13"], tile_n=t, splits=sp)
+                g, u = gu[:, :ffn], gu[:, ffn:]
+            else:
+                g, u = hn @ lw["w1"].t(), hn @ lw["w3"].t()
+            h = h + self._proj(torch.nn.functional.silu(g) * u, lw["w2"])
         h = rms_norm(h, self.final_norm, cfg.eps)
-        torch.matmul(h, self.head.t(), out=self.logits)
+        if self.own_gemm:
+            block.gemm(h, self.head, out=self.logits, dev_err=self.gemm_err)
+        else:
+            torch.matmul(h, self.head.t(), out=self.logits)
         torch.argmax(self.logits, dim=-1, out=self.next_ids)
         self.past.add_(1)
 

@@ -1,11 +1,15 @@
 """The decode layer's projection GEMM (b2_gemm: tcgen05 tensor cores, TMEM
 accumulators, cluster split-K) against torch references.
 
-The plain product accumulates in fp32 like cuBLAS does, so its bf16 result is
-compared with the fp32 product of the same bf16 operands rounded once to
-bf16: every element within 1 bf16 ulp, and all but a few exact (a different
-fp32 summation order can move a value across a rounding boundary).  The
-SwiGLU epilogue is compared with b2_swiglu applied to that rounded product.
+The plain product accumulates in fp32 like cuBLAS does.  Every element of its
+bf16 result lies within half a bf16 ulp of the exact (fp64) product plus an
+fp32 summation bound, 2^-20 x sum |a_i w_i| (this term only matters where the
+terms cancel and the result is small next to them), and all but a few equal
+the exact product rounded once to bf16 (another fp32 summation order can move
+a value across a rounding boundary).  The SwiGLU epilogue carries those
+bounds on g = a w1^T and u = a w3^T through silu(g) * u (first-order error
+propagation plus the roundings of silu(g) and of the result), and almost all
+of it equals b2_swiglu applied to the fp32 products rounded to bf16.
 """
 import numpy as np
 import pytest
@@ -39,10 +43,18 @@ def operands(m, n, k, seed, dev, rows_w=None):
     return a, w
 
 
+def bf16_ulp(x: np.ndarray) -> np.ndarray:
+    return np.exp2(np.floor(np.log2(np.maximum(np.abs(x), 2.0 ** -126))) - 7)
+
+
 def check_product(got, a, w, what, exact_frac=0.999):
-    ref = (a.float() @ w.float().t()).to(torch.bfloat16)
-    d = ulps(got, ref)
-    assert d.max() <= 1, f"{what}: {int((d > 1).sum())} elements beyond 1 ulp (max {d.max()})"
+    exact = a.double() @ w.double().t()
+    scale = (a.double().abs() @ w.double().abs().t()).cpu().numpy()
+    g, e = got.double().cpu().numpy(), exact.cpu().numpy()
+    tol = 0.5 * bf16_ulp(np.maximum(np.abs(g), np.abs(e))) + 2.0 ** -20 * scale
+    bad = np.abs(g - e) > tol
+    assert not bad.any(), f"{what}: {int(bad.sum())} elements beyond the bound, e.g. got {g[bad][:3]} exact {e[bad][:3]}"
+    d = ulps(got, exact.to(torch.bfloat16))
     assert (d == 0).mean() >= exact_frac, f"{what}: only {(d == 0).mean():.5f} exact"
 
 
@@ -93,8 +105,20 @@ def test_gemm_swiglu_epilogue(cuda, m, ffn):
     blk.swiglu(gu, out=ref)
     torch.cuda.synchronize()
     assert err.item() == 0
+    exact = (a.double() @ w13.double().t()).cpu().numpy()
+    scale = (a.double().abs() @ w13.double().abs().t()).cpu().numpy()
+    g, u = exact[:, :ffn], exact[:, ffn:]
+    dg = 0.5 * bf16_ulp(g) + 2.0 ** -20 * scale[:, :ffn]        # bf16 g: rounding + fp32 summation
+    du = 0.5 * bf16_ulp(u) + 2.0 ** -20 * scale[:, ffn:]
+    silu = g / (1.0 + np.exp(-g))
+    want = silu * u
+    tol = (np.abs(silu) * du + np.abs(u) * 1.1 * dg + np.abs(u) * 0.5 * bf16_ulp(silu)
+           + bf16_ulp(want)) * 1.5
+    got = out.double().cpu().numpy()
+    bad = np.abs(got - want) > tol
+    assert not bad.any(), f"{int(bad.sum())} outputs beyond the bound, e.g. got {got[bad][:3]} exact {want[bad][:3]}"
     d = ulps(out, ref)
-    assert d.max() <= 2 and (d == 0).mean() >= 0.995, f"max {d.max()} ulps, exact {(d == 0).mean():.5f}"
+    assert (d == 0).mean() >= 0.995, f"only {(d == 0).mean():.5f} equal to b2_swiglu of the rounded products"
 
 
 def test_gemm_strided_rows_and_column_slices(cuda):
