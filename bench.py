@@ -642,6 +642,7 @@ def run_b200(args):
         line["config"]["workload"] += f"; ONLY shard {args.shard} of it on this GPU (one rank's part)"
     if rank == 0 and world == 1 and not args.no_sweep and not args.shard:
         line["contexts"] = context_sweep(args, dev)
+        line["prefill"] = prefill_points(args, dev)
     if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.shard:
         rate, info = cpu_reference_rate(base_lengths(args), args.cpu_seconds)
         line["cpu_baseline"] = {"value": rate, "unit": "tokens/s", "cores": torch.get_num_threads(),
@@ -943,20 +944,16 @@ def run_c5(args):
         print(json.dumps(line), flush=True)
 
 
-def run_prefill(args):
-    """Batched-prompt attention (the x8p engine's batched prompt tile, grown to
-    64-token chunks): the C3 batch of 64 sequences with cached prefixes
-    L ~ U[128, 8192], each receiving --chunk new tokens through one attention
-    layer (append of the chunk + tcgen05 attention).  tokens/s counts chunk
-    tokens.  Replicas across GPUs."""
-    world, rank, local = dist_env()
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
+def prefill_point(args, dev, T, K, W, rank=0):
+    """K steps of the batched prompt (a CUDA graph; the K/V pool, 0.5 GB,
+    exceeds L2): the C3 batch of 64 sequences with cached prefixes
+    L ~ U[128, 8192], each receiving T new tokens through one attention layer
+    (append of the chunk + tcgen05 attention).  Returns the timing, the HBM
+    figures and the clocks."""
     attn = importlib.import_module(PKG + ".attention")
     pc = importlib.import_module(PKG + ".paged_cache")
     rope = importlib.import_module(PKG + ".rope")
     lengths = seq_lengths(args, 0)
-    T = args.chunk
     caps = [n + T for n in lengths]
     cache = pc.PagedKVCache(sum(pc.blocks_for(c) for c in caps), max(caps), device=dev,
                             shuffle_seed=args.seed * 1000 + 17)
@@ -978,6 +975,7 @@ def run_prefill(args):
     out = torch.empty(b, T, HQ, D, dtype=torch.bfloat16, device=dev)
     kp, vp = cache.pool(0)
     stream = torch.cuda.Stream(dev)
+    bps = attn.prefill_blocks_per_split(b, T, tables.shape[1]) if args.prefill_bps < 0 else args.prefill_bps
 
     def step():
         attn.prefill(qkv, past, k_pool=kp, v_pool=vp, block_tables=tables, gamma_q=gq, gamma_k=gk, cos=cos,
@@ -985,11 +983,10 @@ def run_prefill(args):
                      blocks_per_split=None if args.prefill_bps < 0 else args.prefill_bps)
 
     with torch.cuda.stream(stream):
-        for _ in range(max(args.warmup, 1)):
+        for _ in range(max(W, 1)):
             step()
     torch.cuda.synchronize()
     assert err.item() == 0, "device error in prefill"
-    K = args.steps
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
         for _ in range(K):
@@ -998,7 +995,7 @@ def run_prefill(args):
     torch.cuda.synchronize()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
+    with ClockSampler(dev.index or 0) as clocks:
         with torch.cuda.stream(stream):
             t0.record()
             graph.replay()
@@ -1011,21 +1008,54 @@ def run_prefill(args):
     flops = sum(4 * HQ * D * sum(n + t + 1 for t in range(T)) for n in lengths)
     peak, peak_kind = measured_hbm_peak()
     gbs = nbytes / (ms / 1e3) / 1e9
+    del graph
+    return {"batch": b, "chunk": T, "ms": ms, "tokens_per_s": b * T / (ms / 1e3), "gbs": gbs,
+            "frac": gbs / peak, "peak": peak, "peak_kind": peak_kind, "bytes": nbytes,
+            "tflops": flops / (ms / 1e3) / 1e12, "blocks_per_split": bps, "clocks": clocks.summary()}
+
+
+def prefill_points(args, dev) -> dict:
+    """The batched-prompt kernel beside the decode line (the reference's x8p
+    4-token prompt batches, and 64 / 128-token chunks): 64 sequences x T."""
+    rows = []
+    for T in (4, 64, 128):
+        pt = prefill_point(args, dev, T, 20, 3)
+        rows.append({"chunk": T, "us_per_step": round(pt["ms"] * 1e3, 2),
+                     "tokens_per_s": round(pt["tokens_per_s"], 1), "gbs": round(pt["gbs"], 1),
+                     "frac": round(pt["frac"], 4), "blocks_per_split": pt["blocks_per_split"]})
+        torch.cuda.empty_cache()
+    return {"note": "batched prompt: the C3 batch (64 sequences, cached L ~ U[128, 8192]) each receiving "
+                    "`chunk` new tokens through one attention layer (chunk append + tcgen05 attention, "
+                    "causal within the chunk); frac of the measured HBM copy peak over K/V read once",
+            "points": rows}
+
+
+def run_prefill(args):
+    """Batched-prompt attention (the x8p engine's batched prompt tile, grown to
+    64-token chunks): the C3 batch of 64 sequences with cached prefixes
+    L ~ U[128, 8192], each receiving --chunk new tokens through one attention
+    layer (append of the chunk + tcgen05 attention).  tokens/s counts chunk
+    tokens.  Replicas across GPUs."""
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    T, K = args.chunk, args.steps
+    pt = prefill_point(args, dev, T, K, args.warmup, rank)
+    ms, gbs, peak = pt["ms"], pt["gbs"], pt["peak"]
     line = {
-        "metric": METRIC, "value": b * T / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": K,
+        "metric": METRIC, "value": pt["tokens_per_s"], "unit": "tokens/s", "n_gpus": 1, "steps": K,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "replicas",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": f"batched prompt: 64 sequences with cached L ~ U[128, 8192] each receiving "
                                f"{T} new tokens through one attention layer (chunk append + tcgen05 "
                                f"attention, causal within the chunk)", "chunk": T,
-                   "prefill_blocks_per_split": (attn.prefill_blocks_per_split(b, T, tables.shape[1])
-                                                if args.prefill_bps < 0 else args.prefill_bps),
-                   "global_batch": b, "parallelism": "replicas"},
-        "hbm_gbs_per_gpu": gbs, "tflops": flops / (ms / 1e3) / 1e12,
+                   "prefill_blocks_per_split": pt["blocks_per_split"],
+                   "global_batch": pt["batch"], "parallelism": "replicas"},
+        "hbm_gbs_per_gpu": gbs, "tflops": pt["tflops"],
         "roofline": {"bound": "hbm", "kernel": "append_rope_kernel + prefill_attn_kernel", "achieved": gbs,
-                     "peak": peak, "peak_source": peak_kind, "unit": "GB/s", "frac": gbs / peak,
-                     "traffic": None, "algorithmic_bytes": nbytes},
-        "clocks": clocks.summary(), "gpu_launches": 2 * K,
+                     "peak": peak, "peak_source": pt["peak_kind"], "unit": "GB/s", "frac": gbs / peak,
+                     "traffic": None, "algorithmic_bytes": pt["bytes"]},
+        "clocks": pt["clocks"], "gpu_launches": 2 * K,
     }
     print(json.dumps(line), flush=True)
 
