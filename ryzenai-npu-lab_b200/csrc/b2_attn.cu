@@ -885,9 +885,6 @@ __device__ __forceinline__ void consumers_sync(StepTail *tail, int lane, uint32_
   __syncwarp();
 }
 
-// Lengths of sequence b: past (RoPE position and, with B2_STORE_KV, the
-// append slot) and seq_len (tokens attended).  False for lengths the block
-// table cannot hold, or an append slot that is not the last attended token.
 // A 4-byte load from read-only memory, issued where it stands: the compiler
 // may not move it next to its first use, so a run of these is in flight
 // together.
@@ -897,6 +894,9 @@ __device__ __forceinline__ int ld_nc_now(const int *p) {
   return v;
 }
 
+// Lengths of sequence b: past (RoPE position and, with B2_STORE_KV, the
+// append slot) and seq_len (tokens attended).  False for lengths the block
+// table cannot hold, or an append slot that is not the last attended token.
 __device__ __forceinline__ bool lengths_ok(const StepArgs &a, int past, int seq_len) {
   bool ok = past >= 0 && seq_len >= 0 && seq_len <= a.max_blocks * kBlock;
   if (a.mode & B2_STORE_KV) ok = ok && seq_len == past + 1;
