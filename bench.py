@@ -944,12 +944,13 @@ def run_c5(args):
         print(json.dumps(line), flush=True)
 
 
-def prefill_point(args, dev, T, K, W, rank=0):
+def prefill_point(args, dev, T, K, W, rank=0, path="prefill"):
     """K steps of the batched prompt (a CUDA graph; the K/V pool, 0.5 GB,
     exceeds L2): the C3 batch of 64 sequences with cached prefixes
     L ~ U[128, 8192], each receiving T new tokens through one attention layer
-    (append of the chunk + tcgen05 attention).  Returns the timing, the HBM
-    figures and the clocks."""
+    (append of the chunk + tcgen05 attention; path "step": the fused decode
+    step for T <= 4 new tokens, b2_decode_step_tokens).  Returns the timing,
+    the HBM figures and the clocks."""
     attn = importlib.import_module(PKG + ".attention")
     pc = importlib.import_module(PKG + ".paged_cache")
     rope = importlib.import_module(PKG + ".rope")
@@ -975,12 +976,24 @@ def prefill_point(args, dev, T, K, W, rank=0):
     out = torch.empty(b, T, HQ, D, dtype=torch.bfloat16, device=dev)
     kp, vp = cache.pool(0)
     stream = torch.cuda.Stream(dev)
-    bps = attn.prefill_blocks_per_split(b, T, tables.shape[1]) if args.prefill_bps < 0 else args.prefill_bps
+    if path == "step":
+        bps = attn.step_tokens_blocks_per_split(b, tables.shape[1])
+        counters = torch.zeros(2 + 8 * b, dtype=torch.int32, device=dev)
+        splits = attn.num_splits_for(tables.shape[1], bps)
+        part_ml = torch.empty(b, T, splits, HQ, 2, dtype=torch.float32, device=dev)
+        part_o = torch.empty(b, T, splits, HQ, D, dtype=torch.float32, device=dev)
 
-    def step():
-        attn.prefill(qkv, past, k_pool=kp, v_pool=vp, block_tables=tables, gamma_q=gq, gamma_k=gk, cos=cos,
-                     sin=sin, dev_err=err, out=out, q_out=q_out,
-                     blocks_per_split=None if args.prefill_bps < 0 else args.prefill_bps)
+        def step():
+            attn.decode_step_tokens(qkv, past, k_pool=kp, v_pool=vp, block_tables=tables, out=out,
+                                    counters=counters, dev_err=err, blocks_per_split=bps, part_ml=part_ml,
+                                    part_o=part_o, gamma_q=gq, gamma_k=gk, cos=cos, sin=sin, q_out=q_out)
+    else:
+        bps = attn.prefill_blocks_per_split(b, T, tables.shape[1]) if args.prefill_bps < 0 else args.prefill_bps
+
+        def step():
+            attn.prefill(qkv, past, k_pool=kp, v_pool=vp, block_tables=tables, gamma_q=gq, gamma_k=gk, cos=cos,
+                         sin=sin, dev_err=err, out=out, q_out=q_out,
+                         blocks_per_split=None if args.prefill_bps < 0 else args.prefill_bps)
 
     with torch.cuda.stream(stream):
         for _ in range(max(W, 1)):
@@ -1018,9 +1031,10 @@ def prefill_points(args, dev) -> dict:
     """The batched-prompt kernel beside the decode line (the reference's x8p
     4-token prompt batches, and 64 / 128-token chunks): 64 sequences x T."""
     rows = []
-    for T in (4, 64, 128):
-        pt = prefill_point(args, dev, T, 20, 3)
-        rows.append({"chunk": T, "us_per_step": round(pt["ms"] * 1e3, 2),
+    for T, path in ((4, "prefill"), (64, "prefill"), (128, "prefill"), (4, "step")):
+        pt = prefill_point(args, dev, T, 20, 3, path=path)
+        rows.append({"chunk": T, "kernel": "decode_step_kernel (b2_decode_step_tokens)" if path == "step"
+                     else "prefill_attn_kernel (tcgen05)", "us_per_step": round(pt["ms"] * 1e3, 2),
                      "tokens_per_s": round(pt["tokens_per_s"], 1), "gbs": round(pt["gbs"], 1),
                      "frac": round(pt["frac"], 4), "blocks_per_split": pt["blocks_per_split"]})
         torch.cuda.empty_cache()

@@ -237,6 +237,37 @@ int b2_decode_step(const uint16_t *qkv, int64_t row_stride,
                    int32_t max_ctas, int32_t *dev_err, void *stream);
 
 /*
+ * The fused decode step for 1 to 4 new tokens per sequence (a prompt chunk,
+ * or the reference's x8p engine's 4-token batches,
+ * experiments/kernels/x8/x8p_core.cc:137-226 attn_prep/attn_block4): q/k
+ * RMSNorm + RoPE of every new token t at position past_lens[b] + t, the
+ * append of its k/v into that slot, and attention of token t over the
+ * cached tokens and the new tokens up to itself (causal), in one launch at
+ * the decode kernel's streaming rate (its tensor-core tile has 8 query
+ * columns: tokens x the GQA pair).  tokens == 1 is b2_decode_step.
+ *
+ * qkv          row b * tokens + t (stride row_stride) = the raw [q | k | v]
+ *              projections of token t of sequence b.
+ * chunk_lens   NULL: every sequence has `tokens` new tokens; else int32
+ *              [batch], 1 .. tokens of them valid (the rest of the rows
+ *              are ignored and their contexts left unwritten).  Unused
+ *              with tokens == 1.
+ * out, q_out   bf16 [batch][tokens][16][64] (q_out optional).
+ * part_ml/o    fp32 [batch][tokens][num_splits][16][2 / 64] with num_splits
+ *              = ceil(max_blocks_per_seq / blocks_per_split), which must be
+ *              at most 16 for tokens > 1 (the kernel merges the splits).
+ * counters, blocks_per_split, mode, max_ctas as b2_decode_step; 2 CTAs per SM
+ * for tokens > 1.
+ */
+int b2_decode_step_tokens(const uint16_t *qkv, int64_t row_stride, int32_t tokens, const int32_t *chunk_lens,
+                          const uint16_t *gamma_q, const uint16_t *gamma_k, float eps, const uint16_t *rope_cos,
+                          const uint16_t *rope_sin, int32_t rope_rows, const int32_t *past_lens,
+                          const int32_t *block_tables, int32_t max_blocks_per_seq, uint16_t *k_pool,
+                          uint16_t *v_pool, int32_t num_blocks, int32_t batch, int32_t blocks_per_split,
+                          float scale, int32_t mode, uint16_t *out, uint16_t *q_out, float *part_ml,
+                          float *part_o, int32_t *counters, int32_t max_ctas, int32_t *dev_err, void *stream);
+
+/*
  * One decode step fed from host memory, in one call and stream order: copy
  * the qkv rows (batch x 2048 bf16, packed) and past lengths from pinned host
  * memory into the caller's device staging buffers, run b2_decode_step

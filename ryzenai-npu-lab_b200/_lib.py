@@ -113,6 +113,16 @@ SIGNATURES = {
         _f32, _i32,          # scale, blocks_per_split
         _p, _p, _p, _p, _p,  # part_ml, part_o, out, dev_err, stream
     ]),
+    "b2_decode_step_tokens": (ctypes.c_int, [
+        _p, ctypes.c_int64, _i32, _p,  # qkv, row_stride, tokens, chunk_lens
+        _p, _p, _f32,        # gamma_q, gamma_k, eps
+        _p, _p, _i32,        # rope_cos, rope_sin, rope_rows
+        _p, _p, _i32,        # past_lens, block_tables, max_blocks_per_seq
+        _p, _p, _i32,        # k_pool, v_pool, num_blocks
+        _i32, _i32, _f32, _i32,  # batch, blocks_per_split, scale, mode
+        _p, _p, _p, _p,      # out, q_out, part_ml, part_o
+        _p, _i32, _p, _p,    # counters, max_ctas, dev_err, stream
+    ]),
     "b2_decode_step_exchange": (ctypes.c_int, [
         _p, ctypes.c_int64,  # qkv, row_stride
         _p, _p, _f32,        # gamma_q, gamma_k, eps

@@ -276,6 +276,83 @@ def decode_step(qkv: torch.Tensor, past_lens: torch.Tensor, *, k_pool: torch.Ten
     return splits
 
 
+MAX_STEP_TOKENS = 4   # new tokens per sequence of b2_decode_step_tokens
+MAX_MERGED_SPLITS = 16
+
+
+def step_tokens_blocks_per_split(batch: int, max_blocks: int, sms: int = B200_SMS) -> int:
+    """Split size for b2_decode_step_tokens: the decode step's heuristic, but
+    at most 16 splits per sequence (the kernel merges them itself)."""
+    bps = choose_blocks_per_split(batch, batch * max_blocks, sms, fused=True, max_blocks_per_seq=max_blocks)
+    return int(max(bps, math.ceil(max_blocks / MAX_MERGED_SPLITS)))
+
+
+def decode_step_tokens(qkv: torch.Tensor, past_lens: torch.Tensor, *, k_pool: torch.Tensor, v_pool: torch.Tensor,
+                       block_tables: torch.Tensor, out: torch.Tensor, counters: torch.Tensor,
+                       dev_err: torch.Tensor, blocks_per_split: int | None = None,
+                       part_ml: torch.Tensor | None = None, part_o: torch.Tensor | None = None,
+                       gamma_q: torch.Tensor | None = None, gamma_k: torch.Tensor | None = None,
+                       cos: torch.Tensor | None = None, sin: torch.Tensor | None = None,
+                       q_out: torch.Tensor | None = None, chunk_lens: torch.Tensor | None = None,
+                       mode: int = _lib.B2_NORM_QK | _lib.B2_ROPE_QK | _lib.B2_STORE_KV, eps: float = EPS,
+                       scale: float = SCALE, max_ctas: int = 0, stream: torch.cuda.Stream | None = None) -> int:
+    """The fused decode step for T = 1..4 new tokens per sequence
+    (b2_decode_step_tokens): qkv bf16 [B, T, >= 2048] raw projections of the
+    tokens at positions past_lens[b] + t (chunk_lens[b] of them valid, all
+    when None); appends their k/v, writes the contexts out [B, T, 16, 64]
+    (token t attends the cache and the new tokens up to itself).  Returns the
+    number of splits."""
+    dev = qkv.device
+    if qkv.dim() != 3 or qkv.shape[2] < QKV_WIDTH:
+        raise ValueError(f"qkv must be [batch, tokens, >= {QKV_WIDTH}], got {tuple(qkv.shape)}")
+    b, t = qkv.shape[0], qkv.shape[1]
+    if not 1 <= t <= MAX_STEP_TOKENS:
+        raise ValueError(f"tokens must be in [1, {MAX_STEP_TOKENS}], got {t}")
+    if qkv.dtype != torch.bfloat16 or qkv.device != dev or qkv.stride(2) != 1 or qkv.stride(0) != t * qkv.stride(1):
+        raise ValueError("qkv must be bf16 with rows b * tokens + t at a common stride")
+    _need(past_lens, "past_lens", torch.int32, dev, (b,))
+    if chunk_lens is not None:
+        _need(chunk_lens, "chunk_lens", torch.int32, dev, (b,))
+    _need(k_pool, "k_pool", torch.bfloat16, dev)
+    _need(v_pool, "v_pool", torch.bfloat16, dev, tuple(k_pool.shape))
+    if k_pool.dim() != 4 or tuple(k_pool.shape[1:]) != (HKV, BLOCK, D):
+        raise ValueError("pools must be [num_blocks, 8, 64, 64]")
+    _need(block_tables, "block_tables", torch.int32, dev)
+    if block_tables.dim() != 2 or block_tables.shape[0] != b:
+        raise ValueError("block_tables must be [batch, max_blocks_per_seq]")
+    _need(out, "out", torch.bfloat16, dev, (b, t, HQ, D))
+    if q_out is not None:
+        _need(q_out, "q_out", torch.bfloat16, dev, (b, t, HQ, D))
+    _need(counters, "counters", torch.int32, dev)
+    if counters.numel() < 2 + HKV * b:
+        raise ValueError("counters must hold 2 + 8 * batch int32")
+    _need(dev_err, "dev_err", torch.int32, dev)
+    rope_rows = 0
+    if mode & _lib.B2_NORM_QK:
+        _need(gamma_q, "gamma_q", torch.bfloat16, dev, (D,))
+        _need(gamma_k, "gamma_k", torch.bfloat16, dev, (D,))
+    if mode & _lib.B2_ROPE_QK:
+        rope_rows = _need_rope(cos, sin, dev)
+    max_blocks = block_tables.shape[1]
+    bps = blocks_per_split or step_tokens_blocks_per_split(b, max_blocks)
+    splits = num_splits_for(max_blocks, bps)
+    if part_ml is None:
+        part_ml = torch.empty(b, t, splits, HQ, 2, dtype=torch.float32, device=dev)
+    if part_o is None:
+        part_o = torch.empty(b, t, splits, HQ, D, dtype=torch.float32, device=dev)
+    _need(part_ml, "part_ml", torch.float32, dev)
+    _need(part_o, "part_o", torch.float32, dev)
+    if part_ml.numel() < b * t * splits * HQ * 2 or part_o.numel() < b * t * splits * HQ * D:
+        raise ValueError(f"partial-state buffers too small for {b} x {t} x {splits} splits")
+    rc = _lib.load().b2_decode_step_tokens(
+        _ptr(qkv), qkv.stride(1), t, _ptr(chunk_lens), _ptr(gamma_q), _ptr(gamma_k), ctypes.c_float(eps), _ptr(cos),
+        _ptr(sin), rope_rows, _ptr(past_lens), _ptr(block_tables), max_blocks, _ptr(k_pool), _ptr(v_pool),
+        k_pool.shape[0], b, bps, ctypes.c_float(scale), mode, _ptr(out), _ptr(q_out), _ptr(part_ml), _ptr(part_o),
+        _ptr(counters), max_ctas, _ptr(dev_err), _stream(dev, stream))
+    _lib.check(rc, "b2_decode_step_tokens")
+    return splits
+
+
 def merge_states(states: torch.Tensor, num_parts: int, batch: int, *, out: torch.Tensor | None = None,
                  state_ml: torch.Tensor | None = None, state_o: torch.Tensor | None = None,
                  stream: torch.cuda.Stream | None = None) -> None:

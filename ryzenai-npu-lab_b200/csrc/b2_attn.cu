@@ -811,10 +811,13 @@ constexpr int kFlagLast = 2;   // last block of an item: epilogue
 constexpr int kFlagFinal = 4;  // the item is the whole sequence: write the context directly
 constexpr int kFlagEnd = 8;    // no more work
 
-struct __align__(16) StageMeta {
-  int b, kvh, split, rows;   // rows: valid rows of this block (may exceed 64)
-  int flags, nsplit, pad0, pad1;
-  uint16_t q[2 * kDim];      // bf16 q of heads 2kvh, 2kvh+1 (first block of an item)
+// kT: the largest number of new tokens per sequence of the instantiation (1,
+// or 4 for b2_decode_step_tokens).
+template <int kT>
+struct __align__(16) StageMetaT {
+  int b, kvh, split, rows;   // rows: valid rows of this block for the item's last token (may exceed 64)
+  int flags, nsplit, ntok, pad1;  // ntok: new tokens of the sequence (1 when kT == 1)
+  uint16_t q[kT * 2 * kDim];  // bf16 q [token][head 2kvh, 2kvh+1][64] (first block of an item)
 };
 
 // Batches up to this size enumerate only real work items: the producer
@@ -831,21 +834,27 @@ constexpr int kMergerWarp = kConsumerWarps + 1;
 constexpr int kStepThreads = (kConsumerWarps + 2) * 32;
 constexpr int kPubSlots = 4;  // items published to the merger warp, in flight
 constexpr int kMergeInKernelSplits = 16;  // at most 32: one split per merger lane
+constexpr int kMaxStepTokens = 4;  // new tokens per sequence of b2_decode_step_tokens (N = 8 mma columns / 2 heads)
 constexpr int kStepMaxBlocksPerSplit = 64;  // two block-table entries per producer lane
 
-struct __align__(16) StepTail {
+template <int kT>
+struct __align__(16) StepTailT {
   uint64_t full[kStages];
   uint64_t empty[kStages];
   uint64_t ebar;  // consumer-warp barrier of the epilogue (bounded waits)
   uint64_t stall;  // never completed: the wait of B2_TEST_STALL runs out on it
   uint64_t pub[kPubSlots];    // consumers -> merger: a partial state is in memory
   uint64_t pfree[kPubSlots];  // merger -> consumers: the slot may be reused
-  int4 pubinfo[kPubSlots];    // (b, kv head, split, nsplit); b < 0 ends the work
-  StageMeta meta[kStages];
-  float red[2][kConsumerWarps][2][2 + kDim];  // double-buffered by epilogue parity
+  int4 pubinfo[kPubSlots];    // (b, kv head, split or new tokens, nsplit); b < 0 ends the work
+  StageMetaT<kT> meta[kStages];
+  float red[2][kConsumerWarps][2 * kT][2 + kDim];  // double-buffered by epilogue parity; [token][head]
   int prefix[kMaxCompactBatch + 1];  // prefix[b] = splits of sequences 0..b-1
 };
-constexpr int kStepSmem = kStages * kStageBytes + 1024 + (int)sizeof(StepTail);
+template <int kT>
+constexpr int step_smem() { return kStages * kStageBytes + 1024 + (int)sizeof(StepTailT<kT>); }
+// CTAs per SM: 3 with one token (74 KB of shared memory each), 2 with up to 4
+template <int kT>
+constexpr int step_ctas_per_sm() { return kT == 1 ? 3 : 2; }
 
 struct StepArgs {
   const uint16_t *qkv;
@@ -871,11 +880,17 @@ struct StepArgs {
   int32_t *counters;  // [0] work counter, [1] finished CTAs, [2 + b * 8 + kv head] split arrivals
   int32_t *err;
   uint64_t wait_ns;  // limit of a wait on another warp
+  // b2_decode_step_tokens: up to `tokens` new tokens per sequence (rows b *
+  // tokens + t of qkv; chunk_lens[b] of them valid, all when NULL); contexts,
+  // q_out and partial states gain a token index after the sequence's
+  int tokens;
+  const int32_t *chunk_lens;
 };
 
 // Barrier of the 4 consumer warps on an mbarrier, with a bounded wait (a
 // hardware named barrier could not give up if a warp had left on a timeout).
-__device__ __forceinline__ void consumers_sync(StepTail *tail, int lane, uint32_t &phase, int32_t *err,
+template <class Tail>
+__device__ __forceinline__ void consumers_sync(Tail *tail, int lane, uint32_t &phase, int32_t *err,
                                                uint64_t limit_ns) {
   __syncwarp();
   if (lane == 0) mbar_arrive(smem_u32(&tail->ebar));
@@ -903,10 +918,26 @@ __device__ __forceinline__ bool lengths_ok(const StepArgs &a, int past, int seq_
   return ok;
 }
 
-__device__ __forceinline__ bool step_lengths(const StepArgs &a, int b, int &past, int &seq_len) {
+// Several new tokens (kT > 1): the chunk of sequence b is chunk_lens[b]
+// (all `tokens` when NULL), its tokens sit at past .. past + chunk - 1, and the
+// last of them attends past + chunk tokens.
+__device__ __forceinline__ bool chunk_ok(const StepArgs &a, int past, int chunk) {
+  return past >= 0 && chunk >= 1 && chunk <= a.tokens &&
+         static_cast<int64_t>(past) + chunk <= static_cast<int64_t>(a.max_blocks) * kBlock;
+}
+
+template <int kT>
+__device__ __forceinline__ bool step_lengths(const StepArgs &a, int b, int &past, int &seq_len, int &ntok) {
   past = __ldg(a.past_lens + b);
-  seq_len = a.seq_lens ? __ldg(a.seq_lens + b) : past + 1;
-  return lengths_ok(a, past, seq_len);
+  if constexpr (kT == 1) {
+    ntok = 1;
+    seq_len = a.seq_lens ? __ldg(a.seq_lens + b) : past + 1;
+    return lengths_ok(a, past, seq_len);
+  } else {
+    ntok = a.chunk_lens ? __ldg(a.chunk_lens + b) : a.tokens;
+    seq_len = past + ntok;
+    return chunk_ok(a, past, ntok);
+  }
 }
 
 // Empty result of sequence e (nothing to attend): a zero context, or the
@@ -923,19 +954,21 @@ __device__ __forceinline__ void write_empty_result(const StepArgs &a, int e, int
 }
 
 // One work item as the producer sees it, with its loads already issued.
+template <int kT>
 struct ProducerItem {
-  int valid, b, kvh, split, past, seq_len, nsplit, blk0, n;
+  int valid, b, kvh, split, past, seq_len, nsplit, blk0, n, ntok;
   int my_blk;   // block table entry blk0 + lane (lane < n); entries from 32 on are read when needed
-  uint4 raw;    // this lane's 16 bytes of the item's q/k/v vectors
+  uint4 raw[kT];  // this lane's 16 bytes of the item's q/k/v vectors, per new token
 };
 
 // Decode work index w and issue its loads.  Compact enumeration: w = p * 8 +
 // kvh over the real (sequence, split) pairs p; dense: w = (split * batch + b)
 // * 8 + kvh, returning valid = 0 for a split past the sequence's end (the
 // caller skips it) and -1 past the end of the work.
-__device__ __forceinline__ ProducerItem producer_load(const StepArgs &a, const StepTail *tail, bool compact,
-                                                      int total, int w, int lane) {
-  ProducerItem it;
+template <int kT>
+__device__ __forceinline__ ProducerItem<kT> producer_load(const StepArgs &a, const StepTailT<kT> *tail, bool compact,
+                                                          int total, int w, int lane) {
+  ProducerItem<kT> it;
   it.valid = -1;
   if (w >= total) return it;
   it.valid = 1;
@@ -953,7 +986,7 @@ __device__ __forceinline__ ProducerItem producer_load(const StepArgs &a, const S
     it.split = p / a.batch;
     it.b = p - it.split * a.batch;
   }
-  const bool len_ok = step_lengths(a, it.b, it.past, it.seq_len);
+  const bool len_ok = step_lengths<kT>(a, it.b, it.past, it.seq_len, it.ntok);
   const int nblk = (it.seq_len + kBlock - 1) / kBlock;
   it.nsplit = (nblk + a.blocks_per_split - 1) / a.blocks_per_split;
   if (!len_ok || it.split >= it.nsplit) {
@@ -966,7 +999,15 @@ __device__ __forceinline__ ProducerItem producer_load(const StepArgs &a, const S
   it.my_blk = lane < it.n ? __ldg(a.block_tables + (int64_t)it.b * a.max_blocks + it.blk0 + lane) : 0;
   const int grp = lane >> 3;
   const int vec = grp < 2 ? 2 * it.kvh + grp : (grp == 2 ? kHq + it.kvh : kHq + kHkv + it.kvh);
-  it.raw = __ldg(reinterpret_cast<const uint4 *>(a.qkv + it.b * a.row_stride + vec * kDim + (lane & 7) * 8));
+  if constexpr (kT == 1) {
+    it.raw[0] = __ldg(reinterpret_cast<const uint4 *>(a.qkv + it.b * a.row_stride + vec * kDim + (lane & 7) * 8));
+  } else {
+#pragma unroll
+    for (int t = 0; t < kT; ++t)
+      if (t < it.ntok)
+        it.raw[t] = __ldg(reinterpret_cast<const uint4 *>(a.qkv + ((int64_t)it.b * a.tokens + t) * a.row_stride +
+                                                          vec * kDim + (lane & 7) * 8));
+  }
   return it;
 }
 
@@ -975,7 +1016,8 @@ __device__ __forceinline__ ProducerItem producer_load(const StepArgs &a, const S
 // this item's copies wait for free stages), prepares q (and the appended k/v
 // on the item holding the new token) with all 32 lanes, and lane 0 issues
 // the TMA loads.  Lanes 0-15 hold the two q heads, 16-23 k, 24-31 v.
-__device__ __forceinline__ void step_producer(const StepArgs &a, StepTail *tail, uint8_t *tiles,
+template <int kT>
+__device__ __forceinline__ void step_producer(const StepArgs &a, StepTailT<kT> *tail, uint8_t *tiles,
                                               const CUtensorMap *tm_k, const CUtensorMap *tm_v,
                                               int lane) {
   int32_t *work_ctr = a.counters;
@@ -1000,7 +1042,10 @@ __device__ __forceinline__ void step_producer(const StepArgs &a, StepTail *tail,
       if (32 * k < a.batch) {
         const int b = min(32 * k + lane, a.batch - 1);
         pl[k] = ld_nc_now(a.past_lens + b);
-        sl[k] = a.seq_lens ? ld_nc_now(a.seq_lens + b) : 0;
+        if constexpr (kT == 1)
+          sl[k] = a.seq_lens ? ld_nc_now(a.seq_lens + b) : 0;
+        else  // the chunk; the sequence attends past + chunk tokens
+          sl[k] = a.chunk_lens ? ld_nc_now(a.chunk_lens + b) : a.tokens;
       }
     }
     int running = 0;
@@ -1011,8 +1056,15 @@ __device__ __forceinline__ void step_producer(const StepArgs &a, StepTail *tail,
       int ns = 0;
       bool empty = false;
       if (b < a.batch) {
-        if (!a.seq_lens) sl[k] = pl[k] + 1;
-        if (lengths_ok(a, pl[k], sl[k])) {
+        bool len_ok;
+        if constexpr (kT == 1) {
+          if (!a.seq_lens) sl[k] = pl[k] + 1;
+          len_ok = lengths_ok(a, pl[k], sl[k]);
+        } else {
+          len_ok = chunk_ok(a, pl[k], sl[k]);
+          sl[k] += pl[k];
+        }
+        if (len_ok) {
           const int nblk = (sl[k] + kBlock - 1) / kBlock;
           ns = (nblk + a.blocks_per_split - 1) / a.blocks_per_split;
           empty = sl[k] == 0;
@@ -1040,10 +1092,11 @@ __device__ __forceinline__ void step_producer(const StepArgs &a, StepTail *tail,
     if (lane == 0) tail->prefix[0] = 0;
     __syncwarp();
     total = running * kHkv;
-  } else if (blockIdx.x == 0) {
+  } else if (kT == 1 && blockIdx.x == 0) {
     // Sequences with nothing to attend (seq_lens[b] == 0) get no work item:
     // write their empty result here.  The lengths of 32 * kChunks sequences
-    // are loaded before any is examined.
+    // are loaded before any is examined.  (With new tokens every sequence
+    // attends at least one.)
     for (int c0 = 0; c0 < a.batch; c0 += 32 * kChunks) {
       int pl[kChunks], sl[kChunks];
 #pragma unroll
@@ -1072,7 +1125,7 @@ __device__ __forceinline__ void step_producer(const StepArgs &a, StepTail *tail,
   // first copies); the counter hands out gridDim.x, gridDim.x + 1, ... after it.
   bool first_claim = true;
   auto next_item = [&]() {
-    ProducerItem it;
+    ProducerItem<kT> it;
     do {
       int w = 0;
       if (first_claim) {
@@ -1082,13 +1135,13 @@ __device__ __forceinline__ void step_producer(const StepArgs &a, StepTail *tail,
         if (lane == 0) w = atomicAdd(work_ctr, 1) + static_cast<int>(gridDim.x);
         w = __shfl_sync(0xffffffffu, w, 0);
       }
-      it = producer_load(a, tail, compact, total, w, lane);
+      it = producer_load<kT>(a, tail, compact, total, w, lane);
     } while (it.valid == 0);
     return it;
   };
-  ProducerItem nxt = next_item();
+  ProducerItem<kT> nxt = next_item();
   while (nxt.valid > 0) {
-    const ProducerItem cur = nxt;
+    const ProducerItem<kT> cur = nxt;
     // start the next item's counter update before this item's work
     int w_next = 0;
     if (lane == 0) w_next = atomicAdd(work_ctr, 1) + static_cast<int>(gridDim.x);
@@ -1096,10 +1149,46 @@ __device__ __forceinline__ void step_producer(const StepArgs &a, StepTail *tail,
     const int new_idx = stores ? cur.past / kBlock - cur.blk0 : -1;  // block receiving the new token
     // The q/k work of the item: norm + RoPE of its q, k (and the appended k/v
     // rows with a fence, so the TMA read of that tile sees them).
-    uint4 packed = make_uint4(0u, 0u, 0u, 0u);
+    uint4 packed[kT];
     auto qk_work = [&]() {
+      if constexpr (kT > 1) {
+        // several new tokens: token t at position past + t; its k/v row is
+        // appended by the item whose blocks hold that position
+#pragma unroll
+        for (int t = 0; t < kT; ++t) {
+          if (t >= cur.ntok) break;
+          float x[8];
+          unpack8(cur.raw[t], x);
+          const int pos = cur.past + t;
+          const bool rope_ok = pos < a.rope_rows;
+          if ((a.mode & B2_ROPE_QK) && !rope_ok && lane == 0 && cur.split == 0 && cur.kvh == 0)
+            atomicOr(a.err, B2_DEV_BAD_POSITION);
+          const bool rope = grp < 3 && (a.mode & B2_ROPE_QK) && rope_ok;
+          norm_rope8(x, j, norm, rope, grp < 2 ? a.gamma_q : a.gamma_k, a.eps,
+                     rope ? a.cos + (int64_t)pos * kDim : nullptr, rope ? a.sin + (int64_t)pos * kDim : nullptr);
+          packed[t] = pack8(x);
+          if (cur.split == 0 && grp < 2 && a.q_out)
+            *reinterpret_cast<uint4 *>(a.q_out + (((int64_t)cur.b * a.tokens + t) * kHq + 2 * cur.kvh + grp) * kDim +
+                                       j * 8) = packed[t];
+          const int idx = pos / kBlock - cur.blk0;  // the same in every lane
+          if ((a.mode & B2_STORE_KV) && idx >= 0 && idx < cur.n) {
+            const int nb = idx < 32 ? __shfl_sync(0xffffffffu, cur.my_blk, idx)
+                                    : __ldg(a.block_tables + (int64_t)cur.b * a.max_blocks + cur.blk0 + idx);
+            if (nb < 0 || nb >= a.num_blocks) {
+              if (lane == 0) atomicOr(a.err, B2_DEV_BAD_BLOCK);
+            } else if (grp >= 2) {
+              uint16_t *pool = grp == 2 ? a.k_pool : a.v_pool;
+              *reinterpret_cast<uint4 *>(
+                  pool + (((int64_t)nb * kHkv + cur.kvh) * kBlock + pos % kBlock) * kDim + j * 8) = packed[t];
+              asm volatile("fence.proxy.async.global;" ::: "memory");
+            }
+          }
+        }
+        return;
+      }
+      uint4 &packed0 = packed[0];
       float x[8];
-      unpack8(cur.raw, x);
+      unpack8(cur.raw[0], x);
       const bool rope_ok = cur.past < a.rope_rows;
       if ((a.mode & B2_ROPE_QK) && !rope_ok && lane == 0 && cur.split == 0 && cur.kvh == 0)
         atomicOr(a.err, B2_DEV_BAD_POSITION);
@@ -1107,9 +1196,9 @@ __device__ __forceinline__ void step_producer(const StepArgs &a, StepTail *tail,
       norm_rope8(x, j, norm, rope, grp < 2 ? a.gamma_q : a.gamma_k, a.eps,
                  rope ? a.cos + (int64_t)cur.past * kDim : nullptr,
                  rope ? a.sin + (int64_t)cur.past * kDim : nullptr);
-      packed = pack8(x);
+      packed0 = pack8(x);
       if (cur.split == 0 && grp < 2 && a.q_out)
-        *reinterpret_cast<uint4 *>(a.q_out + ((int64_t)cur.b * kHq + 2 * cur.kvh + grp) * kDim + j * 8) = packed;
+        *reinterpret_cast<uint4 *>(a.q_out + ((int64_t)cur.b * kHq + 2 * cur.kvh + grp) * kDim + j * 8) = packed0;
       if (stores) {
         // The new token's row lies in this item's last block: write it, then
         // fence so the TMA (async proxy) read of that tile sees the store.
@@ -1121,7 +1210,7 @@ __device__ __forceinline__ void step_producer(const StepArgs &a, StepTail *tail,
         } else if (grp >= 2) {
           uint16_t *pool = grp == 2 ? a.k_pool : a.v_pool;
           *reinterpret_cast<uint4 *>(
-              pool + (((int64_t)nb * kHkv + cur.kvh) * kBlock + cur.past % kBlock) * kDim + j * 8) = packed;
+              pool + (((int64_t)nb * kHkv + cur.kvh) * kBlock + cur.past % kBlock) * kDim + j * 8) = packed0;
           asm volatile("fence.proxy.async.global;" ::: "memory");
         }
       }
@@ -1140,8 +1229,9 @@ __device__ __forceinline__ void step_producer(const StepArgs &a, StepTail *tail,
       if (jj == 32)
         blk_hi = lane + 32 < cur.n ? __ldg(a.block_tables + (int64_t)cur.b * a.max_blocks + cur.blk0 + 32 + lane) : 0;
       int blk = __shfl_sync(0xffffffffu, jj < 32 ? cur.my_blk : blk_hi, jj & 31);
-      StageMeta &m = tail->meta[s];
+      StageMetaT<kT> &m = tail->meta[s];
       if (lane == 0) {
+        if constexpr (kT > 1) m.ntok = cur.ntok;
         if (blk < 0 || blk >= a.num_blocks) {
           atomicOr(a.err, B2_DEV_BAD_BLOCK);
           blk = 0;  // read a valid tile instead; the result is flagged as bad
@@ -1163,7 +1253,10 @@ __device__ __forceinline__ void step_producer(const StepArgs &a, StepTail *tail,
     // start earlier anyway.  A first block that receives the new token is
     // copied after the store and its fence in either case.
     const bool early = issued < kStages;
-    const bool first_later = new_idx == 0;
+    // (several tokens: some token's position lies in the item's first block)
+    const bool first_later = kT == 1 ? new_idx == 0
+                                     : (a.mode & B2_STORE_KV) && cur.past / kBlock <= cur.blk0 &&
+                                           cur.blk0 <= (cur.past + cur.ntok - 1) / kBlock;
     {
       const int s = issued % kStages;
       const uint32_t full = smem_u32(&tail->full[s]);
@@ -1187,7 +1280,15 @@ __device__ __forceinline__ void step_producer(const StepArgs &a, StepTail *tail,
         }
         row = write_meta(0, s);
       }
-      if (grp < 2) *reinterpret_cast<uint4 *>(tail->meta[s].q + grp * kDim + j * 8) = packed;
+      if (grp < 2) {
+        if constexpr (kT == 1) {
+          *reinterpret_cast<uint4 *>(tail->meta[s].q + grp * kDim + j * 8) = packed[0];
+        } else {
+#pragma unroll
+          for (int t = 0; t < kT; ++t)
+            if (t < cur.ntok) *reinterpret_cast<uint4 *>(tail->meta[s].q + (2 * t + grp) * kDim + j * 8) = packed[t];
+        }
+      }
       __syncwarp();
       if (lane == 0) {
         if (!early) mbar_expect_tx(full, kStageBytes);  // arrival + expected bytes
@@ -1200,7 +1301,7 @@ __device__ __forceinline__ void step_producer(const StepArgs &a, StepTail *tail,
       ++issued;
       // the first copy of this item is queued: load the next item now
       w_next = __shfl_sync(0xffffffffu, w_next, 0);
-      nxt = producer_load(a, tail, compact, total, w_next, lane);
+      nxt = producer_load<kT>(a, tail, compact, total, w_next, lane);
     }
     for (int jj = 1; jj < cur.n; ++jj, ++issued) {
       const int s = issued % kStages;
@@ -1286,17 +1387,64 @@ __device__ __forceinline__ uint32_t mask_pair(uint32_t v, int tok, int valid) {
 // that follows.  red[] is double-buffered by epilogue parity, so a single
 // barrier separates its writes from its reads and the next epilogue cannot
 // overwrite it early.
-__device__ __forceinline__ void step_epilogue(const StepArgs &a, StepTail *tail, int warp, int lane, int b,
-                                              int kvh, int split, bool final_item, float m0, float m1,
+template <int kT>
+__device__ __forceinline__ void step_epilogue(const StepArgs &a, StepTailT<kT> *tail, int warp, int lane, int b,
+                                              int kvh, int split, bool final_item, int ntok, float m0, float m1,
                                               float l0, float l1, const float o[4][4], uint32_t &ephase,
                                               int rbuf) {
-  float(*red)[2][2 + kDim] = tail->red[rbuf];
+  float(*red)[2 * kT][2 + kDim] = tail->red[rbuf];
 #pragma unroll
   for (int off = 4; off < 32; off <<= 1) {
     l0 += __shfl_xor_sync(0xffffffffu, l0, off);
     l1 += __shfl_xor_sync(0xffffffffu, l1, off);
   }
   const int g = lane >> 2, t = lane & 3;
+  if constexpr (kT > 1) {
+    // lane (g, t) holds token t's state (heads 0, 1) for rows g and g + 8
+    if (t < ntok) {
+#pragma unroll
+      for (int mt = 0; mt < 4; ++mt) {
+        red[warp][2 * t][2 + 16 * mt + g] = o[mt][0];
+        red[warp][2 * t + 1][2 + 16 * mt + g] = o[mt][1];
+        red[warp][2 * t][2 + 16 * mt + g + 8] = o[mt][2];
+        red[warp][2 * t + 1][2 + 16 * mt + g + 8] = o[mt][3];
+      }
+      if (g == 0) {
+        red[warp][2 * t][0] = m0;
+        red[warp][2 * t][1] = l0;
+        red[warp][2 * t + 1][0] = m1;
+        red[warp][2 * t + 1][1] = l1;
+      }
+    }
+    consumers_sync(tail, lane, ephase, a.err, a.wait_ns);
+    // (token, head) column c = 2 token + head, dim d: merge the 4 warps
+    for (int i = threadIdx.x; i < 2 * ntok * kDim; i += kConsumerWarps * 32) {
+      const int c = i >> 6, d = i & 63;
+      const int tok = c >> 1, h = c & 1;
+      float M = -1.0e30f;
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, red[w][c][0]);
+      float L = 0.f, O = 0.f;
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) {
+        const float sc = ex2(red[w][c][0] - M);
+        L = fmaf(red[w][c][1], sc, L);
+        O = fmaf(red[w][c][2 + d], sc, O);
+      }
+      const int64_t row = (int64_t)b * a.tokens + tok;
+      if (final_item) {
+        a.out[(row * kHq + 2 * kvh + h) * kDim + d] = static_cast<uint16_t>(bf16_bits(O / L));
+      } else {
+        const int64_t idx = (row * a.num_splits + split) * kHq + 2 * kvh + h;
+        a.part_o[idx * kDim + d] = O;
+        if (d == 0) {
+          a.part_ml[idx * 2] = M;
+          a.part_ml[idx * 2 + 1] = L;
+        }
+      }
+    }
+    return;
+  }
   if (t == 0) {
 #pragma unroll
     for (int mt = 0; mt < 4; ++mt) {
@@ -1340,7 +1488,8 @@ __device__ __forceinline__ void step_epilogue(const StepArgs &a, StepTail *tail,
 // Hand an item (or, with b < 0, the end of the work) to the merger warp.
 // Every consumer thread arrives (release) after its own stores of the
 // partial state, so the merger sees all of them when the phase completes.
-__device__ __forceinline__ void publish(const StepArgs &a, StepTail *tail, int lane, uint32_t &pubs, int b,
+template <class Tail>
+__device__ __forceinline__ void publish(const StepArgs &a, Tail *tail, int lane, uint32_t &pubs, int b,
                                         int kvh, int split, int nsplit) {
   const int slot = pubs % kPubSlots;
   if (pubs >= kPubSlots && !mbar_wait(smem_u32(&tail->pfree[slot]), ((pubs / kPubSlots) - 1) & 1, a.wait_ns)) {
@@ -1361,7 +1510,8 @@ __device__ __forceinline__ void publish(const StepArgs &a, StepTail *tail, int l
 // lane sp loads split sp's (max, sum) of both heads, the warp reduces the
 // maximum and the rescaled sums with shuffles, then each lane accumulates its
 // two dims of both heads over the splits, loading eight splits per round.
-__device__ __forceinline__ void step_merger(const StepArgs &a, StepTail *tail, int lane) {
+template <int kT>
+__device__ __forceinline__ void step_merger(const StepArgs &a, StepTailT<kT> *tail, int lane) {
   for (uint32_t k = 0;; ++k) {
     const int slot = k % kPubSlots;
     if (!mbar_wait(smem_u32(&tail->pub[slot]), (k / kPubSlots) & 1, a.wait_ns)) {
@@ -1383,54 +1533,114 @@ __device__ __forceinline__ void step_merger(const StepArgs &a, StepTail *tail, i
     last = __shfl_sync(0xffffffffu, last, 0);
     __syncwarp();
     if (!last) continue;
-    const int64_t base = (int64_t)b * a.num_splits * kHq + 2 * kvh;  // (b, split 0, head 2kvh)
-    // (max, sum) of heads 2kvh and 2kvh+1 of split `lane`: 4 adjacent floats
-    float4 ml = make_float4(-1.0e30f, 0.f, -1.0e30f, 0.f);
-    if (lane < nsplit) ml = __ldcg(reinterpret_cast<const float4 *>(a.part_ml + (base + (int64_t)lane * kHq) * 2));
-    float M0 = ml.x, M1 = ml.z;
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      M0 = fmaxf(M0, __shfl_xor_sync(0xffffffffu, M0, off));
-      M1 = fmaxf(M1, __shfl_xor_sync(0xffffffffu, M1, off));
-    }
-    const float c0 = ex2(ml.x - M0), c1 = ex2(ml.z - M1);  // lanes past nsplit carry l = 0
-    float L0 = ml.y * c0, L1 = ml.w * c1;
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      L0 += __shfl_xor_sync(0xffffffffu, L0, off);
-      L1 += __shfl_xor_sync(0xffffffffu, L1, off);
-    }
-    float2 O0 = make_float2(0.f, 0.f), O1 = make_float2(0.f, 0.f);
-    for (int s0 = 0; s0 < nsplit; s0 += 8) {
-      float2 v0[8], v1[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        v0[e] = v1[e] = make_float2(0.f, 0.f);
-        if (s0 + e < nsplit) {
-          const float *po = a.part_o + (base + (int64_t)(s0 + e) * kHq) * kDim + 2 * lane;
-          v0[e] = __ldcg(reinterpret_cast<const float2 *>(po));
-          v1[e] = __ldcg(reinterpret_cast<const float2 *>(po + kDim));
+    // One new token: the merge of (sequence b, kv head) as it stood before
+    // several tokens were added (kept apart: in the lambda form below the
+    // one-token step measured ~3 us slower at C3).
+    if constexpr (kT == 1) {
+      const int64_t base = (int64_t)b * a.num_splits * kHq + 2 * kvh;  // (b, split 0, head 2kvh)
+      // (max, sum) of heads 2kvh and 2kvh+1 of split `lane`: 4 adjacent floats
+      float4 ml = make_float4(-1.0e30f, 0.f, -1.0e30f, 0.f);
+      if (lane < nsplit) ml = __ldcg(reinterpret_cast<const float4 *>(a.part_ml + (base + (int64_t)lane * kHq) * 2));
+      float M0 = ml.x, M1 = ml.z;
+  #pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        M0 = fmaxf(M0, __shfl_xor_sync(0xffffffffu, M0, off));
+        M1 = fmaxf(M1, __shfl_xor_sync(0xffffffffu, M1, off));
+      }
+      const float c0 = ex2(ml.x - M0), c1 = ex2(ml.z - M1);  // lanes past nsplit carry l = 0
+      float L0 = ml.y * c0, L1 = ml.w * c1;
+  #pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        L0 += __shfl_xor_sync(0xffffffffu, L0, off);
+        L1 += __shfl_xor_sync(0xffffffffu, L1, off);
+      }
+      float2 O0 = make_float2(0.f, 0.f), O1 = make_float2(0.f, 0.f);
+      for (int s0 = 0; s0 < nsplit; s0 += 8) {
+        float2 v0[8], v1[8];
+  #pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          v0[e] = v1[e] = make_float2(0.f, 0.f);
+          if (s0 + e < nsplit) {
+            const float *po = a.part_o + (base + (int64_t)(s0 + e) * kHq) * kDim + 2 * lane;
+            v0[e] = __ldcg(reinterpret_cast<const float2 *>(po));
+            v1[e] = __ldcg(reinterpret_cast<const float2 *>(po + kDim));
+          }
+        }
+  #pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float w0 = __shfl_sync(0xffffffffu, c0, (s0 + e) & 31);
+          const float w1 = __shfl_sync(0xffffffffu, c1, (s0 + e) & 31);
+          O0.x = fmaf(w0, v0[e].x, O0.x);
+          O0.y = fmaf(w0, v0[e].y, O0.y);
+          O1.x = fmaf(w1, v1[e].x, O1.x);
+          O1.y = fmaf(w1, v1[e].y, O1.y);
         }
       }
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const float w0 = __shfl_sync(0xffffffffu, c0, (s0 + e) & 31);
-        const float w1 = __shfl_sync(0xffffffffu, c1, (s0 + e) & 31);
-        O0.x = fmaf(w0, v0[e].x, O0.x);
-        O0.y = fmaf(w0, v0[e].y, O0.y);
-        O1.x = fmaf(w1, v1[e].x, O1.x);
-        O1.y = fmaf(w1, v1[e].y, O1.y);
+      const int64_t oi = ((int64_t)b * kHq + 2 * kvh) * kDim + 2 * lane;
+      if (a.direct_out) {
+        *reinterpret_cast<uint32_t *>(a.out + oi) = bf16_bits(O0.x / L0) | (bf16_bits(O0.y / L0) << 16);
+        *reinterpret_cast<uint32_t *>(a.out + oi + kDim) = bf16_bits(O1.x / L1) | (bf16_bits(O1.y / L1) << 16);
+      } else {
+        *reinterpret_cast<float2 *>(a.state_o + oi) = O0;
+        *reinterpret_cast<float2 *>(a.state_o + oi + kDim) = O1;
+        if (lane == 0)
+          *reinterpret_cast<float4 *>(a.state_ml + ((int64_t)b * kHq + 2 * kvh) * 2) = make_float4(M0, L0, M1, L1);
       }
-    }
-    const int64_t oi = ((int64_t)b * kHq + 2 * kvh) * kDim + 2 * lane;
-    if (a.direct_out) {
-      *reinterpret_cast<uint32_t *>(a.out + oi) = bf16_bits(O0.x / L0) | (bf16_bits(O0.y / L0) << 16);
-      *reinterpret_cast<uint32_t *>(a.out + oi + kDim) = bf16_bits(O1.x / L1) | (bf16_bits(O1.y / L1) << 16);
     } else {
-      *reinterpret_cast<float2 *>(a.state_o + oi) = O0;
-      *reinterpret_cast<float2 *>(a.state_o + oi + kDim) = O1;
-      if (lane == 0)
-        *reinterpret_cast<float4 *>(a.state_ml + ((int64_t)b * kHq + 2 * kvh) * 2) = make_float4(M0, L0, M1, L1);
+      // merge the splits of (row, kv head): row = the sequence, or with several
+      // new tokens (sequence, token) (info.z carries the sequence's new tokens)
+      auto merge_row = [&](int64_t row) {
+        const int64_t base = row * a.num_splits * kHq + 2 * kvh;  // (row, split 0, head 2kvh)
+        // (max, sum) of heads 2kvh and 2kvh+1 of split `lane`: 4 adjacent floats
+        float4 ml = make_float4(-1.0e30f, 0.f, -1.0e30f, 0.f);
+        if (lane < nsplit) ml = __ldcg(reinterpret_cast<const float4 *>(a.part_ml + (base + (int64_t)lane * kHq) * 2));
+        float M0 = ml.x, M1 = ml.z;
+    #pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+          M0 = fmaxf(M0, __shfl_xor_sync(0xffffffffu, M0, off));
+          M1 = fmaxf(M1, __shfl_xor_sync(0xffffffffu, M1, off));
+        }
+        const float c0 = ex2(ml.x - M0), c1 = ex2(ml.z - M1);  // lanes past nsplit carry l = 0
+        float L0 = ml.y * c0, L1 = ml.w * c1;
+    #pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+          L0 += __shfl_xor_sync(0xffffffffu, L0, off);
+          L1 += __shfl_xor_sync(0xffffffffu, L1, off);
+        }
+        float2 O0 = make_float2(0.f, 0.f), O1 = make_float2(0.f, 0.f);
+        for (int s0 = 0; s0 < nsplit; s0 += 8) {
+          float2 v0[8], v1[8];
+    #pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            v0[e] = v1[e] = make_float2(0.f, 0.f);
+            if (s0 + e < nsplit) {
+              const float *po = a.part_o + (base + (int64_t)(s0 + e) * kHq) * kDim + 2 * lane;
+              v0[e] = __ldcg(reinterpret_cast<const float2 *>(po));
+              v1[e] = __ldcg(reinterpret_cast<const float2 *>(po + kDim));
+            }
+          }
+    #pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float w0 = __shfl_sync(0xffffffffu, c0, (s0 + e) & 31);
+            const float w1 = __shfl_sync(0xffffffffu, c1, (s0 + e) & 31);
+            O0.x = fmaf(w0, v0[e].x, O0.x);
+            O0.y = fmaf(w0, v0[e].y, O0.y);
+            O1.x = fmaf(w1, v1[e].x, O1.x);
+            O1.y = fmaf(w1, v1[e].y, O1.y);
+          }
+        }
+        const int64_t oi = (row * kHq + 2 * kvh) * kDim + 2 * lane;
+        if (a.direct_out) {
+          *reinterpret_cast<uint32_t *>(a.out + oi) = bf16_bits(O0.x / L0) | (bf16_bits(O0.y / L0) << 16);
+          *reinterpret_cast<uint32_t *>(a.out + oi + kDim) = bf16_bits(O1.x / L1) | (bf16_bits(O1.y / L1) << 16);
+        } else {
+          *reinterpret_cast<float2 *>(a.state_o + oi) = O0;
+          *reinterpret_cast<float2 *>(a.state_o + oi + kDim) = O1;
+          if (lane == 0)
+            *reinterpret_cast<float4 *>(a.state_ml + (row * kHq + 2 * kvh) * 2) = make_float4(M0, L0, M1, L1);
+        }
+      };
+      for (int tok = 0; tok < info.z; ++tok) merge_row((int64_t)b * a.tokens + tok);
     }
     if (lane == 0) atomicExch(cnt, 0);
   }
@@ -1449,7 +1659,8 @@ __device__ __forceinline__ void step_merger(const StepArgs &a, StepTail *tail, i
 // (g, t) = (lane / 4, lane % 4): scores of rows g and g+8 for both heads live
 // in lanes with t == 0; the output accumulator o[mt] holds dims 16mt+g and
 // 16mt+g+8 (heads 2t, 2t+1: only t == 0 carries real heads).
-__device__ __forceinline__ void step_consumer(const StepArgs &a, StepTail *tail, const uint8_t *tiles, int warp,
+template <int kT>
+__device__ __forceinline__ void step_consumer(const StepArgs &a, StepTailT<kT> *tail, const uint8_t *tiles, int warp,
                                               int lane) {
   const int g = lane >> 2, t = lane & 3;
   const int j = lane >> 3;  // ldmatrix sub-matrix this lane addresses
@@ -1465,6 +1676,7 @@ __device__ __forceinline__ void step_consumer(const StepArgs &a, StepTail *tail,
   uint32_t ephase = 0;  // completed phases of the epilogue barrier
   int epilogues = 0;    // red[] buffer parity
   uint32_t pubs = 0;    // items published to the merger warp
+  int ntok = 1;         // new tokens of the current item's sequence (kT > 1)
   // ldmatrix row addresses (without the stage base): rows of this lane's
   // sub-matrix, the 16-byte chunk index is added per k-step / m-tile.
   const int qk_row = 16 * warp + (lane & 7) + 8 * (j & 1);
@@ -1483,7 +1695,7 @@ __device__ __forceinline__ void step_consumer(const StepArgs &a, StepTail *tail,
       if (lane == 0) atomicOr(a.err, B2_DEV_TIMEOUT);
       break;
     }
-    const StageMeta &meta = tail->meta[s];
+    const StageMetaT<kT> &meta = tail->meta[s];
     const int flags = meta.flags;
     if (flags & kFlagEnd) break;
     const int b = meta.b, kvh = meta.kvh, split = meta.split, meta_nsplit = meta.nsplit;
@@ -1491,11 +1703,15 @@ __device__ __forceinline__ void step_consumer(const StepArgs &a, StepTail *tail,
     if (flags & kFlagFirst) {
       // B fragment of Q^T: (k = 2t, 2t+1 | 2t+8, 2t+9 of the k-step, n = g)
       // = q[head g][16ks + ...] for g < 2, zero for the padding columns.
+      // With several new tokens column g is (token g / 2, head g % 2), as q
+      // is laid out [token][head][64] in the meta.
+      if constexpr (kT > 1) ntok = meta.ntok;
+      const int ncols = kT == 1 ? 2 : 2 * ntok;
       const uint32_t *q32 = reinterpret_cast<const uint32_t *>(meta.q);
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks) {
-        bq[ks][0] = g < 2 ? q32[(g * kDim + 16 * ks + 2 * t) >> 1] : 0u;
-        bq[ks][1] = g < 2 ? q32[(g * kDim + 16 * ks + 2 * t + 8) >> 1] : 0u;
+        bq[ks][0] = g < ncols ? q32[(g * kDim + 16 * ks + 2 * t) >> 1] : 0u;
+        bq[ks][1] = g < ncols ? q32[(g * kDim + 16 * ks + 2 * t + 8) >> 1] : 0u;
       }
       m0 = m1 = -1.0e30f;
       l0 = l1 = 0.f;
@@ -1517,14 +1733,18 @@ __device__ __forceinline__ void step_consumer(const StepArgs &a, StepTail *tail,
       mma_bf16(c, a0, a1, a2, a3, bq[ks][0], bq[ks][1]);
     }
     // online softmax over this warp's 16 rows (rows >= valid masked)
-    const bool head_lane = t == 0;
-    const float s00 = head_lane && g < valid ? c[0] * a.scale_log2 : -INFINITY;      // row g,   head 0
-    const float s01 = head_lane && g < valid ? c[1] * a.scale_log2 : -INFINITY;      // row g,   head 1
-    const float s10 = head_lane && g + 8 < valid ? c[2] * a.scale_log2 : -INFINITY;  // row g+8, head 0
-    const float s11 = head_lane && g + 8 < valid ? c[3] * a.scale_log2 : -INFINITY;  // row g+8, head 1
+    // (several tokens: lane t holds token t, which sees ntok - 1 - t rows
+    // fewer than the last token: causal within the new tokens)
+    const bool head_lane = kT == 1 ? t == 0 : t < ntok;
+    const int tv = kT == 1 ? valid : valid - (ntok - 1 - t);
+    const float s00 = head_lane && g < tv ? c[0] * a.scale_log2 : -INFINITY;      // row g,   head 0
+    const float s01 = head_lane && g < tv ? c[1] * a.scale_log2 : -INFINITY;      // row g,   head 1
+    const float s10 = head_lane && g + 8 < tv ? c[2] * a.scale_log2 : -INFINITY;  // row g+8, head 0
+    const float s11 = head_lane && g + 8 < tv ? c[3] * a.scale_log2 : -INFINITY;  // row g+8, head 1
     float bm0 = fmaxf(s00, s10), bm1 = fmaxf(s01, s11);
+    // over the rows (lanes of the same t; with one token the other lanes hold -inf)
 #pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
+    for (int off = kT == 1 ? 1 : 4; off < 32; off <<= 1) {
       bm0 = fmaxf(bm0, __shfl_xor_sync(0xffffffffu, bm0, off));
       bm1 = fmaxf(bm1, __shfl_xor_sync(0xffffffffu, bm1, off));
     }
@@ -1546,13 +1766,17 @@ __device__ __forceinline__ void step_consumer(const StepArgs &a, StepTail *tail,
     // P^T as the B fragment: (k = tokens 2t, 2t+1 | 2t+8, 2t+9, n = head g)
     const uint32_t pk0 = pack_bf16x2(p00, p01);  // row g:   (head 0, head 1)
     const uint32_t pk1 = pack_bf16x2(p10, p11);  // row g+8
-    const uint32_t v0 = __shfl_sync(0xffffffffu, pk0, 8 * t);
-    const uint32_t v1 = __shfl_sync(0xffffffffu, pk0, 8 * t + 4);
-    const uint32_t v2 = __shfl_sync(0xffffffffu, pk1, 8 * t);
-    const uint32_t v3 = __shfl_sync(0xffffffffu, pk1, 8 * t + 4);
-    const uint32_t sel = g == 0 ? 0x5410u : 0x7632u;
-    const uint32_t bp0 = g < 2 ? __byte_perm(v0, v1, sel) : 0u;
-    const uint32_t bp1 = g < 2 ? __byte_perm(v2, v3, sel) : 0u;
+    // (several tokens: column g is (token g / 2, head g % 2), whose rows 2t,
+    // 2t + 1 sit in lanes 8t + token and 8t + 4 + token)
+    const int ptok = kT == 1 ? 0 : g >> 1;
+    const uint32_t v0 = __shfl_sync(0xffffffffu, pk0, 8 * t + ptok);
+    const uint32_t v1 = __shfl_sync(0xffffffffu, pk0, 8 * t + 4 + ptok);
+    const uint32_t v2 = __shfl_sync(0xffffffffu, pk1, 8 * t + ptok);
+    const uint32_t v3 = __shfl_sync(0xffffffffu, pk1, 8 * t + 4 + ptok);
+    const uint32_t sel = (kT == 1 ? g == 0 : (g & 1) == 0) ? 0x5410u : 0x7632u;
+    const int pcols = kT == 1 ? 2 : 2 * ntok;
+    const uint32_t bp0 = g < pcols ? __byte_perm(v0, v1, sel) : 0u;
+    const uint32_t bp1 = g < pcols ? __byte_perm(v2, v3, sel) : 0u;
     // O^T += V^T . P^T
 #pragma unroll
     for (int mt = 0; mt < 4; ++mt) {
@@ -1571,21 +1795,22 @@ __device__ __forceinline__ void step_consumer(const StepArgs &a, StepTail *tail,
     if (lane == 0) mbar_arrive(smem_u32(&tail->empty[s]));
     if (flags & kFlagLast) {
       const bool final_item = (flags & kFlagFinal) != 0;
-      step_epilogue(a, tail, warp, lane, b, kvh, split, final_item, m0, m1, l0, l1, o, ephase,
-                    (epilogues++) & 1);
-      if (!final_item && a.merge_here) publish(a, tail, lane, pubs, b, kvh, split, meta_nsplit);
+      step_epilogue<kT>(a, tail, warp, lane, b, kvh, split, final_item, ntok, m0, m1, l0, l1, o, ephase,
+                        (epilogues++) & 1);
+      if (!final_item && a.merge_here) publish(a, tail, lane, pubs, b, kvh, kT == 1 ? split : ntok, meta_nsplit);
     }
   }
   publish(a, tail, lane, pubs, -1, 0, 0, 0);  // end of work for the merger warp
 }
 
-__global__ void __launch_bounds__(kStepThreads, 3)
+template <int kT>
+__global__ void __launch_bounds__(kStepThreads, step_ctas_per_sm<kT>())
     decode_step_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                        const StepArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *tiles = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  StepTail *tail = reinterpret_cast<StepTail *>(tiles + kStages * kStageBytes);
+  StepTailT<kT> *tail = reinterpret_cast<StepTailT<kT> *>(tiles + kStages * kStageBytes);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -1613,11 +1838,11 @@ __global__ void __launch_bounds__(kStepThreads, 3)
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == kProducerWarp)
-    step_producer(a, tail, tiles, &tm_k, &tm_v, lane);
+    step_producer<kT>(a, tail, tiles, &tm_k, &tm_v, lane);
   else if (warp == kMergerWarp)
-    step_merger(a, tail, lane);
+    step_merger<kT>(a, tail, lane);
   else
-    step_consumer(a, tail, tiles, warp, lane);
+    step_consumer<kT>(a, tail, tiles, warp, lane);
   __syncthreads();
   if (threadIdx.x == 0) {
     // The last CTA to finish resets the work counter for the next launch.
@@ -2214,13 +2439,14 @@ bool decode_smem_ready() {
   return true;
 }
 
+template <int kT>
 bool step_smem_ready() {
   static std::atomic<bool> done[128];  // per device; several host threads may launch at once
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return false;
   if (!done[dev]) {
-    if (cudaFuncSetAttribute(decode_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kStepSmem) !=
-        cudaSuccess)
+    if (cudaFuncSetAttribute(decode_step_kernel<kT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             step_smem<kT>()) != cudaSuccess)
       return false;
     done[dev] = true;
   }
@@ -2372,9 +2598,14 @@ int decode_step_impl(const uint16_t *qkv, int64_t row_stride, const uint16_t *ga
                      int32_t max_blocks_per_seq, uint16_t *k_pool, uint16_t *v_pool, int32_t num_blocks,
                      int32_t batch, int32_t blocks_per_split, float scale, int32_t mode, uint16_t *out,
                      uint16_t *q_out, float *state_ml, float *state_o, float *part_ml, float *part_o,
-                     int32_t *counters, int32_t max_ctas, int32_t *dev_err, void *stream, const XchgArgs *x) {
+                     int32_t *counters, int32_t max_ctas, int32_t *dev_err, void *stream, const XchgArgs *x,
+                     int32_t tokens = 1, const int32_t *chunk_lens = nullptr) {
   if (batch < 0) return fail(B2_ERR_ARG, "batch must be >= 0 (got %d)", batch);
   if (batch == 0) return ok();
+  if (tokens < 1 || tokens > kMaxStepTokens) return fail(B2_ERR_ARG, "tokens must be in [1, %d]", kMaxStepTokens);
+  if (tokens > 1 && (x || !out || state_o || state_ml || seq_lens))
+    return fail(B2_ERR_ARG, "several new tokens: out is required; no states, seq_lens or exchange");
+  if (tokens > 1 && (int64_t)batch * tokens > 0x7fffffff) return fail(B2_ERR_ARG, "batch * tokens too large");
   if (!qkv || !past_lens || !block_tables || !k_pool || !v_pool || !part_ml || !part_o || !counters || !dev_err)
     return fail(B2_ERR_ARG, "null pointer argument");
   if (x && (!out || state_o || state_ml)) return fail(B2_ERR_ARG, "an exchange writes out and no state");
@@ -2405,12 +2636,17 @@ int decode_step_impl(const uint16_t *qkv, int64_t row_stride, const uint16_t *ga
   const int64_t splits = (static_cast<int64_t>(max_blocks_per_seq) + blocks_per_split - 1) / blocks_per_split;
   const int64_t total = splits * batch * kHkv;
   if (total >= (int64_t(1) << 31)) return fail(B2_ERR_ARG, "too many work items");
+  if (tokens > 1 && splits > kMergeInKernelSplits)
+    return fail(B2_ERR_ARG,
+                "several new tokens need at most %d splits per sequence: blocks_per_split >= ceil(%d / %d)",
+                kMergeInKernelSplits, max_blocks_per_seq, kMergeInKernelSplits);
   CUtensorMap mk, mv;
   int rc = make_pool_map(&mk, k_pool, num_blocks);
   if (rc) return rc;
   rc = make_pool_map(&mv, v_pool, num_blocks);
   if (rc) return rc;
-  if (!step_smem_ready()) return fail(B2_ERR_CUDA, "cannot set the decode-step kernel's shared memory size");
+  if (!(tokens == 1 ? step_smem_ready<1>() : step_smem_ready<kMaxStepTokens>()))
+    return fail(B2_ERR_CUDA, "cannot set the decode-step kernel's shared memory size");
   const int direct_out = state_o == nullptr && !x;
   // One warp merges a (sequence, kv head)'s splits serially: right for a
   // handful of splits; long single sequences with many splits are merged by
@@ -2420,8 +2656,9 @@ int decode_step_impl(const uint16_t *qkv, int64_t row_stride, const uint16_t *ga
              block_tables, max_blocks_per_seq, k_pool, v_pool, num_blocks, batch, blocks_per_split,
              static_cast<int>(splits), static_cast<int>(total), direct_out, merge_here,
              scale * 1.4426950408889634f, mode, x ? nullptr : out, q_out, state_ml, state_o, part_ml, part_o,
-             counters, dev_err, wait_limit()};
-  int64_t ctas = static_cast<int64_t>(sm_count()) * 3;
+             counters, dev_err, wait_limit(), tokens, chunk_lens};
+  int64_t ctas = static_cast<int64_t>(sm_count()) *
+                 (tokens == 1 ? step_ctas_per_sm<1>() : step_ctas_per_sm<kMaxStepTokens>());
   if (max_ctas > 0 && max_ctas < ctas) ctas = max_ctas;
   if (ctas > total) ctas = total;
   // Equal waves: items are handed out dynamically, so with `waves` rounds the
@@ -2439,11 +2676,13 @@ int decode_step_impl(const uint16_t *qkv, int64_t row_stride, const uint16_t *ga
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(ctas));
     cfg.blockDim = dim3(kStepThreads);
-    cfg.dynamicSmemBytes = kStepSmem;
+    cfg.dynamicSmemBytes = tokens == 1 ? step_smem<1>() : step_smem<kMaxStepTokens>();
     cfg.stream = st;
     cfg.attrs = pdl;
     cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, decode_step_kernel, mk, mv, a) != cudaSuccess) {
+    const cudaError_t le = tokens == 1 ? cudaLaunchKernelEx(&cfg, decode_step_kernel<1>, mk, mv, a)
+                                       : cudaLaunchKernelEx(&cfg, decode_step_kernel<kMaxStepTokens>, mk, mv, a);
+    if (le != cudaSuccess) {
       const cudaError_t e = cudaGetLastError();
       return fail(B2_ERR_CUDA, "decode_step_kernel launch failed: %s", cudaGetErrorString(e));
     }
@@ -2485,6 +2724,21 @@ extern "C" int b2_decode_step(const uint16_t *qkv, int64_t row_stride, const uin
                           block_tables, max_blocks_per_seq, k_pool, v_pool, num_blocks, batch, blocks_per_split,
                           scale, mode, out, q_out, state_ml, state_o, part_ml, part_o, counters, max_ctas, dev_err,
                           stream, nullptr);
+}
+
+extern "C" int b2_decode_step_tokens(const uint16_t *qkv, int64_t row_stride, int32_t tokens,
+                                     const int32_t *chunk_lens, const uint16_t *gamma_q, const uint16_t *gamma_k,
+                                     float eps, const uint16_t *rope_cos, const uint16_t *rope_sin,
+                                     int32_t rope_rows, const int32_t *past_lens, const int32_t *block_tables,
+                                     int32_t max_blocks_per_seq, uint16_t *k_pool, uint16_t *v_pool,
+                                     int32_t num_blocks, int32_t batch, int32_t blocks_per_split, float scale,
+                                     int32_t mode, uint16_t *out, uint16_t *q_out, float *part_ml, float *part_o,
+                                     int32_t *counters, int32_t max_ctas, int32_t *dev_err, void *stream) {
+  if (!out) return fail(B2_ERR_ARG, "out is required");
+  return decode_step_impl(qkv, row_stride, gamma_q, gamma_k, eps, rope_cos, rope_sin, rope_rows, past_lens, nullptr,
+                          block_tables, max_blocks_per_seq, k_pool, v_pool, num_blocks, batch, blocks_per_split,
+                          scale, mode, out, q_out, nullptr, nullptr, part_ml, part_o, counters, max_ctas, dev_err,
+                          stream, nullptr, tokens, tokens > 1 ? chunk_lens : nullptr);
 }
 
 extern "C" int b2_decode_step_exchange(const uint16_t *qkv, int64_t row_stride, const uint16_t *gamma_q,
