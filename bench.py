@@ -993,7 +993,7 @@ def prefill_point(args, dev, T, K, W, rank=0, path="prefill"):
         def step():
             attn.prefill(qkv, past, k_pool=kp, v_pool=vp, block_tables=tables, gamma_q=gq, gamma_k=gk, cos=cos,
                          sin=sin, dev_err=err, out=out, q_out=q_out,
-                         blocks_per_split=None if args.prefill_bps < 0 else args.prefill_bps)
+                         blocks_per_split=None if args.prefill_bps < 0 else args.prefill_bps, kernel="tcgen05")
 
     with torch.cuda.stream(stream):
         for _ in range(max(W, 1)):

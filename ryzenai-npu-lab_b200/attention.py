@@ -380,7 +380,8 @@ def prefill(qkv: torch.Tensor, past_lens: torch.Tensor, *, k_pool: torch.Tensor,
             chunk_lens: torch.Tensor | None = None, out: torch.Tensor | None = None,
             q_out: torch.Tensor | None = None, eps: float = EPS, scale: float = SCALE,
             mode: int = _lib.B2_NORM_QK | _lib.B2_ROPE_QK | _lib.B2_STORE_KV,
-            blocks_per_split: int | None = None, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+            blocks_per_split: int | None = None, stream: torch.cuda.Stream | None = None,
+            kernel: str = "auto") -> torch.Tensor:
     """Batched-prompt attention (b2_prefill_append + b2_prefill_attn): qkv bf16
     [B, T, >= 2048] raw projections of T new tokens per sequence at positions
     past_lens[b] + t (chunk_lens[b] <= T valid).  Appends their k/v and returns
@@ -388,7 +389,11 @@ def prefill(qkv: torch.Tensor, past_lens: torch.Tensor, *, k_pool: torch.Tensor,
     (B2_STORE_KV alone for projections that are already normalised and rotated;
     gamma/cos/sin are then unused).  blocks_per_split > 0 splits every tile's
     keys over more CTAs (b2_prefill_attn_split; None = the heuristic
-    prefill_blocks_per_split, 0 = no split)."""
+    prefill_blocks_per_split, 0 = no split).  kernel: "tcgen05" (the above),
+    "step" (the fused decode step for up to 4 new tokens,
+    b2_decode_step_tokens: 1.3-1.5x faster there; blocks_per_split is then its
+    split size) or "auto" (the step for T <= 4 without chunk_lens when a
+    sequence's keys fit 16 splits, else tcgen05)."""
     dev = qkv.device
     if qkv.dim() != 3 or qkv.shape[2] < QKV_WIDTH:
         raise ValueError(f"qkv must be [batch, tokens, >= {QKV_WIDTH}], got {tuple(qkv.shape)}")
@@ -417,6 +422,16 @@ def prefill(qkv: torch.Tensor, past_lens: torch.Tensor, *, k_pool: torch.Tensor,
     if out is None:
         out = torch.empty(b, t, HQ, D, dtype=torch.bfloat16, device=dev)
     _need(out, "out", torch.bfloat16, dev, (b, t, HQ, D))
+    if kernel not in ("auto", "step", "tcgen05"):
+        raise ValueError("kernel must be auto, step or tcgen05")
+    if kernel == "step" or (kernel == "auto" and t <= MAX_STEP_TOKENS and chunk_lens is None and
+                            math.ceil(block_tables.shape[1] / MAX_MERGED_SPLITS) <= 64):
+        counters = torch.zeros(2 + HKV * b, dtype=torch.int32, device=dev)
+        decode_step_tokens(qkv, past_lens, k_pool=k_pool, v_pool=v_pool, block_tables=block_tables, out=out,
+                           counters=counters, dev_err=dev_err, blocks_per_split=blocks_per_split or None,
+                           gamma_q=gamma_q, gamma_k=gamma_k, cos=cos, sin=sin, q_out=q_out, chunk_lens=chunk_lens,
+                           mode=mode, eps=eps, scale=scale, stream=stream)
+        return out
     lib = _lib.load()
     st = _stream(dev, stream)
     rc = lib.b2_prefill_append(_ptr(qkv), qkv.stride(1), _ptr(gamma_q), _ptr(gamma_k), ctypes.c_float(eps),

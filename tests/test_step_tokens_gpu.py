@@ -98,7 +98,7 @@ def test_tokens_match_the_prefill_kernel(cuda):
     err = torch.zeros(1, dtype=torch.int32, device=cuda)
     out2 = attn.prefill(qkv.to(cuda), torch.tensor(past, dtype=torch.int32, device=cuda), k_pool=kp, v_pool=vp,
                         block_tables=cache2.block_tables(), gamma_q=w["q_gamma"].to(cuda),
-                        gamma_k=w["k_gamma"].to(cuda), cos=cos, sin=sin, dev_err=err)
+                        gamma_k=w["k_gamma"].to(cuda), cos=cos, sin=sin, dev_err=err, kernel="tcgen05")
     torch.cuda.synchronize()
     assert err.item() == 0
     check_close(out, out2, "decode step tokens vs prefill kernel")
@@ -128,3 +128,25 @@ def test_tokens_refusals(cuda):
                                     1, 5, 16, 64, dtype=torch.bfloat16, device=cuda)))
     torch.cuda.synchronize()
     assert err.item() == 0
+
+
+def test_prefill_routes_short_chunks_to_the_step(cuda):
+    """attention.prefill picks the fused step for T <= 4 (kernel="auto"): the
+    same results as the reference path."""
+    attn = load_pkg("attention")
+    rope = load_pkg("rope")
+    past = [0, 63, 129]
+    tokens = 3
+    w = orc.attention_weights(0)
+    cache, hist = build_batch(past, cuda, seed=44, capacity=max(past) + tokens + 1)
+    qkv = torch.stack([rand_qkv(tokens, 930 + i) for i in range(len(past))])
+    cos, sin = rope.rope_table(512, device=cuda)
+    kp, vp = cache.pool(0)
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    q_out = torch.empty(len(past), tokens, 16, 64, dtype=torch.bfloat16, device=cuda)
+    out = attn.prefill(qkv.to(cuda), torch.tensor(past, dtype=torch.int32, device=cuda), k_pool=kp, v_pool=vp,
+                       block_tables=cache.block_tables(), gamma_q=w["q_gamma"].to(cuda),
+                       gamma_k=w["k_gamma"].to(cuda), cos=cos, sin=sin, dev_err=err, q_out=q_out)
+    torch.cuda.synchronize()
+    assert err.item() == 0
+    _check(w, cache, hist, qkv, out, q_out, past, [tokens] * len(past), "prefill auto")
