@@ -74,6 +74,9 @@ def parse():
     p.add_argument("--chunk", type=int, default=64, help="prefill: new tokens per sequence")
     p.add_argument("--prefill-bps", type=int, default=-1,
                    help="prefill: blocks per key split (-1 = heuristic, 0 = no split)")
+    p.add_argument("--prefill-kernel", choices=["tcgen05", "step"], default="tcgen05",
+                   help="prefill: tcgen05 = the batched prompt kernel; step = the fused decode step for "
+                        "chunks of up to 4 tokens (b2_decode_step_tokens)")
     p.add_argument("--config", choices=["c3", "c4", "c1", "c2", "c5", "prefill"], default="c3",
                    help="c3: batched paged decode (default); c4: one long sequence split over the GPUs; "
                         "c1: one attention layer (projections included) for one token at 512 cached tokens; "
@@ -1048,28 +1051,35 @@ def run_prefill(args):
     """Batched-prompt attention (the x8p engine's batched prompt tile, grown to
     64-token chunks): the C3 batch of 64 sequences with cached prefixes
     L ~ U[128, 8192], each receiving --chunk new tokens through one attention
-    layer (append of the chunk + tcgen05 attention).  tokens/s counts chunk
+    layer (append of the chunk + tcgen05 attention; --prefill-kernel step: the
+    fused decode step for chunks of up to 4 tokens).  tokens/s counts chunk
     tokens.  Replicas across GPUs."""
+    T, K = args.chunk, args.steps
+    step = args.prefill_kernel == "step"
+    if step and not 1 <= T <= 4:
+        raise SystemExit("--prefill-kernel step takes chunks of 1-4 tokens")
     world, rank, local = dist_env()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    T, K = args.chunk, args.steps
-    pt = prefill_point(args, dev, T, K, args.warmup, rank)
+    pt = prefill_point(args, dev, T, K, args.warmup, rank, path="step" if step else "prefill")
     ms, gbs, peak = pt["ms"], pt["gbs"], pt["peak"]
+    kernel = "decode_step_kernel" if step else "append_rope_kernel + prefill_attn_kernel"
     line = {
         "metric": METRIC, "value": pt["tokens_per_s"], "unit": "tokens/s", "n_gpus": 1, "steps": K,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "replicas",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": f"batched prompt: 64 sequences with cached L ~ U[128, 8192] each receiving "
-                               f"{T} new tokens through one attention layer (chunk append + tcgen05 "
-                               f"attention, causal within the chunk)", "chunk": T,
+                               f"{T} new tokens through one attention layer ("
+                               + ("fused decode step: norm + RoPE + append + attention + merge in one launch"
+                                  if step else "chunk append + tcgen05 attention")
+                               + ", causal within the chunk)", "chunk": T, "kernel": args.prefill_kernel,
                    "prefill_blocks_per_split": pt["blocks_per_split"],
                    "global_batch": pt["batch"], "parallelism": "replicas"},
         "hbm_gbs_per_gpu": gbs, "tflops": pt["tflops"],
-        "roofline": {"bound": "hbm", "kernel": "append_rope_kernel + prefill_attn_kernel", "achieved": gbs,
+        "roofline": {"bound": "hbm", "kernel": kernel, "achieved": gbs,
                      "peak": peak, "peak_source": pt["peak_kind"], "unit": "GB/s", "frac": gbs / peak,
                      "traffic": None, "algorithmic_bytes": pt["bytes"]},
-        "clocks": pt["clocks"], "gpu_launches": 2 * K,
+        "clocks": pt["clocks"], "gpu_launches": (1 if step else 2) * K,
     }
     print(json.dumps(line), flush=True)
 
