@@ -565,7 +565,7 @@ class PagedDecodeAttention:
             raise ValueError("partial-state buffers too small")
         kp, vp = self.cache.pool(layer)
         slots = 2 if double_buffered else 1
-        hp = {"b": b, "tables": block_tables, "slot": 0, "double": double_buffered,
+        hp = {"b": b, "tables": block_tables, "slot": 0, "double": double_buffered, "pinned": set(),
               "qkv": torch.empty(slots, b, QKV_WIDTH, dtype=torch.bfloat16, device=dev),
               "past": torch.empty(slots, b, dtype=torch.int32, device=dev),
               "out": torch.empty(slots, b, HQ, D, dtype=torch.bfloat16, device=dev)}
@@ -590,12 +590,24 @@ class PagedDecodeAttention:
         Asynchronous: the host buffers must stay alive and unchanged until
         join_host() and a synchronise of the stream; then out_host is valid."""
         hp = self._hp
+        pinned = hp["pinned"]
+        host = []
         for t, n, dt in ((qkv_host, hp["b"] * QKV_WIDTH, torch.bfloat16), (past_host, hp["b"], torch.int32),
                          (out_host, hp["b"] * HQ * D, torch.bfloat16)):
-            if t.dtype != dt or t.numel() != n or not t.is_contiguous() or not t.is_pinned():
+            if t.dtype != dt or t.numel() != n or not t.is_contiguous():
                 raise ValueError("host buffers must be pinned, contiguous and of the pipeline's shape")
-        host = (ctypes.c_void_p(qkv_host.data_ptr()), ctypes.c_void_p(past_host.data_ptr()),
-                ctypes.c_void_p(out_host.data_ptr()))
+            # is_pinned() asks the CUDA host allocator (several us per call):
+            # asked once per storage, so the rows of one pinned buffer (a
+            # step's slice of it each call) are checked once.  A pinned block
+            # stays pinned while the caching host allocator holds it.
+            s = t.untyped_storage().data_ptr()
+            if s not in pinned:
+                if not t.is_pinned():
+                    raise ValueError("host buffers must be pinned, contiguous and of the pipeline's shape")
+                if len(pinned) >= 1024:
+                    pinned.clear()
+                pinned.add(s)
+            host.append(t.data_ptr())
         if hp["double"]:
             rc = hp["call"](*host, *hp["bufs"], hp["slot"], *hp["args"], _stream(self.device, stream))
             hp["slot"] ^= 1

@@ -2396,7 +2396,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // Pool viewed as a 2-D tensor: 64 bf16 per row, num_blocks*8*64 rows; a box
 // is one (block, head) tile of 64 rows, swizzled in 128-byte groups.
-int make_pool_map(CUtensorMap *map, const void *pool, int num_blocks) {
+int encode_pool_map(CUtensorMap *map, const void *pool, int num_blocks) {
   auto fn = encode_fn();
   if (!fn) return fail(B2_ERR_NOSYM, "cuTensorMapEncodeTiled is not available from the driver");
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(kDim),
@@ -2409,6 +2409,33 @@ int make_pool_map(CUtensorMap *map, const void *pool, int num_blocks) {
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(B2_ERR_ARG, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return B2_OK;
+}
+
+// The pool's tensor map, encoded once per (pool, num_blocks) and calling
+// thread: a decode loop launches on the same pools every step, and the
+// encode is host work on the launch path.  The map describes only the
+// address range, so a pool freed and allocated again at the same address and
+// size is described by the same map.
+int make_pool_map(CUtensorMap *map, const void *pool, int num_blocks) {
+  struct Entry {
+    const void *pool;
+    int num_blocks;
+    CUtensorMap map;
+  };
+  constexpr int kEntries = 8;
+  thread_local Entry cache[kEntries] = {};
+  thread_local int next = 0;
+  for (int i = 0; i < kEntries; ++i)
+    if (cache[i].pool == pool && cache[i].num_blocks == num_blocks && pool) {
+      *map = cache[i].map;
+      return B2_OK;
+    }
+  const int rc = encode_pool_map(map, pool, num_blocks);
+  if (rc == B2_OK) {
+    cache[next] = Entry{pool, num_blocks, *map};
+    next = (next + 1) % kEntries;
+  }
+  return rc;
 }
 
 // Wait limits of the launches (b2_set_wait_limits), read at every launch.

@@ -434,3 +434,33 @@ def test_step_host_pipeline_matches_step(cuda, double_buffered):
         outs.append(list(out_host) if host else res)
     for step, (a, c) in enumerate(zip(*outs)):
         assert torch.equal(a, c), f"step {step}"
+
+
+def test_step_host_buffer_checks(cuda):
+    """step_host refuses pageable or wrongly sized host buffers on every call,
+    and accepts each row of one pinned buffer (its storage checked once):
+    the same inputs give the same context in either row."""
+    lengths = [5, 70]
+    b = len(lengths)
+    w = orc.attention_weights(0)
+    cache, _ = build_batch(lengths, cuda, seed=33, capacity=200)
+    runner = _attn().PagedDecodeAttention(cache, w["q_gamma"], w["k_gamma"], b, 512, blocks_per_split=4)
+    runner.open_host_pipeline(0, cache.block_tables())
+    raw = rand_qkv(b, 7)
+    qkv_h = raw.pin_memory()
+    past_h = torch.tensor(lengths, dtype=torch.int32).pin_memory()
+    out_h = torch.zeros(2, b, 16, 64, dtype=torch.bfloat16).pin_memory()
+    with pytest.raises(ValueError):
+        runner.step_host(raw.clone(), past_h, out_h[0])                        # pageable qkv
+    with pytest.raises(ValueError):
+        runner.step_host(qkv_h, past_h, torch.empty(b, 16, 64, dtype=torch.bfloat16))   # pageable out
+    runner.step_host(qkv_h, past_h, out_h[0])
+    with pytest.raises(ValueError):
+        runner.step_host(qkv_h, past_h, out_h[1][:1])                          # a row short
+    with pytest.raises(ValueError):
+        runner.step_host(qkv_h, past_h.clone(), out_h[1])                      # pageable lengths
+    runner.step_host(qkv_h, past_h, out_h[1])   # the same token again: the same slot, the same context
+    runner.join_host()
+    torch.cuda.synchronize()
+    runner.check()
+    assert torch.equal(out_h[0], out_h[1]) and out_h[0].abs().sum() > 0
