@@ -1867,16 +1867,18 @@ __global__ void __launch_bounds__(kStepThreads, step_ctas_per_sm<kT>())
 // Warp roles: warp 4 lane 0 feeds K tiles and warp 6 lane 0 V tiles with TMA
 // (two 3-stage rings: a K stage is free again once its S product is done, so
 // K copies run two to three blocks ahead), warp 5 lane 0 issues the MMAs,
-// warps 0-3 run the online softmax (thread = query row = TMEM lane).  S is double-buffered in TMEM and P in shared memory, so
-// the tensor cores compute S_{j+1} and P_j.V_j while the softmax of the next
-// block runs.  The running maximum is re-based lazily: a row's O is rescaled
+// warps 0-3 run the online softmax (thread = query row = TMEM lane).  S and
+// P are double-buffered in TMEM, so the tensor cores compute S_{j+1} and
+// P_j.V_j while the softmax of the next block runs; P_j (bf16 pairs written
+// with tcgen05.st) is the A operand of its P.V product straight from TMEM,
+// with no shared-memory round trip or proxy fence between softmax and MMA.  The running maximum is re-based lazily: a row's O is rescaled
 // (TMEM load, scale, store) only when its block maximum exceeds the one in
 // use by more than kPfRebase (log2 units); between re-bases P <= 2^kPfRebase,
 // well inside bf16 and fp32 range.
 
 constexpr int kPfStages = 3;
 constexpr int kPfThreads = 7 * 32;  // 4 softmax warps + K TMA warp + MMA warp + V TMA warp
-constexpr int kPfTmemCols = 256;    // S buffers at columns 0 and 64, O at 128
+constexpr int kPfTmemCols = 256;    // S buffers at columns 0 and 64, O at 128, P buffers at 192 and 224
 constexpr float kPfRebase = 8.0f;
 // Up to this many sequences, CTAs take the sequences longest first (blocks
 // launch in blockIdx order, so the longest runs start in the first wave).
@@ -1898,7 +1900,7 @@ struct __align__(8) PrefillTail {
   uint32_t tmem_base;
   int abort;
 };
-constexpr int kPfSmem = 1024 + 3 * 16384 + kPfStages * kStageBytes + (int)sizeof(PrefillTail);
+constexpr int kPfSmem = 1024 + 16384 + kPfStages * kStageBytes + (int)sizeof(PrefillTail);
 
 struct PrefillArgs {
   const uint16_t *q;  // [batch][tokens][16][64] normalised + rotated
@@ -1944,6 +1946,16 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a, uint64_t b
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+
+// The same with A from tensor memory: M rows = TMEM lanes, K along the
+// columns (two bf16 per 32-bit column).
+__device__ __forceinline__ void umma_f16_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                            uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc));
 }
 
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
@@ -1996,6 +2008,18 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float v[16]) {
       "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])),
       "r"(__float_as_uint(v[11])), "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])),
       "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15]))
+      : "memory");
+}
+
+// 32 consecutive 32-bit columns into this thread's TMEM lane.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t v[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+      "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]),
+      "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]),
+      "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
       : "memory");
 }
 
@@ -2068,8 +2092,7 @@ __global__ void __launch_bounds__(kPfThreads, 2)
   extern __shared__ uint8_t smem_raw[];
   uint8_t *sQ = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint8_t *sP = sQ + 16384;  // two P buffers of 16 KiB
-  uint8_t *kring = sP + 2 * 16384;             // kPfStages K tiles of 8 KiB
+  uint8_t *kring = sQ + 16384;                 // kPfStages K tiles of 8 KiB
   uint8_t *vring = kring + kPfStages * kTileBytes;  // kPfStages V tiles of 8 KiB
   PrefillTail *tail = reinterpret_cast<PrefillTail *>(vring + kPfStages * kTileBytes);
   const int tid = threadIdx.x;
@@ -2182,11 +2205,11 @@ __global__ void __launch_bounds__(kPfThreads, 2)
         }
         tmem_fence_after();
         const uint32_t vt = smem_u32(vring + s * kTileBytes);
-        const uint32_t pb = smem_u32(sP + (j & 1) * 16384);
+        const uint32_t pt = tmem + 192 + 32 * (j & 1);  // P_j: 16 keys per K step = 8 columns
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks)
-          umma_f16(tmem + 128, umma_desc(pb + 32 * ks, 16), umma_desc(vt + 2048 * ks, 0), kPfIdescPV,
-                   (j > 0 || ks > 0) ? 1u : 0u);
+          umma_f16_ta(tmem + 128, pt + 8 * ks, umma_desc(vt + 2048 * ks, 0), kPfIdescPV,
+                      (j > 0 || ks > 0) ? 1u : 0u);
         umma_commit(smem_u32(&tail->pvbar));
         umma_commit(smem_u32(&tail->pfree[j & 1]));
         umma_commit(smem_u32(&tail->vempty[s]));
@@ -2321,10 +2344,13 @@ __global__ void __launch_bounds__(kPfThreads, 2)
         ok = false;
         break;
       }
-      uint8_t *pbuf = sP + (j & 1) * 16384;
+      {
+        uint32_t pk[32];  // P_j of this row as bf16 pairs, into TMEM buffer j % 2
 #pragma unroll
-      for (int c = 0; c < 64; c += 8)
-        *reinterpret_cast<uint4 *>(pbuf + tid * 128 + (((c >> 3) ^ (tid & 7)) << 4)) = pack8(sc + c);
+        for (int c = 0; c < 64; c += 2) pk[c >> 1] = pack_bf16x2_rn(sc[c], sc[c + 1]);
+        tmem_st32(trow + 192 + 32 * (j & 1), pk);
+        tmem_wait_st();
+      }
       if (key0 + kBlock - 1 > last_key) {
         // rows of the last block past every query of the tile may hold stale
         // (even NaN) data: zero them so that P = 0 cannot meet them in P.V
@@ -2337,8 +2363,8 @@ __global__ void __launch_bounds__(kPfThreads, 2)
         uint8_t *v_gen = vring + s * kTileBytes;
         for (int i = tid; i < (kBlock - first_bad) * 8; i += 128)
           *reinterpret_cast<uint4 *>(v_gen + (first_bad + (i >> 3)) * 128 + ((i & 7) << 4)) = make_uint4(0, 0, 0, 0);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // before the P.V product reads V
       }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       tmem_fence_before();
       mbar_arrive(smem_u32(&tail->pready[j & 1]));
     }

@@ -2,7 +2,7 @@
 prefill_attn_kernel), checked under random schedules.
 
 Roles, as in the kernel: a K and a V TMA producer (rings of 3 stages), the
-MMA issuer (S_j = Q.K_j^T into TMEM buffer j % 2, O += P_j.V_j from shared
+MMA issuer (S_j = Q.K_j^T into TMEM buffer j % 2, O += P_j.V_j from TMEM
 P buffer j % 2) and four softmax warps (read S_j, re-base O when the maximum
 jumps, write P_j, sometimes zero the V rows past the tile).  They hand work
 over through mbarriers: kfull/vfull (TMA landed), kempty/vempty (stage read
