@@ -51,6 +51,7 @@ PKG = "ryzenai-npu-lab_b200"
 METRIC = "decode-attn tokens/s & HBM GB/s (% of 8 TB/s) vs context at 1/2/4/8 B200"
 HQ, HKV, D, BLOCK = 16, 8, 64, 64
 KV_BYTES_PER_TOKEN = 2 * HKV * D * 2          # K + V, bf16: 2048 B
+L2_BYTES = 126 * 2 ** 20
 FALLBACK_HBM_GBS = 6650.0
 
 
@@ -212,10 +213,17 @@ def build_workload(args, rank: int, dev: torch.device, world: int = 1):
     pc = importlib.import_module(PKG + ".paged_cache")
     lengths = seq_lengths(args, rank, world)
     caps = [n + 1 for n in lengths]
-    num_blocks = sum(pc.blocks_for(c) for c in caps)
+    # A shard whose K/V would stay in L2 from one step to the next (4 or 8
+    # ranks of the strong-scaling batch) is held `copies` times in its own
+    # blocks, and the steps rotate over the copies' block tables, so that the
+    # K/V streamed between two reads of a block is at least twice L2.
+    footprint = sum(KV_BYTES_PER_TOKEN * c for c in caps)
+    copies = max(1, math.ceil(2 * L2_BYTES / footprint))
+    num_blocks = copies * sum(pc.blocks_for(c) for c in caps)
     cache = pc.PagedKVCache(num_blocks, max(caps), device=dev, shuffle_seed=args.seed * 1000 + rank + 17)
-    for n, c in zip(lengths, caps):
-        cache.add_sequence(n, capacity=c)
+    for _ in range(copies):
+        for n, c in zip(lengths, caps):
+            cache.add_sequence(n, capacity=c)
     gen = torch.Generator(device=dev).manual_seed(args.seed * 1000 + rank + 29)
     cache.k.normal_(generator=gen)
     cache.v.normal_(generator=gen)
@@ -229,8 +237,12 @@ def build_workload(args, rank: int, dev: torch.device, world: int = 1):
     ring = 8
     qkv = (torch.randn(ring, len(lengths), 2048, generator=gen, device=dev) * 0.6).to(torch.bfloat16)
     past = torch.tensor(lengths, dtype=torch.int32, device=dev)
+    nb = len(lengths)
+    all_tables = cache.block_tables()
+    tables = [all_tables[c * nb:(c + 1) * nb].contiguous() for c in range(copies)]
     return {"lengths": lengths, "cache": cache, "runner": runner, "qkv": qkv, "past": past,
-            "seq": past + 1, "tables": cache.block_tables(), "ring": ring}
+            "seq": past + 1, "tables": tables[0], "table_ring": tables, "copies": copies,
+            "kv_bytes": footprint, "ring": ring}
 
 
 def step_bytes(lengths) -> tuple[int, int]:
@@ -300,7 +312,7 @@ def run_reference(args):
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1000.0 * args.batch / value, "higher_is_better": True, "scaling": args.scaling,
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": config_block(args, lengths, None, args.gpus),
+        "config": config_block(args, lengths, args.gpus),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
                          "sample": f"median of {args.steps} samples, each a {cpu_sample_info(info)}",
                          "mean_context": info["mean_context"]},
@@ -309,7 +321,17 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
-def config_block(args, lengths, bps, world: int = 1):
+def l2_policy(lengths, world: int, weak: bool) -> str:
+    """How the steps avoid reading K/V out of L2 (build_workload), from the
+    job's lengths alone, so that both arms print the same config."""
+    total = sum(KV_BYTES_PER_TOKEN * (n + 1) for n in lengths) * (world if weak else 1)
+    per_rank = total / world
+    return (f"{total / 1e6:.0f} MB of K/V per step over {world} GPU(s), ~{per_rank / 1e6:.0f} MB per rank; "
+            f"a rank whose share is under 2x L2 (126 MB) rotates its steps over copies of its sequences "
+            f"in their own blocks, so every step streams its K/V from HBM; no flush")
+
+
+def config_block(args, lengths, world: int = 1):
     """lengths: every sequence of the job (all ranks)."""
     weak = args.scaling == "weak" and world > 1
     return {
@@ -322,14 +344,13 @@ def config_block(args, lengths, bps, world: int = 1):
         "global_batch": global_tokens_per_step(args, world), "batch_per_gpu": "sharded" if not weak else args.batch,
         "context_min": args.min_len, "context_max": args.max_len,
         "context_mean": round(sum(lengths) / len(lengths), 1),
-        "block_tokens": BLOCK, "blocks_per_split": bps, "parallelism": f"seq-shard x{world}",
-        "l2": "inputs larger than L2 (KV pool > 126 MB per GPU), no flush",
+        "block_tokens": BLOCK, "parallelism": f"seq-shard x{world}",
+        "l2": l2_policy(base_lengths(args), world, weak),
     }
 
 
 # ----------------------------------------------------------------- vs-context points
 
-L2_BYTES = 126 * 2 ** 20
 
 
 def time_graph(graph, stream, reps: int = 1) -> float:
@@ -507,17 +528,19 @@ def run_b200(args):
     graph = torch.cuda.CUDAGraph()
     kp, vp = runner.cache.pool(0)
     b = len(wl["lengths"])
+    copies = wl["copies"]
     with torch.cuda.graph(graph, stream=stream):
         for j in range(K):
+            tables = wl["table_ring"][j % copies]
             if runner.fused:
-                runner.step(0, wl["qkv"][j % ring], wl["past"], wl["seq"], wl["tables"])
+                runner.step(0, wl["qkv"][j % ring], wl["past"], wl["seq"], tables)
                 continue
             q = runner.q[:b]
             attn.append_rope(wl["qkv"][j % ring], wl["past"], q_out=q, dev_err=runner.dev_err,
                              gamma_q=runner.gamma_q, gamma_k=runner.gamma_k, cos=runner.cos, sin=runner.sin,
-                             k_pool=kp, v_pool=vp, block_tables=wl["tables"])
+                             k_pool=kp, v_pool=vp, block_tables=tables)
             ev0[j].record()
-            splits = attn.decode_attn(q, kp, vp, wl["tables"], wl["seq"],
+            splits = attn.decode_attn(q, kp, vp, tables, wl["seq"],
                                       blocks_per_split=runner.blocks_per_split, part_ml=runner.part_ml,
                                       part_o=runner.part_o, dev_err=runner.dev_err)
             ev1[j].record()
@@ -565,6 +588,8 @@ def run_b200(args):
         with torch.cuda.stream(stream):
             e0.record()
             for j in range(e2e_steps):
+                if copies > 1:
+                    runner.set_host_tables(wl["table_ring"][j % copies])
                 runner.step_host(qkv_host[j % ring], past_host, out_host[j])
             runner.join_host()
             e1.record()
@@ -584,7 +609,7 @@ def run_b200(args):
             for j in range(e2e_steps):
                 qkv_dev.copy_(qkv_host[j % ring], non_blocking=True)
                 lens_dev.copy_(lens_host, non_blocking=True)
-                o = runner.step(0, qkv_dev, lens_dev[0], lens_dev[1], wl["tables"])
+                o = runner.step(0, qkv_dev, lens_dev[0], lens_dev[1], wl["table_ring"][j % copies])
                 out_host[j].copy_(o, non_blocking=True)
             e1.record()
     torch.cuda.synchronize()
@@ -626,7 +651,11 @@ def run_b200(args):
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
         "warmup": W, "ms_per_step": ms_step, "higher_is_better": True, "scaling": args.scaling,
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": config_block(args, all_lengths, runner.blocks_per_split, world),
+        "config": config_block(args, all_lengths, world),
+        # this rank's kernel plan: work-item size, and how many copies of its
+        # sequences the steps rotate over (1 = its K/V alone exceeds 2x L2)
+        "plan": {"blocks_per_split": runner.blocks_per_split, "copies": copies,
+                 "kv_mb_per_step": round(wl["kv_bytes"] / 1e6, 1)},
         "per_rank": {"columns": ["step_us", "sequences", "cached_tokens"], "rows": per_rank_rows},
         "hbm_gbs_per_gpu": step_gbs, "hbm_pct_of_8tbs": 100.0 * step_gbs / 8000.0,
         "roofline": {"bound": "hbm", "kernel": kernel, "achieved": achieved,
@@ -770,7 +799,11 @@ def run_c4(args):
                    "global_batch": 1, "blocks_per_split": lc.bps, "parallelism": f"split-kv x{world}",
                    "timing": "K steps after one untimed replay of the K-step graph (ranks in step)" if world > 1
                    else "K steps",
-                   "l2": "inputs larger than L2 (268 MB of K/V), no flush"},
+                   "l2": (f"{KV_BYTES_PER_TOKEN * args.context / 1e6:.0f} MB of K/V, "
+                          f"~{KV_BYTES_PER_TOKEN * args.context / world / 1e6:.0f} MB per rank, no flush"
+                          + ("; a rank's share fits in L2 (126 MB): its K/V loads carry an evict-first "
+                             "hint, but steps may partly read it from L2"
+                             if KV_BYTES_PER_TOKEN * args.context / world < 2 * L2_BYTES else ""))},
         "hbm_gbs_aggregate": total_bytes / (ms / K / 1e3) / 1e9,
         "per_rank": {"columns": ["step_us", "partial_us", "local_tokens"], "rows": per_rank_rows},
         "roofline": {"bound": "hbm", "kernel": "decode_step_kernel (+ combine of its splits)",

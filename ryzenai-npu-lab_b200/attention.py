@@ -580,6 +580,18 @@ class PagedDecodeAttention:
                       _ptr(self.counters), _ptr(self.dev_err))
         self._hp = hp
 
+    def set_host_tables(self, block_tables: torch.Tensor) -> None:
+        """Point the host-fed pipeline at another block table of the pipeline's
+        shape (a scheduler that fills the next step's table while the current
+        one is in use); the next step_host() reads it.  A table must stay alive
+        and unchanged until the steps that read it have run."""
+        hp = self._hp
+        _need(block_tables, "block_tables", torch.int32, self.device, shape=hp["tables"].shape)
+        args = list(hp["args"])
+        args[6] = _ptr(block_tables)
+        hp["args"] = tuple(args)
+        hp["tables"] = block_tables
+
     def step_host(self, qkv_host: torch.Tensor, past_host: torch.Tensor, out_host: torch.Tensor,
                   stream: torch.cuda.Stream | None = None) -> None:
         """One decode step fed from pinned host memory (one C-ABI call): H2D of

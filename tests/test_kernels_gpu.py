@@ -436,6 +436,49 @@ def test_step_host_pipeline_matches_step(cuda, double_buffered):
         assert torch.equal(a, c), f"step {step}"
 
 
+def test_step_host_table_swap(cuda):
+    """set_host_tables moves the host-fed pipeline between two block tables of
+    one pool (the same histories in other blocks) from step to step: every
+    step's context equals step() over the table it was given, and a table of
+    another shape is refused."""
+    lengths = [5, 300, 64]
+    b = len(lengths)
+    w = orc.attention_weights(0)
+    outs = []
+    keep = []
+    for host in (False, True):
+        cache, _ = build_batch(lengths + lengths, cuda, seed=37, capacity=400)
+        for i, n in enumerate(lengths):   # copy 1 holds copy 0's histories in its own blocks
+            k, v = orc.past_cache(100 * 37 + i, n)
+            cache.write_dense(0, b + i, k[0], v[0])
+        runner = _attn().PagedDecodeAttention(cache, w["q_gamma"], w["k_gamma"], b, 1024, blocks_per_split=2)
+        all_tables = cache.block_tables()
+        tables = [all_tables[:b].contiguous(), all_tables[b:].contiguous()]
+        res = []
+        if host:
+            runner.open_host_pipeline(0, tables[0])
+            with pytest.raises(ValueError):
+                runner.set_host_tables(all_tables)
+            out_host = torch.empty(4, b, 16, 64, dtype=torch.bfloat16).pin_memory()
+        for step in range(4):
+            raw = rand_qkv(b, 80 + step)
+            past = torch.tensor([n + step // 2 for n in lengths], dtype=torch.int32)
+            if host:
+                runner.set_host_tables(tables[step % 2])
+                keep.append((raw.pin_memory(), past.pin_memory()))
+                runner.step_host(*keep[-1], out_host[step])
+            else:
+                res.append(runner.step(0, raw.to(cuda), past.to(cuda), (past + 1).to(cuda), tables[step % 2]).cpu())
+        if host:
+            runner.join_host()
+        torch.cuda.synchronize()
+        runner.check()
+        outs.append(list(out_host) if host else res)
+    for step, (a, c) in enumerate(zip(*outs)):
+        assert torch.equal(a, c), f"step {step}"
+    assert not torch.equal(outs[0][0], outs[0][1])   # the two tables' steps saw different new tokens
+
+
 def test_step_host_buffer_checks(cuda):
     """step_host refuses pageable or wrongly sized host buffers on every call,
     and accepts each row of one pinned buffer (its storage checked once):
