@@ -208,17 +208,22 @@ def global_tokens_per_step(args, world: int) -> int:
     return args.batch * (world if getattr(args, "scaling", "strong") == "weak" else 1)
 
 
+def rotation_copies(lengths) -> tuple[int, int]:
+    """(K/V bytes one step reads, copies of the sequences its steps rotate
+    over).  A shard whose K/V would stay in L2 from one step to the next (4 or
+    8 ranks of the strong-scaling batch) is held `copies` times in its own
+    blocks and the steps rotate over the copies' block tables, so that the
+    K/V streamed between two reads of a block is at least twice L2."""
+    footprint = sum(KV_BYTES_PER_TOKEN * (n + 1) for n in lengths)
+    return footprint, max(1, math.ceil(2 * L2_BYTES / max(1, footprint)))
+
+
 def build_workload(args, rank: int, dev: torch.device, world: int = 1):
     attn = importlib.import_module(PKG + ".attention")
     pc = importlib.import_module(PKG + ".paged_cache")
     lengths = seq_lengths(args, rank, world)
     caps = [n + 1 for n in lengths]
-    # A shard whose K/V would stay in L2 from one step to the next (4 or 8
-    # ranks of the strong-scaling batch) is held `copies` times in its own
-    # blocks, and the steps rotate over the copies' block tables, so that the
-    # K/V streamed between two reads of a block is at least twice L2.
-    footprint = sum(KV_BYTES_PER_TOKEN * c for c in caps)
-    copies = max(1, math.ceil(2 * L2_BYTES / footprint))
+    footprint, copies = rotation_copies(lengths)
     num_blocks = copies * sum(pc.blocks_for(c) for c in caps)
     cache = pc.PagedKVCache(num_blocks, max(caps), device=dev, shuffle_seed=args.seed * 1000 + rank + 17)
     for _ in range(copies):

@@ -23,6 +23,35 @@ def test_reference_arm_prints_one_json_line():
     assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["cores"] >= 1
     assert "workload" in d["config"]
     assert d["cpu_baseline"]["mean_context"] == d["config"]["context_mean"]
+    # the same config dict the GPU arm prints for the same flags (one function of the job's lengths)
+    sys.path.insert(0, str(ROOT))
+    import bench
+    argv = sys.argv
+    try:
+        sys.argv = ["bench.py", "--impl", "reference", "--steps", "2", "--warmup", "1"]
+        args = bench.parse()
+    finally:
+        sys.argv = argv
+    assert d["config"] == bench.config_block(args, bench.base_lengths(args), 1)
+
+
+def test_small_shards_rotate_over_copies_larger_than_l2():
+    """Every rank of the strong-scaling runs streams at least twice L2 of K/V
+    between two reads of the same block: N = 1 reads its 0.49 GB once per
+    step, N = 2 / 4 / 8 ranks rotate over 2 / 3 / 5 copies of their share."""
+    sys.path.insert(0, str(ROOT))
+    import bench
+    a = types.SimpleNamespace(seed=3, min_len=128, max_len=8192, batch=64, scaling="strong")   # bench's default draw
+    want = {1: 1, 2: 2, 4: 3, 8: 5}
+    for world in (1, 2, 4, 8):
+        for rank in range(world):
+            lengths = bench.seq_lengths(a, rank, world)
+            footprint, copies = bench.rotation_copies(lengths)
+            assert footprint == sum(2048 * (n + 1) for n in lengths)
+            assert copies * footprint >= 2 * bench.L2_BYTES
+            assert copies == 1 or (copies - 1) * footprint < 2 * bench.L2_BYTES
+            assert copies == want[world], (world, rank, copies)
+    assert bench.rotation_copies([])[1] >= 1
 
 
 def test_strong_scaling_shards_the_one_batch():
@@ -64,7 +93,7 @@ def test_cpu_baseline_sample_is_the_whole_workload():
     rate, info = bench.cpu_reference_rate(lengths, 0.0)
     assert rate > 0 and info["sequences"] == 64
     assert info["mean_context"] == round(sum(lengths) / 64, 1)
-    assert bench.config_block(types.SimpleNamespace(**vars(a), gpus=1), lengths, 12)["context_mean"] == \
+    assert bench.config_block(types.SimpleNamespace(**vars(a), gpus=1), lengths, 1)["context_mean"] == \
         info["mean_context"]
 
 
