@@ -208,6 +208,57 @@ def global_tokens_per_step(args, world: int) -> int:
     return args.batch * (world if getattr(args, "scaling", "strong") == "weak" else 1)
 
 
+def synthetic_attention_weights(seed: int, hidden: int = 1024) -> dict:
+    """Seeded random-init weights of one LFM2.5 attention layer (the configs'
+    N(0, 0.02) projections; q/k RMSNorm gains 1 + N(0, 0.1)), bf16 on the host."""
+    g = torch.Generator().manual_seed(seed)
+    w = {"q_proj": torch.randn(HQ * D, hidden, generator=g) * 0.02,
+         "k_proj": torch.randn(HKV * D, hidden, generator=g) * 0.02,
+         "v_proj": torch.randn(HKV * D, hidden, generator=g) * 0.02,
+         "out_proj": torch.randn(hidden, HQ * D, generator=g) * 0.02,
+         "q_gamma": 1.0 + 0.1 * torch.randn(D, generator=g),
+         "k_gamma": 1.0 + 0.1 * torch.randn(D, generator=g)}
+    return {k: v.to(torch.bfloat16) for k, v in w.items()}
+
+
+def synthetic_lfm2_weights(seed: int, dev, hidden: int = 1024, ffn: int = 2560, vocab: int = 65536) -> dict:
+    """Seeded random-init LFM2.5-230M-shaped weights under Hugging Face
+    parameter names, drawn on the device: matrices N(0, 0.02), short-conv taps
+    N(0, 0.3), norm gains 1 (q/k layernorm gains 1 + N(0, 0.1)), the head tied
+    to the embedding; the layer pattern is the runner's (8 short-conv, 6 GQA)."""
+    runner_mod = importlib.import_module(PKG + ".lfm2_runner")
+    g = torch.Generator(device=dev).manual_seed(seed)
+
+    def n(*shape, std=0.02):
+        return (torch.randn(*shape, generator=g, device=dev) * std).to(torch.bfloat16)
+
+    def ones(k):
+        return torch.ones(k, dtype=torch.bfloat16, device=dev)
+
+    sd = {"model.embed_tokens.weight": n(vocab, hidden)}
+    for i, kind in enumerate(runner_mod.LFM25_LAYER_TYPES):
+        p = f"model.layers.{i}."
+        if kind == "attention":
+            sd[p + "self_attn.q_proj.weight"] = n(HQ * D, hidden)
+            sd[p + "self_attn.k_proj.weight"] = n(HKV * D, hidden)
+            sd[p + "self_attn.v_proj.weight"] = n(HKV * D, hidden)
+            sd[p + "self_attn.out_proj.weight"] = n(hidden, HQ * D)
+            sd[p + "self_attn.q_layernorm.weight"] = (1.0 + n(D, std=0.1).float()).to(torch.bfloat16)
+            sd[p + "self_attn.k_layernorm.weight"] = (1.0 + n(D, std=0.1).float()).to(torch.bfloat16)
+        else:
+            sd[p + "conv.conv.weight"] = n(hidden, 1, 3, std=0.3)
+            sd[p + "conv.in_proj.weight"] = n(3 * hidden, hidden)
+            sd[p + "conv.out_proj.weight"] = n(hidden, hidden)
+        sd[p + "feed_forward.w1.weight"] = n(ffn, hidden)
+        sd[p + "feed_forward.w3.weight"] = n(ffn, hidden)
+        sd[p + "feed_forward.w2.weight"] = n(hidden, ffn)
+        sd[p + "operator_norm.weight"] = ones(hidden)
+        sd[p + "ffn_norm.weight"] = ones(hidden)
+    sd["model.embedding_norm.weight"] = ones(hidden)
+    sd["lm_head.weight"] = sd["model.embed_tokens.weight"]
+    return sd
+
+
 def rotation_copies(lengths) -> tuple[int, int]:
     """(K/V bytes one step reads, copies of the sequences its steps rotate
     over).  A shard whose K/V would stay in L2 from one step to the next (4 or
@@ -479,6 +530,15 @@ def c2_point(args, dev, L0: int, reps: int = 4, sampler=None) -> dict:
     return out
 
 
+def guarded(fn, *a, **kw):
+    """An extra point of the N = 1 line: its failure is recorded in the line
+    rather than costing the headline measurement."""
+    try:
+        return fn(*a, **kw)
+    except Exception as e:   # noqa: BLE001 - reported in the JSON line
+        return {"error": f"{type(e).__name__}: {e}"[:400]}
+
+
 def context_sweep(args, dev) -> dict:
     """The metric's 'vs context' axis on one GPU (after the headline run)."""
     points = [fixed_batch_point(args, dev, b, L) for b in (32, 64) for L in (1024, 4096, 8192, 16384)]
@@ -486,7 +546,10 @@ def context_sweep(args, dev) -> dict:
                     "context; frac of the measured HBM copy peak; copies > 1: the step rotates over that "
                     "many batches so that its K/V is not served from L2",
             "batched": points,
-            "c2": [c2_point(args, dev, L0) for L0 in (1024, 4096, 16384)]}
+            "c2": [c2_point(args, dev, L0) for L0 in (1024, 4096, 16384)],
+            # config C4 on one GPU: one sequence of 131 072 cached tokens (the step splits its keys
+            # over the CTAs and merges them with the combine kernel)
+            "c4_one_gpu": guarded(fixed_batch_point, args, dev, 1, 131072, steps=48)}
 
 
 # ----------------------------------------------------------------- B200 path
@@ -680,6 +743,13 @@ def run_b200(args):
     if rank == 0 and world == 1 and not args.no_sweep and not args.shard:
         line["contexts"] = context_sweep(args, dev)
         line["prefill"] = prefill_points(args, dev)
+        # config C5 on this GPU (the default runner: cuBLAS projections, layer glue in libb2attn)
+        c5 = guarded(c5_point, args, dev)
+        if "ms" in c5:
+            c5 = {"workload": "C5 end-to-end greedy decode, LFM2.5-230M-shaped random-init model, 256 prompts "
+                              "x 32 ids, 256 new tokens (prefill included), paged KV, CUDA graph per token",
+                  **{k: (round(v, 2) if isinstance(v, float) else v) for k, v in c5.items()}}
+        line["c5"] = c5
     if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.shard:
         rate, info = cpu_reference_rate(base_lengths(args), args.cpu_seconds)
         line["cpu_baseline"] = {"value": rate, "unit": "tokens/s", "cores": torch.get_num_threads(),
@@ -839,14 +909,13 @@ def run_c1(args):
     dev = torch.device("cuda", local)
     attn = importlib.import_module(PKG + ".attention")
     pc = importlib.import_module(PKG + ".paged_cache")
-    from oracle import lfm2_attention as orc   # seeded weight generator (set-up only)
     L = args.context if args.context != 131072 else 512
     cache = pc.PagedKVCache(pc.blocks_for(L + 1), L + 1, device=dev, shuffle_seed=args.seed * 1000 + 17)
     cache.add_sequence(L, capacity=L + 1)
     gen = torch.Generator(device=dev).manual_seed(args.seed * 1000 + rank + 29)
     cache.k.normal_(generator=gen)
     cache.v.normal_(generator=gen)
-    w = orc.attention_weights(args.seed)
+    w = synthetic_attention_weights(args.seed)
     wqkv = torch.cat([w["q_proj"], w["k_proj"], w["v_proj"]]).to(dev).contiguous()
     wo = w["out_proj"].to(dev).contiguous()
     runner = attn.PagedDecodeAttention(cache, w["q_gamma"], w["k_gamma"], 1, L + 2)
@@ -936,19 +1005,12 @@ def run_c2(args):
         print(json.dumps(line), flush=True)
 
 
-def run_c5(args):
-    """Config C5: end-to-end greedy decode of an LFM2.5-230M-shaped random-init
-    model (14 layers: 8 short-conv + 6 GQA attention, SwiGLU 2560, tied 65536
-    head): 256 prompts x 32 random ids, 256 new tokens each, paged KV, one
-    CUDA graph per token.  value = new tokens per second over the whole job
-    (prefill included); replicas across GPUs (each rank its own batch)."""
-    world, rank, local = dist_env()
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
+def c5_point(args, dev, rank: int = 0) -> dict:
+    """One C5 run (see run_c5): ms for the whole job, its clocks and the
+    generated ids' shape."""
     runner_mod = importlib.import_module(PKG + ".lfm2_runner")
-    from oracle import lfm2_attention as orc   # seeded weight generator (set-up only)
     batch, prompt_len, new = 256, 32, 256
-    sd = orc.lfm2_model_weights(args.seed)
+    sd = synthetic_lfm2_weights(args.seed, dev)
     runner = runner_mod.LFM2DecodeRunner(sd, max_batch=batch, max_context=prompt_len + new + 1, device=dev,
                                          fused_glue=not args.torch_glue,
                                          own_gemm=args.b2_gemm and not args.torch_glue)
@@ -960,13 +1022,34 @@ def run_c5(args):
     runner.reset()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
+    with ClockSampler(dev.index) as clocks:
         t0.record()
         out = runner.generate(prompts, new)
         t1.record()
         torch.cuda.synchronize()
     runner.check()
     ms = t0.elapsed_time(t1)
+    del runner
+    torch.cuda.empty_cache()
+    return {"ms": ms, "batch": batch, "prompt": prompt_len, "new": new, "shape": list(out.shape),
+            "clocks": clocks.summary(), "tokens_per_s": batch * new / (ms / 1e3),
+            "us_per_token_step": 1e3 * ms / (prompt_len + new - 1),
+            "projections": "b2_gemm (tcgen05, SwiGLU fused into w1/w3)" if args.b2_gemm and not args.torch_glue
+            else "cuBLAS (torch.matmul)",
+            "layer_glue": "torch ops" if args.torch_glue else "libb2attn kernels"}
+
+
+def run_c5(args):
+    """Config C5: end-to-end greedy decode of an LFM2.5-230M-shaped random-init
+    model (14 layers: 8 short-conv + 6 GQA attention, SwiGLU 2560, tied 65536
+    head): 256 prompts x 32 random ids, 256 new tokens each, paged KV, one
+    CUDA graph per token.  value = new tokens per second over the whole job
+    (prefill included); replicas across GPUs (each rank its own batch)."""
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pt = c5_point(args, dev, rank)
+    batch, prompt_len, new, ms = pt["batch"], pt["prompt"], pt["new"], pt["ms"]
     line = {
         "metric": METRIC, "value": batch * new / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
         "steps": prompt_len + new - 1, "warmup": 1, "ms_per_step": ms / (prompt_len + new - 1),
@@ -979,7 +1062,7 @@ def run_c5(args):
                    else "cuBLAS (torch.matmul)",
                    "global_batch": batch * world, "prompt": prompt_len, "new_tokens": new,
                    "parallelism": f"replicas x{world}"},
-        "generated_shape": list(out.shape), "clocks": clocks.summary(),
+        "generated_shape": pt["shape"], "clocks": pt["clocks"],
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
