@@ -740,6 +740,8 @@ def run_b200(args):
     if args.shard:
         line["config"]["shard"] = args.shard
         line["config"]["workload"] += f"; ONLY shard {args.shard} of it on this GPU (one rank's part)"
+        line["config"]["l2"] = l2_policy(base_lengths(args), int(args.shard.split("/")[1]),
+                                         args.scaling == "weak")
     if rank == 0 and world == 1 and not args.no_sweep and not args.shard:
         line["contexts"] = context_sweep(args, dev)
         line["prefill"] = prefill_points(args, dev)
